@@ -1,0 +1,69 @@
+/*
+ * ltq_b200 — C ABI of the B200 (sm_100a) LTQ / TCQ quantizer kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (cudaStream_t passed as void*), runs
+ * asynchronously on that stream and returns an int status:
+ *     0   success (launch errors of the queued kernels are reported as positive cudaError_t codes),
+ *    -1   unsupported or invalid parameters (the same validation table as the reference, plus the limits named below),
+ *    >0   a cudaError_t from the launch.
+ * No entry point allocates device memory: outputs and scratch are passed in by the caller.  All entry points are
+ * re-entrant; calls on different streams may run concurrently.
+ *
+ * Reference: lumen-inference/ltq-research (paths below are relative to its root).
+ */
+#ifndef LTQ_B200_H
+#define LTQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library version string, e.g. "ltq_b200 0.1 sm_100a". */
+const char* ltq_b200_version(void);
+
+/*
+ * Drop-in replacement for the reference C-ABI `tcq_viterbi` (src/cuda/tcq_viterbi.cu:743-746), bound by ctypes in
+ * src/tcq_proto.py:529 as 15 pointers, 18 ints, pointer, int, pointer.  Same argument list, same meaning, same
+ * validation (returns -1 where the reference returns -1, src/cuda/tcq_viterbi.cu:748-751), same outputs:
+ *   rec [N, ld], code [N, ld] ((gain index << 16) | (label * U + u), optional), gcand [N, T/sub, G] (when G < Gfull),
+ *   best [N] (g * S + s), end_st [N] (optional), mid_st [N] (first tail-biting pass, optional).
+ * bp [N, T, G, S/32] u32, gsel [N, T/sub, S] u8 and pbits (pp = 1: [N, T/2, G, S/32]; pp >= 2: [N, T/4, G, 9, S/32])
+ * are caller-allocated scratch of the sizes the reference's Python wrapper allocates (src/tcq_proto.py:623-637);
+ * this implementation stores its own survivor layout in them.
+ * Limits beyond the reference: S must be 1024 (nu = 10); nl must be 4, 8 or 16; with pp = 1 and T < 10 the
+ * caller's scratch is too small for the survivor layout (returns -1).
+ */
+int tcq_viterbi(const float* x, const float* w, const float* tab, const float* gains, float* rec, uint32_t* bp,
+                uint8_t* gsel, const int* init_st, int* end_st, const float* tab_hi, const float* gains_hi,
+                uint8_t* gcand, int* best, int* code, int* mid_st, int mid_t, int tail, int N, int T, int S, int U,
+                int G, int Gfull, int m, int sub, int U_hi, int mix, int m2, int m3, int m4, int nl, int ld, int rot,
+                uint32_t* pbits, int pp, void* stream);
+
+/*
+ * The whole tail-biting schedule of `viterbi_ub_cuda(..., tail_biting=True)` (src/tcq_proto.py:584-609) in one
+ * call: pass 1 (free start; over the window [T/2 - tb_window, T/2 + tb_window) when tb_window > 0, over tb_cand1 gain
+ * candidates when tb_cand1 > 0) finds the path state before sample T/2; tb_passes - 1 further passes run on the tile
+ * rotated by T/2 with that state as start and end.  The last pass writes rec [N, T] and code [N, T] (optional) at the
+ * original positions.
+ *   x [N, T] fp32; w: per-position weights, row stride w_stride (0 = one row [T] shared by all tiles);
+ *   tab [nl * 2^(K-1)], gains [Gfull]; tab_hi / gains_hi / mix: half-integer mode (NULL / 0 when unused);
+ *   m: primary label mask, m_extra[n_extra]: extra label masks (nl = 4 << n_extra);
+ *   n_cand: Viterbi over n_cand gain candidates per sub-block (0 = all Gfull); pp: 0 none, 1 D2, 2 D4, 3 EQ.
+ * workspace: device memory of at least ltq_viterbi_tb_workspace_bytes(...) bytes, 256-byte aligned.
+ */
+size_t ltq_viterbi_tb_workspace_bytes(int N, int T, int Gfull, int n_cand, int sub, int pp, int tb_window,
+                                      int tb_cand1);
+int ltq_viterbi_tb(const float* x, const float* w, int w_stride, const float* tab, const float* gains,
+                   const float* tab_hi, const float* gains_hi, float* rec, int* code, int N, int T, int nu, int K,
+                   int m, const int* m_extra, int n_extra, int Gfull, int n_cand, int sub, int U_hi, int mix, int pp,
+                   int tb_passes, int tb_cand1, int tb_window, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LTQ_B200_H */

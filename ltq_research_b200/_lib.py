@@ -1,0 +1,78 @@
+"""Loader of the in-tree CUDA library ``libltq_b200.so`` (C ABI: include/ltq_b200.h).
+
+There is no fallback: if the library is missing, or a call is made without a CUDA device, the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libltq_b200.so"
+_LIB = None
+_LOCK = threading.Lock()
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/ltq_b200.h
+SIGNATURES = {
+    "ltq_b200_version": (ctypes.c_char_p, []),
+    # reference ctypes binding, src/tcq_proto.py:529: 15 pointers, 18 ints, pointer, int, pointer
+    "tcq_viterbi": (I, [P] * 15 + [I] * 18 + [P, I, P]),
+    "ltq_viterbi_tb_workspace_bytes": (SZ, [I] * 8),
+    "ltq_viterbi_tb": (I, [P, P, I, P, P, P, P, P, P] + [I] * 5 + [P] + [I] * 10 + [P, SZ, P]),
+}
+
+
+class LtqLibraryError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises LtqLibraryError when it has not been built."""
+    global _LIB
+    if _LIB is None:
+        with _LOCK:
+            if _LIB is None:
+                if not LIB_PATH.exists():
+                    raise LtqLibraryError(f"{LIB_PATH} is missing: build it with `python -m ltq_research_b200.build`")
+                L = ctypes.CDLL(str(LIB_PATH))
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _LIB = L
+    return _LIB
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors: torch.Tensor) -> torch.device:
+    """Every tensor must live on one CUDA device; there is no CPU path."""
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("ltq_research_b200: inputs must be CUDA tensors (there is no CPU implementation)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError("ltq_research_b200: all inputs must be on the same CUDA device")
+    if dev is None:
+        raise RuntimeError("ltq_research_b200: no CUDA tensor given")
+    return dev
+
+
+def ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()

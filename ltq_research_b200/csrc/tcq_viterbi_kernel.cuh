@@ -1,0 +1,831 @@
+// B200 (sm_100a) TCQ Viterbi for the LTQ tile format: forward add-compare-select, in-block traceback,
+// reconstruction and code emission, for one tile of T samples per CTA.
+//
+// Semantics follow the reference kernel tcq_forward_kernel (lumen-inference/ltq-research,
+// src/cuda/tcq_viterbi.cu:97-683) bit for bit: the same fp32 operations on the same operands (branch error
+// w * min_u fma(-g, tab[u], x)^2, path metric = selected predecessor + branch error), the same strict-`<` tie-breaks,
+// the same sub-block gain merge, gain candidates, D2 / D4 / EQ parity classes, tail-biting start / end constraints.
+// The organisation is new:
+//
+//   * one warp per gain slot g; a CTA is one tile with G warps;
+//   * each lane keeps 32 of the 1024 path metrics in registers.  In "layout j" lane L holds the states
+//       s = r_lo | L << j | r_hi << (j + 5),  register r = r_hi << j | r_lo   (r_lo: j bits, r_hi: 5 - j bits)
+//     so the two predecessors of a butterfly (bit 9 of the state = bit 4 of the register) sit in registers ra and
+//     ra + 16 of the same lane, and one trellis step maps registers (ra, ra + 16) -> (2 ra, 2 ra + 1) for every j
+//     (a perfect shuffle).  Four steps (j = 0..3) run in registers; then the metrics go through shared memory once
+//     (layout 4 -> layout 0, padded, conflict-free), i.e. one exchange per 4 trellis steps;
+//   * a compare is the sign of (b - a) on the FMA pipe, the select is FMNMX, and the decision bit is packed with a
+//     funnel shift: 16 decisions per lane per step become one half word, stored coalesced as survivor words;
+//   * subset labels are split into a per-lane part (a table variant chosen once per step) and a per-register part
+//     that is a compile-time constant when the label masks are template parameters (MaskCT), so a branch error is a
+//     register operand, not a shared-memory lookup.  MaskRT is the same kernel for arbitrary masks (errors read from
+//     shared memory per butterfly).
+//
+// Survivors (decision bits) go to global memory in a per-(tile, slot) linear word stream (see SvStream below);
+// the traceback walks them per sub-block chunk from shared memory.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ltqb {
+
+constexpr float BIG = 3.4e38f;  // the reference's "infinite" path metric (src/cuda/tcq_viterbi.cu:48, :227)
+constexpr int NS = 1024;        // trellis states (10-bit memory)
+constexpr int NSP = NS + NS / 32;  // exchange slots per gain slot (padded)
+constexpr int MAXG = 16, MAXU = 128, MAXSUBS = 32, MAXT = 512;
+
+struct VitParams {
+    const float *x, *w, *tab, *gains, *tab_hi, *gains_hi;
+    float* rec;
+    int* code;
+    const int* init_st;
+    int *end_st, *mid_st, *best;
+    uint8_t* gcand;
+    uint32_t *svA, *svB;   // survivor word stream: first capA words of each (tile, slot) in A, the rest in B
+    uint32_t* gsw;         // gain-merge decisions: [N][T/sub][NB][32] words
+    long long capA, capB;  // words per (tile, slot) in A / B
+    int mid_t, tail;
+    int N, T, U, G, Gfull, sub, U_hi, mix, ld, ldw, rot;
+    int m, m2, m3, m4, nl;
+    int W4;                // survivor words per 4-step group
+    int NB;                // gsel bit planes
+    int cand;
+};
+
+// ------------------------------------------------------------------------------------------------
+// label masks
+// ------------------------------------------------------------------------------------------------
+__host__ __device__ constexpr int cpar(unsigned v)
+{
+    v ^= v >> 16; v ^= v >> 8; v ^= v >> 4; v ^= v >> 2; v ^= v >> 1;
+    return (int)(v & 1u);
+}
+
+// A branch-error row of one trellis step: NL labels x NP parity classes, permuted for this lane's label variant.
+template <int EW>
+struct ERow {
+    float r[EW];
+    const float* ptr;
+};
+
+// Compile-time masks: label bits of every register are constants after unrolling.
+template <int M0, int M1, int M2, int M3, int NL_>
+struct MaskCT {
+    static constexpr int NL = NL_;
+    static constexpr bool RT = false;
+    __device__ __forceinline__ explicit MaskCT(const VitParams&) {}
+    // label bits 1.. of a state s whose (s >> 1) == v
+    __device__ __forceinline__ int hi(unsigned v) const
+    {
+        int r = cpar(v & (unsigned)M0);
+        if (NL >= 8) r |= cpar(v & (unsigned)M1) << 1;
+        if (NL >= 16) r |= cpar(v & (unsigned)M2) << 2;
+        if (NL >= 32) r |= cpar(v & (unsigned)M3) << 3;
+        return r;
+    }
+    template <int EW>
+    __device__ __forceinline__ float get(const ERow<EW>& e, int i) const { return e.r[i]; }
+};
+
+// Runtime masks: same recursion, branch errors read from the shared-memory row.
+template <int NL_>
+struct MaskRT {
+    static constexpr int NL = NL_;
+    static constexpr bool RT = true;
+    unsigned m0, m1, m2, m3;
+    __device__ __forceinline__ explicit MaskRT(const VitParams& p)
+        : m0((unsigned)p.m), m1((unsigned)p.m2), m2((unsigned)p.m3), m3((unsigned)p.m4) {}
+    __device__ __forceinline__ int hi(unsigned v) const
+    {
+        int r = __popc(v & m0) & 1;
+        if (NL >= 8) r |= (__popc(v & m1) & 1) << 1;
+        if (NL >= 16) r |= (__popc(v & m2) & 1) << 2;
+        if (NL >= 32) r |= (__popc(v & m3) & 1) << 3;
+        return r;
+    }
+    template <int EW>
+    __device__ __forceinline__ float get(const ERow<EW>& e, int i) const { return e.ptr[i]; }
+};
+
+// ------------------------------------------------------------------------------------------------
+// shared memory layout (host and device)
+// ------------------------------------------------------------------------------------------------
+struct SmemLayout {
+    int x, w, tab, tabhi, gain, gainhi, ce, gc, dp, err, tbw, tbg, st, sg, par, red, flag, total;
+};
+
+__host__ __device__ inline int al16(int v) { return (v + 15) & ~15; }
+
+__host__ __device__ inline SmemLayout smem_layout(int T, int G, int Gfull, int sub, int NL, int NP, int U, int U_hi,
+                                                  int W4, int NB)
+{
+    SmemLayout L;
+    const int NV = NL / 2, EW = NL * NP;
+    int o = 0;
+    L.x = o; o = al16(o + 4 * T);
+    L.w = o; o = al16(o + 4 * T);
+    L.tab = o; o = al16(o + 4 * NL * U);
+    L.tabhi = o; o = al16(o + 4 * NL * U_hi);
+    L.gain = o; o = al16(o + 4 * MAXG);
+    L.gainhi = o; o = al16(o + 4 * MAXG);
+    L.ce = o; o = al16(o + 4 * (T / sub) * Gfull);
+    L.gc = o; o = al16(o + (T / sub) * G);
+    L.dp = o; o = al16(o + 4 * NSP * G);
+    L.err = o; o = al16(o + 4 * G * sub * NV * EW);
+    const int groups = (sub + 3) / 4 + 1;
+    L.tbw = o; o = al16(o + 4 * 32 * W4 * groups);
+    L.tbg = o; o = al16(o + 4 * 32 * NB);
+    L.st = o; o = al16(o + 2 * T);
+    L.sg = o; o = al16(o + T);
+    L.par = o; o = al16(o + T);
+    L.red = o; o = al16(o + 8 * MAXG);
+    L.flag = o; o = al16(o + 16);
+    L.total = o;
+    return L;
+}
+
+// state held by register r of lane L in layout j
+__host__ __device__ __forceinline__ int state_of(int j, int L, int r)
+{
+    return (r & ((1 << j) - 1)) | (L << j) | ((r >> j) << (j + 5));
+}
+// exchange slot of state s: one pad word per 32 states.  For every layout j the address is a per-lane base
+// (L << j) + (L >> (5 - j)) plus a per-register constant, and the 32 lanes of a warp hit 32 distinct banks.
+__device__ __forceinline__ int swz(int s) { return s + (s >> 5); }
+
+// register index ra (0..15) of the butterfly whose outputs have (s >> 1) == b9, in layout j; lane = (b9 >> j) & 31
+__device__ __forceinline__ int bfly_of(int j, int b9) { return (b9 & ((1 << j) - 1)) | ((b9 >> (j + 5)) << j); }
+
+// label bits 1.. of the outputs of butterfly ra at step j, register part (the lane part is PLj[j])
+template <int J, class MP>
+__device__ __forceinline__ int qreg(const MP& mp, int ra)
+{
+    return mp.hi((unsigned)((ra & ((1 << J) - 1)) | ((ra >> J) << (J + 5))));
+}
+
+__device__ __forceinline__ uint32_t pushbit(float d, uint32_t acc)
+{
+    return __funnelshift_l(__float_as_uint(d), acc, 1);  // acc << 1 | sign(d)
+}
+
+// min_u (x - g tab[u])^2, u = u0, u0 + du, ... : the reference's contracted form d = fma(-g, tab, x)
+__device__ __forceinline__ float branch_err(float x, float g, const float* tl, int u0, int du, int U)
+{
+    float e = BIG;
+    for (int u = u0; u < U; u += du) {
+        const float d = __fmaf_rn(-g, tl[u], x);
+        e = fminf(e, __fmul_rn(d, d));
+    }
+    return e;
+}
+
+template <class MP, int EW>
+__device__ __forceinline__ void load_row(ERow<EW>& e, const float* row)
+{
+    e.ptr = row;
+    if (!MP::RT) {
+#pragma unroll
+        for (int k = 0; k < EW; k += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(row + k);
+            e.r[k] = v.x; e.r[k + 1] = v.y; e.r[k + 2] = v.z; e.r[k + 3] = v.w;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// survivors
+// ------------------------------------------------------------------------------------------------
+struct SvStream {
+    uint32_t *a, *b;
+    long long capA;
+    __device__ __forceinline__ void put(long long k, uint32_t v) const
+    {
+        if (k < capA) a[k] = v; else b[k - capA] = v;
+    }
+    __device__ __forceinline__ uint32_t get(long long k) const { return k < capA ? a[k] : b[k - capA]; }
+};
+
+// ------------------------------------------------------------------------------------------------
+// trellis pairs: steps (J, J + 1), J in {0, 2}, processed as 8 radix-4 units per lane.
+// Unit u: step-J butterflies u and u + 8 -> intermediates 2u, 2u+1, 2u+16, 2u+17 -> step-(J+1) butterflies
+// 2u + 1, 2u -> outputs 4u .. 4u + 3.  Units run u = 7 .. 0 so every packed bit word is built in descending order.
+// INIT: the step-J inputs are the start of the tile (t = 0): no predecessor, only the successors of s0 are allowed.
+// ------------------------------------------------------------------------------------------------
+template <int J, bool INIT, class MP, int EW>
+__device__ __forceinline__ void pair_plain(const MP& mp, float (&cur)[32], const ERow<EW>& E0, const ERow<EW>& E1,
+                                           uint32_t& word, bool okL, int ok_ra)
+{
+    float nx[32];
+    uint32_t alo = 0, ahi = 0, a2 = 0;
+#pragma unroll
+    for (int u = 7; u >= 0; u--) {
+        float iv[4];
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+            const int ra = u + 8 * hh;
+            const int q = qreg<J>(mp, ra);
+            if (INIT) {
+                const bool ok = okL && (ok_ra < 0 || ok_ra == ra);
+                iv[2 * hh] = ok ? mp.get(E0, q << 1) : BIG;
+                iv[2 * hh + 1] = ok ? mp.get(E0, (q << 1) | 1) : BIG;
+            } else {
+                const float va = cur[ra], vb = cur[ra + 16];
+                const float d = __fsub_rn(vb, va);
+                const float mn = fminf(va, vb);
+                if (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
+                iv[2 * hh] = __fadd_rn(mn, mp.get(E0, q << 1));
+                iv[2 * hh + 1] = __fadd_rn(mn, mp.get(E0, (q << 1) | 1));
+            }
+        }
+#pragma unroll
+        for (int c = 1; c >= 0; c--) {
+            const int x = 2 * u + c;
+            const float va = iv[c], vb = iv[2 + c];
+            const float d = __fsub_rn(vb, va);
+            const float mn = fminf(va, vb);
+            a2 = pushbit(d, a2);
+            const int q = qreg<J + 1>(mp, x);
+            nx[2 * x] = __fadd_rn(mn, mp.get(E1, q << 1));
+            nx[2 * x + 1] = __fadd_rn(mn, mp.get(E1, (q << 1) | 1));
+        }
+    }
+    word = INIT ? a2 : ((((ahi << 8) | alo) << 16) | a2);
+#pragma unroll
+    for (int r = 0; r < 32; r++) cur[r] = nx[r];
+}
+
+// D2: pair (J, J+1); intermediates per parity class p, the output takes the class with the smaller metric (tie p=0).
+// Words: wi = step-J decisions (16 bits), wh = step-(J+1) decisions per class (p0 << 16 | p1), wc = class per output.
+template <int J, bool INIT, class MP, int EW>
+__device__ __forceinline__ void pair_d2(const MP& mp, float (&cur)[32], const ERow<EW>& E0, const ERow<EW>& E1,
+                                        uint32_t& wi, uint32_t& wh, uint32_t& wc, bool okL, int ok_ra)
+{
+    float nx[32];
+    uint32_t alo = 0, ahi = 0, h0 = 0, h1 = 0, cc = 0;
+#pragma unroll
+    for (int u = 7; u >= 0; u--) {
+        float iv[2][4];
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+            const int ra = u + 8 * hh;
+            const int q = qreg<J>(mp, ra);
+            if (INIT) {
+                const bool ok = okL && (ok_ra < 0 || ok_ra == ra);
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+#pragma unroll
+                    for (int p = 0; p < 2; p++) iv[p][2 * hh + c] = ok ? mp.get(E0, (((q << 1) | c) << 1) | p) : BIG;
+            } else {
+                const float va = cur[ra], vb = cur[ra + 16];
+                const float d = __fsub_rn(vb, va);
+                const float mn = fminf(va, vb);
+                if (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+#pragma unroll
+                    for (int p = 0; p < 2; p++) iv[p][2 * hh + c] = __fadd_rn(mn, mp.get(E0, (((q << 1) | c) << 1) | p));
+            }
+        }
+#pragma unroll
+        for (int c = 1; c >= 0; c--) {
+            const int x = 2 * u + c;
+            const int q = qreg<J + 1>(mp, x);
+            float mnp[2];
+#pragma unroll
+            for (int p = 0; p < 2; p++) {
+                const float va = iv[p][c], vb = iv[p][2 + c];
+                const float d = __fsub_rn(vb, va);
+                mnp[p] = fminf(va, vb);
+                if (p) h1 = pushbit(d, h1); else h0 = pushbit(d, h0);
+            }
+#pragma unroll
+            for (int c2 = 1; c2 >= 0; c2--) {
+                const int lb = (q << 1) | c2;
+                const float v0 = __fadd_rn(mnp[0], mp.get(E1, lb << 1));
+                const float v1 = __fadd_rn(mnp[1], mp.get(E1, (lb << 1) | 1));
+                cc = pushbit(__fsub_rn(v1, v0), cc);
+                nx[2 * x + c2] = fminf(v0, v1);
+            }
+        }
+    }
+    wi = INIT ? 0u : ((ahi << 8) | alo);
+    wh = (h0 << 16) | h1;
+    wc = cc;
+#pragma unroll
+    for (int r = 0; r < 32; r++) cur[r] = nx[r];
+}
+
+// D4 / EQ phase A: steps (0, 1) of a group of 4.  Step 0 (or the tile start): intermediates per low bit b of the
+// first sample; step 1: outputs per class c = b0 ^ b1 (EQ: c = b0 = b1), best b per class (tie b = 0).
+// Words: w0 = step-0 decisions, w1 = step-1 decisions per b (b0 << 16 | b1), w2 / w3 = chosen b of class 0 / 1.
+template <bool INIT, bool EQ, class MP, int EW>
+__device__ __forceinline__ void phase_a(const MP& mp, const float (&cur)[32], float (&o0)[32], float (&o1)[32],
+                                        const ERow<EW>& E0, const ERow<EW>& E1, uint32_t (&wd)[9], bool okL, int ok_ra)
+{
+    uint32_t alo = 0, ahi = 0, hb0 = 0, hb1 = 0, bc0 = 0, bc1 = 0;
+#pragma unroll
+    for (int u = 7; u >= 0; u--) {
+        float iv[2][4];
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+            const int ra = u + 8 * hh;
+            const int q = qreg<0>(mp, ra);
+            if (INIT) {
+                const bool ok = okL && (ok_ra < 0 || ok_ra == ra);
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+#pragma unroll
+                    for (int b = 0; b < 2; b++) iv[b][2 * hh + c] = ok ? mp.get(E0, (((q << 1) | c) << 1) | b) : BIG;
+            } else {
+                const float va = cur[ra], vb = cur[ra + 16];
+                const float d = __fsub_rn(vb, va);
+                const float mn = fminf(va, vb);
+                if (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+#pragma unroll
+                    for (int b = 0; b < 2; b++) iv[b][2 * hh + c] = __fadd_rn(mn, mp.get(E0, (((q << 1) | c) << 1) | b));
+            }
+        }
+#pragma unroll
+        for (int c = 1; c >= 0; c--) {
+            const int x = 2 * u + c;
+            const int q = qreg<1>(mp, x);
+            float mnb[2];
+#pragma unroll
+            for (int b = 0; b < 2; b++) {
+                const float va = iv[b][c], vb = iv[b][2 + c];
+                const float d = __fsub_rn(vb, va);
+                mnb[b] = fminf(va, vb);
+                if (b) hb1 = pushbit(d, hb1); else hb0 = pushbit(d, hb0);
+            }
+#pragma unroll
+            for (int c2 = 1; c2 >= 0; c2--) {
+                const int lb = (q << 1) | c2;
+                if (EQ) {
+                    o0[2 * x + c2] = __fadd_rn(mnb[0], mp.get(E1, lb << 1));
+                    o1[2 * x + c2] = __fadd_rn(mnb[1], mp.get(E1, (lb << 1) | 1));
+                    bc0 = bc0 << 1;
+                    bc1 = (bc1 << 1) | 1u;
+                } else {
+#pragma unroll
+                    for (int cl = 0; cl < 2; cl++) {
+                        const float v0 = __fadd_rn(mnb[0], mp.get(E1, (lb << 1) | cl));        // b = 0: low bit 0 ^ cl
+                        const float v1 = __fadd_rn(mnb[1], mp.get(E1, (lb << 1) | (1 ^ cl)));  // b = 1
+                        const uint32_t dbit = __float_as_uint(__fsub_rn(v1, v0));
+                        if (cl) { bc1 = __funnelshift_l(dbit, bc1, 1); o1[2 * x + c2] = fminf(v0, v1); }
+                        else { bc0 = __funnelshift_l(dbit, bc0, 1); o0[2 * x + c2] = fminf(v0, v1); }
+                    }
+                }
+            }
+        }
+    }
+    wd[0] = INIT ? 0u : ((ahi << 8) | alo);
+    wd[1] = (hb0 << 16) | hb1;
+    wd[2] = bc0;
+    wd[3] = bc1;
+}
+
+// D4 / EQ phase B: steps (2, 3).  Step 2: intermediates per class c and low bit b; step 3: outputs over the candidates
+// (c, b) = (0,0), (0,1), (1,0), (1,1) in that order with strict `<` (EQ: (0,0), (1,1)).
+// Words: w4 = step-2 decisions per class (c0 << 16 | c1), w5 / w6 = step-3 decisions for class 0 / 1 per b
+// (b0 << 16 | b1), w7 = chosen class per output, w8 = chosen b per output.
+template <bool EQ, class MP, int EW>
+__device__ __forceinline__ void phase_b(const MP& mp, const float (&o0)[32], const float (&o1)[32], float (&cur)[32],
+                                        const ERow<EW>& E2, const ERow<EW>& E3, uint32_t (&wd)[9])
+{
+    uint32_t hlo[2] = {0, 0}, hhi[2] = {0, 0}, hbb[2][2] = {{0, 0}, {0, 0}}, S1 = 0, S2 = 0, S3 = 0;
+#pragma unroll
+    for (int u = 7; u >= 0; u--) {
+        float iv[2][2][4];
+#pragma unroll
+        for (int cl = 0; cl < 2; cl++) {
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const int ra = u + 8 * hh;
+                const int q = qreg<2>(mp, ra);
+                const float va = cl ? o1[ra] : o0[ra], vb = cl ? o1[ra + 16] : o0[ra + 16];
+                const float d = __fsub_rn(vb, va);
+                const float mn = fminf(va, vb);
+                if (hh) hhi[cl] = pushbit(d, hhi[cl]); else hlo[cl] = pushbit(d, hlo[cl]);
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+#pragma unroll
+                    for (int b = 0; b < 2; b++)
+                        if (!EQ || b == cl)
+                            iv[cl][b][2 * hh + c] = __fadd_rn(mn, mp.get(E2, (((q << 1) | c) << 1) | b));
+            }
+        }
+#pragma unroll
+        for (int c = 1; c >= 0; c--) {
+            const int x = 2 * u + c;
+            const int q = qreg<3>(mp, x);
+            float mnx[2][2];
+#pragma unroll
+            for (int cl = 0; cl < 2; cl++)
+#pragma unroll
+                for (int b = 0; b < 2; b++) {
+                    if (EQ && b != cl) { hbb[cl][b] <<= 1; mnx[cl][b] = BIG; continue; }
+                    const float va = iv[cl][b][c], vb = iv[cl][b][2 + c];
+                    const float d = __fsub_rn(vb, va);
+                    mnx[cl][b] = fminf(va, vb);
+                    hbb[cl][b] = pushbit(d, hbb[cl][b]);
+                }
+#pragma unroll
+            for (int c2 = 1; c2 >= 0; c2--) {
+                const int lb = (q << 1) | c2;
+                if (EQ) {
+                    const float v0 = __fadd_rn(mnx[0][0], mp.get(E3, lb << 1));
+                    const float v1 = __fadd_rn(mnx[1][1], mp.get(E3, (lb << 1) | 1));
+                    S3 = pushbit(__fsub_rn(v1, v0), S3);
+                    cur[2 * x + c2] = fminf(v0, v1);
+                } else {
+                    const float v00 = __fadd_rn(mnx[0][0], mp.get(E3, lb << 1));
+                    const float v01 = __fadd_rn(mnx[0][1], mp.get(E3, (lb << 1) | 1));
+                    const float v10 = __fadd_rn(mnx[1][0], mp.get(E3, (lb << 1) | 1));
+                    const float v11 = __fadd_rn(mnx[1][1], mp.get(E3, lb << 1));
+                    float best = v00;
+                    S1 = pushbit(__fsub_rn(v01, best), S1);
+                    best = fminf(best, v01);
+                    S2 = pushbit(__fsub_rn(v10, best), S2);
+                    best = fminf(best, v10);
+                    S3 = pushbit(__fsub_rn(v11, best), S3);
+                    best = fminf(best, v11);
+                    cur[2 * x + c2] = best;
+                }
+            }
+        }
+    }
+    wd[4] = (((hhi[0] << 8) | hlo[0]) << 16) | ((hhi[1] << 8) | hlo[1]);
+    wd[5] = (hbb[0][0] << 16) | (hbb[0][1] & 0xffffu);
+    wd[6] = (hbb[1][0] << 16) | (hbb[1][1] & 0xffffu);
+    if (EQ) {
+        wd[7] = S3;
+        wd[8] = S3;
+    } else {
+        wd[7] = S2 | S3;
+        wd[8] = S3 | (S1 & ~S2);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// the kernel
+// ------------------------------------------------------------------------------------------------
+// SUB2: sub-block boundaries may fall in the middle of a 4-step group (sub = 2 mod 4; plain and D2 only).
+template <class MP, int MD, bool SUB2>
+__global__ void __launch_bounds__(256) vit_kernel(const VitParams p)
+{
+    constexpr int NL = MP::NL, NP = MD ? 2 : 1, NV = NL / 2, EW = NL * NP;
+    constexpr bool PP = MD == 1, G4 = MD >= 2, EQ = MD == 3;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int T = p.T, G = p.G, sub = p.sub, nsub = T / sub, U = p.U, U_hi = p.U_hi, mix = p.mix, Gf = p.Gfull;
+    const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, g = tid >> 5, nthr = blockDim.x;
+    const SmemLayout SL = smem_layout(T, G, Gf, sub, NL, NP, U, U_hi, p.W4, p.NB);
+    float* s_x = reinterpret_cast<float*>(smem + SL.x);
+    float* s_w = reinterpret_cast<float*>(smem + SL.w);
+    float* s_tab = reinterpret_cast<float*>(smem + SL.tab);
+    float* s_tabhi = reinterpret_cast<float*>(smem + SL.tabhi);
+    float* s_gain = reinterpret_cast<float*>(smem + SL.gain);
+    float* s_gainhi = reinterpret_cast<float*>(smem + SL.gainhi);
+    float* s_ce = reinterpret_cast<float*>(smem + SL.ce);
+    uint8_t* s_gc = smem + SL.gc;
+    float* s_dp = reinterpret_cast<float*>(smem + SL.dp);
+    float* s_err = reinterpret_cast<float*>(smem + SL.err);
+    uint32_t* s_tbw = reinterpret_cast<uint32_t*>(smem + SL.tbw);
+    uint32_t* s_tbg = reinterpret_cast<uint32_t*>(smem + SL.tbg);
+    uint16_t* s_st = reinterpret_cast<uint16_t*>(smem + SL.st);
+    uint8_t* s_sg = smem + SL.sg;
+    uint8_t* s_par = smem + SL.par;
+    float* red_v = reinterpret_cast<float*>(smem + SL.red);
+    int* red_i = reinterpret_cast<int*>(smem + SL.red + 4 * MAXG);
+    int* s_flag = reinterpret_cast<int*>(smem + SL.flag);
+    const MP mp(p);
+
+    // ---- tile inputs (sample t is element (t + rot) % ld), tables, gains ----
+    for (int i = tid; i < T; i += nthr) {
+        const int j = (i + p.rot) % p.ld;
+        s_x[i] = p.x[(size_t)n * p.ld + j];
+        s_w[i] = p.w[(size_t)n * p.ldw + j];
+    }
+    for (int i = tid; i < NL * U; i += nthr) s_tab[i] = p.tab[i];
+    for (int i = tid; i < NL * U_hi; i += nthr) s_tabhi[i] = p.tab_hi[i];
+    if (tid < Gf) { s_gain[tid] = p.gains[tid]; s_gainhi[tid] = p.gains_hi[tid]; }
+    __syncthreads();
+
+    // ---- gain candidates: weighted scalar error of each sub-block over the merged table (src/cuda/tcq_viterbi.cu:155-180)
+    if (p.cand) {
+        for (int i = tid; i < nsub * Gf; i += nthr) {
+            const int j = i / Gf, gi = i % Gf;
+            float e = 0.f;
+            for (int t = j * sub; t < (j + 1) * sub; t++) {
+                const bool hi = mix > 0 && ((t / mix) & 1);
+                const float be = hi ? branch_err(s_x[t], s_gainhi[gi], s_tabhi, 0, 1, NL * U_hi)
+                                    : branch_err(s_x[t], s_gain[gi], s_tab, 0, 1, NL * U);
+                e = __fmaf_rn(be, s_w[t], e);
+            }
+            s_ce[i] = e;
+        }
+        __syncthreads();
+        if (tid < nsub) {
+            uint32_t used = 0;
+            for (int c = 0; c < G; c++) {
+                int bg = 0;
+                float be = BIG;
+                for (int gi = 0; gi < Gf; gi++)
+                    if (!((used >> gi) & 1u) && s_ce[tid * Gf + gi] < be) { be = s_ce[tid * Gf + gi]; bg = gi; }
+                used |= 1u << bg;
+                s_gc[tid * G + c] = (uint8_t)bg;
+                p.gcand[((size_t)n * nsub + tid) * G + c] = (uint8_t)bg;
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- per-lane constants ----
+    int PLj[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) PLj[j] = mp.hi((unsigned)((lane << j) & 511));
+    const int s0 = p.init_st ? p.init_st[n] : -1;
+    const bool okL = s0 < 0 || lane == (s0 & 31);
+    const int ok_ra = s0 < 0 ? -1 : ((s0 >> 5) & 15);
+    const SvStream sv{p.svA + ((size_t)n * G + g) * (size_t)p.capA, p.svB + ((size_t)n * G + g) * (size_t)p.capB,
+                      p.capA};
+    float* myerr = s_err + (size_t)g * sub * NV * EW;
+
+    // branch-error table of sub-block sb for this warp's gain slot, NV label variants per step (src/cuda/tcq_viterbi.cu:202-213)
+    auto build_err = [&](int sb) {
+        const int t0 = sb * sub;
+        const int gi = p.cand ? (int)s_gc[sb * G + g] : g;
+        __syncwarp();
+        for (int it = lane; it < sub * NL * NP; it += 32) {
+            const int tt = it / (NL * NP), lb = (it / NP) % NL, pc = it % NP;
+            const int t = t0 + tt;
+            const bool hi = mix > 0 && ((t / mix) & 1);
+            float e;
+            if (MD) e = branch_err(s_x[t], s_gain[gi], s_tab + lb * U, pc, 2, U);
+            else if (hi) e = branch_err(s_x[t], s_gainhi[gi], s_tabhi + lb * U_hi, 0, 1, U_hi);
+            else e = branch_err(s_x[t], s_gain[gi], s_tab + lb * U, 0, 1, U);
+            e = __fmul_rn(e, s_w[t]);
+#pragma unroll
+            for (int P = 0; P < NV; P++) myerr[((size_t)tt * NV + P) * EW + ((lb ^ (P << 1)) * NP + pc)] = e;
+        }
+        __syncwarp();
+    };
+    auto row = [&](int t, int j) -> const float* {
+        return myerr + ((size_t)(t % sub) * NV + PLj[j]) * EW;
+    };
+
+    float* mydp = s_dp + (size_t)g * NSP;
+    // metrics of layout jf -> shared -> layout jt; with merge: min over all G slots (strict <, lowest g), slot 0
+    // records the winner per state (src/cuda/tcq_viterbi.cu:185-201)
+    auto exchange = [&](float (&cur)[32], int jf, int jt, bool merge, int sb) {
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < 32; r++) mydp[swz(state_of(jf, lane, r))] = cur[r];
+        if (!merge) {
+            __syncwarp();
+#pragma unroll
+            for (int r = 0; r < 32; r++) cur[r] = mydp[swz(state_of(jt, lane, r))];
+            return;
+        }
+        __syncthreads();
+        uint32_t gw0 = 0, gw1 = 0, gw2 = 0, gw3 = 0;
+#pragma unroll
+        for (int r = 31; r >= 0; r--) {
+            const int a = swz(state_of(jt, lane, r));
+            float v = s_dp[a];
+            if (g == 0) {
+                int bg = 0;
+                for (int gg = 1; gg < G; gg++) {
+                    const float vv = s_dp[(size_t)gg * NSP + a];
+                    if (vv < v) { v = vv; bg = gg; }
+                }
+                gw0 = (gw0 << 1) | (uint32_t)(bg & 1);
+                gw1 = (gw1 << 1) | (uint32_t)((bg >> 1) & 1);
+                gw2 = (gw2 << 1) | (uint32_t)((bg >> 2) & 1);
+                gw3 = (gw3 << 1) | (uint32_t)((bg >> 3) & 1);
+            } else {
+                for (int gg = 1; gg < G; gg++) v = fminf(v, s_dp[(size_t)gg * NSP + a]);
+            }
+            cur[r] = v;
+        }
+        if (g == 0) {
+            uint32_t* gp = p.gsw + ((size_t)n * nsub + sb) * p.NB * 32 + lane;
+            gp[0] = gw0;
+            if (p.NB > 1) gp[32] = gw1;
+            if (p.NB > 2) { gp[64] = gw2; gp[96] = gw3; }
+        }
+        __syncthreads();
+    };
+
+    // ---- forward ----
+    float cur[32];
+    for (int t4 = 0; t4 < T; t4 += 4) {
+        const long long kbase = (long long)(t4 >> 2) * p.W4 * 32 + lane;
+        uint32_t wd[9];
+#pragma unroll
+        for (int k = 0; k < 9; k++) wd[k] = 0;
+        // pair / phase A: steps t4, t4 + 1
+        if (t4 == 0) {
+            build_err(0);
+        } else {
+            const bool bnd = (t4 % sub) == 0;
+            exchange(cur, 4, 0, bnd && G > 1, t4 / sub);
+            if (bnd) build_err(t4 / sub);
+        }
+        ERow<EW> E0, E1;
+        load_row<MP>(E0, row(t4, 0));
+        load_row<MP>(E1, row(t4 + 1, 1));
+        float o0[G4 ? 32 : 1], o1[G4 ? 32 : 1];
+        if (!MD) {
+            if (t4 == 0) pair_plain<0, true>(mp, cur, E0, E1, wd[0], okL, ok_ra);
+            else pair_plain<0, false>(mp, cur, E0, E1, wd[0], okL, ok_ra);
+        } else if (PP) {
+            uint32_t wi;
+            if (t4 == 0) pair_d2<0, true>(mp, cur, E0, E1, wi, wd[1], wd[2], okL, ok_ra);
+            else pair_d2<0, false>(mp, cur, E0, E1, wi, wd[1], wd[2], okL, ok_ra);
+            wd[0] = wi << 16;  // step-0 decisions in the high half, step-2 decisions in the low half
+        } else {
+            if constexpr (G4) {
+                if (t4 == 0) phase_a<true, EQ>(mp, cur, o0, o1, E0, E1, wd, okL, ok_ra);
+                else phase_a<false, EQ>(mp, cur, o0, o1, E0, E1, wd, okL, ok_ra);
+            }
+        }
+        // pair / phase B: steps t4 + 2, t4 + 3
+        if (t4 + 2 < T) {
+            if constexpr (SUB2 && !G4) {
+                if (((t4 + 2) % sub) == 0) {  // sub-block boundary inside the group
+                    if (G > 1) exchange(cur, 2, 2, true, (t4 + 2) / sub);
+                    build_err((t4 + 2) / sub);
+                }
+            }
+            ERow<EW> E2, E3;
+            load_row<MP>(E2, row(t4 + 2, 2));
+            load_row<MP>(E3, row(t4 + 3, 3));
+            if (!MD) {
+                uint32_t w1;
+                pair_plain<2, false>(mp, cur, E2, E3, w1, okL, ok_ra);
+                wd[1] = w1;
+            } else if (PP) {
+                uint32_t wi;
+                pair_d2<2, false>(mp, cur, E2, E3, wi, wd[3], wd[4], okL, ok_ra);
+                wd[0] |= wi;
+            } else {
+                if constexpr (G4) phase_b<EQ>(mp, o0, o1, cur, E2, E3, wd);
+            }
+        }
+        // survivor words of this group (the last group of T = 2 mod 4 keeps only its first pair's words)
+        const int nw = (t4 + 2 < T) ? p.W4 : (MD == 0 ? 1 : 3);
+        if (!MD) {
+            sv.put(kbase, wd[0]);
+            if (nw > 1) sv.put(kbase + 32, wd[1]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 9; k++)
+                if (k < nw) sv.put(kbase + 32 * k, wd[k]);
+        }
+    }
+
+    // ---- final argmin over (slot, state), tail-biting keeps s == s0 (src/cuda/tcq_viterbi.cu:561-579) ----
+    const int jend = ((T - 1) & 3) + 1;
+    const int s_end = p.tail ? s0 : -1;
+    float bv = BIG;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int r = 0; r < 32; r++) {
+        const int s = state_of(jend, lane, r);
+        const int idx = g * NS + s;
+        const float v = (s_end < 0 || s == s_end) ? cur[r] : BIG;
+        if (v < bv || (v == bv && idx < bi)) { bv = v; bi = idx; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_down_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_down_sync(0xffffffffu, bi, off);
+        if (ov < bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { red_v[g] = bv; red_i[g] = bi; }
+    __syncthreads();
+
+    // ---- traceback (warp 0): one sub-block chunk at a time, chunk survivors staged in shared memory ----
+    if (g == 0) {
+        if (lane == 0) {
+            for (int k = 1; k < G; k++)
+                if (red_v[k] < bv || (red_v[k] == bv && red_i[k] < bi)) { bv = red_v[k]; bi = red_i[k]; }
+            p.best[n] = bi;
+            if (p.end_st) p.end_st[n] = bi % NS;
+            s_flag[0] = bi % NS;  // state
+            s_flag[1] = bi / NS;  // slot
+            s_flag[2] = 0;        // stopped at the first-pass middle
+        }
+        __syncwarp();
+        for (int lo = T - sub; lo >= 0; lo -= sub) {
+            const int gc = s_flag[1];
+            const int grp0 = lo >> 2, grp1 = (lo + sub - 1) >> 2;
+            const SvStream svg{p.svA + ((size_t)n * G + gc) * (size_t)p.capA,
+                               p.svB + ((size_t)n * G + gc) * (size_t)p.capB, p.capA};
+            for (int grp = grp0; grp <= grp1; grp++) {
+                const int nw = (grp * 4 + 2 < T) ? p.W4 : (MD == 0 ? 1 : 3);
+                for (int k = 0; k < nw; k++)
+                    s_tbw[((grp - grp0) * p.W4 + k) * 32 + lane] = svg.get(((long long)grp * p.W4 + k) * 32 + lane);
+            }
+            if (G > 1 && lo > 0)
+                for (int k = 0; k < p.NB; k++)
+                    s_tbg[k * 32 + lane] = p.gsw[(((size_t)n * nsub + lo / sub) * p.NB + k) * 32 + lane];
+            __syncwarp();
+            if (lane == 0) {
+                int st = s_flag[0], gs = s_flag[1], pcur = 0, cstar = 0;
+                bool stop = false;
+                for (int t = lo + sub - 1; t >= lo; t--) {
+                    s_st[t] = (uint16_t)st;
+                    s_sg[t] = (uint8_t)gs;
+                    const int j = t & 3;
+                    const int b9 = st >> 1;
+                    const int L = (b9 >> j) & 31;
+                    const int bi4 = bfly_of(j, b9);
+                    const uint32_t* W = s_tbw + ((t >> 2) - grp0) * p.W4 * 32 + L;  // word k of this group: W[32 k]
+                    if (PP && (t & 1)) {
+                        pcur = (W[32 * (j == 1 ? 2 : 4)] >> ((bi4 << 1) | (st & 1))) & 1;
+                        s_par[t] = s_par[t - 1] = (uint8_t)pcur;
+                    }
+                    if (p.mid_st && t == p.mid_t - 1) { p.mid_st[n] = st; stop = true; break; }
+                    if (t == 0) break;
+                    int h;
+                    if (!MD) {
+                        h = (W[32 * (j >> 1)] >> ((j & 1) ? bi4 : 16 + bi4)) & 1;
+                    } else if (PP) {
+                        if (j & 1) h = (W[32 * (j == 1 ? 1 : 3)] >> (pcur ? bi4 : 16 + bi4)) & 1;
+                        else h = (W[0] >> ((j == 0) ? 16 + bi4 : bi4)) & 1;
+                    } else {
+                        const int ro = (bi4 << 1) | (st & 1);  // output register of st at steps j = 1, 3
+                        if (j == 3) {
+                            cstar = (W[32 * 7] >> ro) & 1;
+                            const int bb = (W[32 * 8] >> ro) & 1;
+                            h = (W[32 * (5 + cstar)] >> (bb ? bi4 : 16 + bi4)) & 1;
+                            if (EQ) {
+                                s_par[t] = s_par[t - 1] = s_par[t - 2] = s_par[t - 3] = (uint8_t)cstar;
+                            } else {
+                                s_par[t] = (uint8_t)(bb ^ cstar);
+                                s_par[t - 1] = (uint8_t)bb;
+                            }
+                        } else if (j == 2) {
+                            h = (W[32 * 4] >> (cstar ? bi4 : 16 + bi4)) & 1;
+                        } else if (j == 1) {
+                            const int bb = (W[32 * (2 + cstar)] >> ro) & 1;
+                            h = (W[32 * 1] >> (bb ? bi4 : 16 + bi4)) & 1;
+                            if (!EQ) {
+                                s_par[t] = (uint8_t)(bb ^ cstar);
+                                s_par[t - 1] = (uint8_t)bb;
+                            }
+                        } else {
+                            h = (W[0] >> bi4) & 1;
+                        }
+                    }
+                    st = (h << 9) | b9;
+                    if (G > 1 && t == lo) {  // sub-block boundary: slot of the previous sub-block
+                        const int jm = lo & 3;
+                        const int Lg = (st >> jm) & 31;
+                        const int rg = (st & ((1 << jm) - 1)) | ((st >> (jm + 5)) << jm);
+                        int v = 0;
+                        for (int k = 0; k < p.NB; k++) v |= (int)((s_tbg[k * 32 + Lg] >> rg) & 1u) << k;
+                        gs = v;
+                    }
+                }
+                s_flag[0] = st;
+                s_flag[1] = gs;
+                if (stop) s_flag[2] = 1;
+            }
+            __syncwarp();
+            if (s_flag[2]) break;
+        }
+    }
+    __syncthreads();
+    if (s_flag[2]) return;  // first tail-biting pass: only the middle state was needed
+
+    // ---- reconstruction and codes (src/cuda/tcq_viterbi.cu:662-682) ----
+    float* rn = p.rec + (size_t)n * p.ld;
+    for (int t = tid; t < T; t += nthr) {
+        const int stt = s_st[t], gg = s_sg[t];
+        const int lb = (stt & 1) | (mp.hi((unsigned)(stt >> 1)) << 1);
+        const bool hi = mix > 0 && ((t / mix) & 1);
+        const int Ut = hi ? U_hi : U;
+        const int gi = p.cand ? (int)s_gc[(t / sub) * G + gg] : gg;
+        const float gt = hi ? s_gainhi[gi] : s_gain[gi];
+        const float* tt = (hi ? s_tabhi : s_tab) + lb * Ut;
+        const float xt = s_x[t];
+        float bestd = BIG, val = 0.f;
+        int bu = 0;
+        for (int u = MD ? s_par[t] : 0; u < Ut; u += MD ? 2 : 1) {
+            const float v = __fmul_rn(gt, tt[u]);
+            const float d = __fmaf_rn(-gt, tt[u], xt);
+            const float dd = __fmul_rn(d, d);
+            if (dd < bestd) { bestd = dd; val = v; bu = u; }
+        }
+        const int tp = (t + p.rot) % p.ld;
+        rn[tp] = val;
+        if (p.code) p.code[(size_t)n * p.ld + tp] = (gi << 16) | (lb * Ut + bu);
+    }
+}
+
+}  // namespace ltqb

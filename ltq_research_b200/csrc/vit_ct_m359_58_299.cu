@@ -1,0 +1,8 @@
+// Viterbi kernel instantiation: label masks (359, 58, 299, 0), 16 subsets.
+#include "vit_launch.cuh"
+namespace ltqb {
+int launch_ct_m359_58_299(const VitParams& p, int md, int smem, cudaStream_t st)
+{
+    return launch_md<MaskCT<359, 58, 299, 0, 16>>(p, md, smem, st);
+}
+}  // namespace ltqb

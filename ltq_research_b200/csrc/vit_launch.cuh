@@ -1,0 +1,71 @@
+// Launch helpers for the Viterbi kernel instantiations (one translation unit per label-mask set).
+#pragma once
+#include <atomic>
+#include "tcq_viterbi_kernel.cuh"
+
+namespace ltqb {
+
+// Raise the kernel's dynamic shared-memory limit to the device maximum once per (kernel, device).  The limit is
+// always set to the same value, so concurrent callers on other host threads cannot lower it under a launch.
+template <class K>
+inline int ensure_smem(K kernel, int smem)
+{
+    if (smem <= 48 * 1024) return 0;
+    static std::atomic<int> done[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (done[dev].load(std::memory_order_acquire)) return 0;
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess) return -1;
+    const int want = optin - (int)fa.sharedSizeBytes;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want) != cudaSuccess) return -1;
+    done[dev].store(1, std::memory_order_release);
+    return smem <= want ? 0 : -1;
+}
+
+template <class MP, int MD, bool SUB2 = false>
+inline int launch_one(const VitParams& p, int smem, cudaStream_t st)
+{
+    auto k = vit_kernel<MP, MD, SUB2>;
+    if (ensure_smem(k, smem) != 0) return -1;
+    k<<<p.N, 32 * p.G, smem, st>>>(p);
+    return 0;
+}
+
+// sub-blocks that are not a multiple of 4 steps (no format uses them) run the SUB2 variant, plain and D2 only
+template <class MP>
+inline int launch_md_sub2(const VitParams& p, int md, int smem, cudaStream_t st)
+{
+    switch (md) {
+        case 0: return launch_one<MP, 0, true>(p, smem, st);
+        case 1: return launch_one<MP, 1, true>(p, smem, st);
+        default: return -1;
+    }
+}
+
+template <class MP>
+inline int launch_md(const VitParams& p, int md, int smem, cudaStream_t st)
+{
+    switch (md) {
+        case 0: return launch_one<MP, 0>(p, smem, st);
+        case 1: return launch_one<MP, 1>(p, smem, st);
+        case 2: return launch_one<MP, 2>(p, smem, st);
+        case 3: return launch_one<MP, 3>(p, smem, st);
+        default: return -1;
+    }
+}
+
+// label-mask sets with compiled-in masks (every set used by the reference's format tables; primary mask 359)
+int launch_ct_m359(const VitParams& p, int md, int smem, cudaStream_t st);          // 4 subsets
+int launch_ct_m359_241(const VitParams& p, int md, int smem, cudaStream_t st);      // 8
+int launch_ct_m359_462(const VitParams& p, int md, int smem, cudaStream_t st);      // 8
+int launch_ct_m359_146(const VitParams& p, int md, int smem, cudaStream_t st);      // 8
+int launch_ct_m359_58_299(const VitParams& p, int md, int smem, cudaStream_t st);   // 16
+int launch_ct_m359_211_397(const VitParams& p, int md, int smem, cudaStream_t st);  // 16
+int launch_ct_m359_40_475(const VitParams& p, int md, int smem, cudaStream_t st);   // 16
+int launch_rt(const VitParams& p, int md, int smem, cudaStream_t st);               // any masks, nl 4 / 8 / 16
+int launch_rt_sub2(const VitParams& p, int md, int smem, cudaStream_t st);          // any masks, sub = 2 mod 4
+
+}  // namespace ltqb
