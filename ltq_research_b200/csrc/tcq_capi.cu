@@ -2,7 +2,7 @@
 // (include/ltq_b200.h): the reference-compatible `tcq_viterbi` and the one-call tail-biting schedule `ltq_viterbi_tb`.
 #include <stdlib.h>
 #include <algorithm>
-#include "../../include/ltq_b200.h"
+#include "ltq_b200.h"
 #include "vit_launch.cuh"
 
 namespace ltqb {
@@ -39,7 +39,7 @@ static bool valid(int N, int T, int S, int U, int G, int Gfull, bool cand, int s
 static int dispatch(const VitParams& p, int pp, cudaStream_t st)
 {
     const int NP = pp ? 2 : 1;
-    const int smem = smem_layout(p.T, p.G, p.Gfull, p.sub, p.nl, NP, p.U, p.U_hi, p.W4, p.NB).total;
+    const int smem = fwd_smem(p.T, p.G, p.Gfull, p.sub, p.nl, NP, p.U, p.U_hi).total;
     if (p.sub % 4) return launch_rt_sub2(p, pp, smem, st);
     if (p.m == 359) {
         if (p.nl == 4) return launch_ct_m359(p, pp, smem, st);
@@ -63,7 +63,9 @@ static int run_pass(VitParams p, int pp, cudaStream_t st)
     p.W4 = words_per_group(pp);
     p.NB = gsel_planes(p.G);
     if (p.N <= 0) return (int)cudaErrorInvalidConfiguration;  // the reference launches an empty grid: error 9
-    return dispatch(p, pp, st);
+    const int rc = dispatch(p, pp, st);
+    if (rc != 0) return rc;
+    return launch_tb(p, pp, st);
 }
 
 static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }

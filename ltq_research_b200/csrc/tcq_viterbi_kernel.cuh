@@ -1,28 +1,30 @@
-// B200 (sm_100a) TCQ Viterbi for the LTQ tile format: forward add-compare-select, in-block traceback,
-// reconstruction and code emission, for one tile of T samples per CTA.
+// B200 (sm_100a) TCQ Viterbi for the LTQ tile format.
 //
 // Semantics follow the reference kernel tcq_forward_kernel (lumen-inference/ltq-research,
 // src/cuda/tcq_viterbi.cu:97-683) bit for bit: the same fp32 operations on the same operands (branch error
 // w * min_u fma(-g, tab[u], x)^2, path metric = selected predecessor + branch error), the same strict-`<` tie-breaks,
 // the same sub-block gain merge, gain candidates, D2 / D4 / EQ parity classes, tail-biting start / end constraints.
-// The organisation is new:
+// The organisation is new; two kernels per Viterbi pass:
 //
-//   * one warp per gain slot g; a CTA is one tile with G warps;
+// vit_fwd_kernel — forward add-compare-select, one CTA per tile, one warp per gain slot g:
 //   * each lane keeps 32 of the 1024 path metrics in registers.  In "layout j" lane L holds the states
 //       s = r_lo | L << j | r_hi << (j + 5),  register r = r_hi << j | r_lo   (r_lo: j bits, r_hi: 5 - j bits)
 //     so the two predecessors of a butterfly (bit 9 of the state = bit 4 of the register) sit in registers ra and
 //     ra + 16 of the same lane, and one trellis step maps registers (ra, ra + 16) -> (2 ra, 2 ra + 1) for every j
-//     (a perfect shuffle).  Four steps (j = 0..3) run in registers; then the metrics go through shared memory once
-//     (layout 4 -> layout 0, padded, conflict-free), i.e. one exchange per 4 trellis steps;
+//     (a perfect shuffle).  Four steps (j = 0..3) run in registers as two radix-4 passes; then the metrics go through
+//     shared memory once (layout 4 -> layout 0, padded, conflict-free), i.e. one exchange per 4 trellis steps;
 //   * a compare is the sign of (b - a) on the FMA pipe, the select is FMNMX, and the decision bit is packed with a
 //     funnel shift: 16 decisions per lane per step become one half word, stored coalesced as survivor words;
-//   * subset labels are split into a per-lane part (a table variant chosen once per step) and a per-register part
-//     that is a compile-time constant when the label masks are template parameters (MaskCT), so a branch error is a
-//     register operand, not a shared-memory lookup.  MaskRT is the same kernel for arbitrary masks (errors read from
-//     shared memory per butterfly).
-//
-// Survivors (decision bits) go to global memory in a per-(tile, slot) linear word stream (see SvStream below);
-// the traceback walks them per sub-block chunk from shared memory.
+//   * subset labels are split into a per-lane part (a branch-error table variant chosen once per step) and a
+//     per-register part that is a compile-time constant when the label masks are template parameters (MaskCT), so a
+//     branch error is a register operand.  MaskRT is the same kernel for arbitrary masks (errors read from shared
+//     memory per butterfly);
+//   * the tile start is a virtual step from metrics 0 (allowed predecessors of the start state) / 3.4e38 (others), which
+//     yields exactly the reference's initial metrics (err, or 3.4e38 for states the start state cannot reach);
+//   * decision bits go to global memory as a per-(tile, slot) linear word stream (SvStream), the gain-merge winners as
+//     bit planes; the final argmin over (slot, state) goes to best[n].
+// vit_tb_kernel — traceback, reconstruction and codes, one warp per tile: one sub-block chunk of survivor words at a
+//   time is staged in shared memory and walked by lane 0; all lanes then rebuild the samples.
 #pragma once
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -34,6 +36,7 @@ constexpr float BIG = 3.4e38f;  // the reference's "infinite" path metric (src/c
 constexpr int NS = 1024;        // trellis states (10-bit memory)
 constexpr int NSP = NS + NS / 32;  // exchange slots per gain slot (padded)
 constexpr int MAXG = 16, MAXU = 128, MAXSUBS = 32, MAXT = 512;
+constexpr int TB_WARPS = 8;     // tiles (warps) per traceback CTA
 
 struct VitParams {
     const float *x, *w, *tab, *gains, *tab_hi, *gains_hi;
@@ -43,7 +46,7 @@ struct VitParams {
     int *end_st, *mid_st, *best;
     uint8_t* gcand;
     uint32_t *svA, *svB;   // survivor word stream: first capA words of each (tile, slot) in A, the rest in B
-    uint32_t* gsw;         // gain-merge decisions: [N][T/sub][NB][32] words
+    uint32_t* gsw;         // gain-merge winners: [N][T/sub][NB planes][32 words], bit s & 31 of word s >> 5
     long long capA, capB;  // words per (tile, slot) in A / B
     int mid_t, tail;
     int N, T, U, G, Gfull, sub, U_hi, mix, ld, ldw, rot;
@@ -52,6 +55,23 @@ struct VitParams {
     int NB;                // gsel bit planes
     int cand;
 };
+
+// ------------------------------------------------------------------------------------------------
+// compile-time loops: every register index and every label bit below is a constant expression
+// ------------------------------------------------------------------------------------------------
+template <int I>
+struct IC {
+    static constexpr int value = I;
+};
+// f(IC<B>), f(IC<B + S>), ... while the index has not reached E (S = +1 or -1)
+template <int B, int E, int S, class F>
+__device__ __forceinline__ void cfor(F&& f)
+{
+    if constexpr ((S > 0 && B < E) || (S < 0 && B > E)) {
+        f(IC<B>{});
+        cfor<B + S, E, S>(f);
+    }
+}
 
 // ------------------------------------------------------------------------------------------------
 // label masks
@@ -76,19 +96,23 @@ struct MaskCT {
     static constexpr bool RT = false;
     __device__ __forceinline__ explicit MaskCT(const VitParams&) {}
     // label bits 1.. of a state s whose (s >> 1) == v
-    __device__ __forceinline__ int hi(unsigned v) const
+    __host__ __device__ static constexpr int hic(unsigned v)
     {
-        int r = cpar(v & (unsigned)M0);
-        if (NL >= 8) r |= cpar(v & (unsigned)M1) << 1;
-        if (NL >= 16) r |= cpar(v & (unsigned)M2) << 2;
-        if (NL >= 32) r |= cpar(v & (unsigned)M3) << 3;
-        return r;
+        return cpar(v & (unsigned)M0) | (NL >= 8 ? cpar(v & (unsigned)M1) << 1 : 0) |
+               (NL >= 16 ? cpar(v & (unsigned)M2) << 2 : 0) | (NL >= 32 ? cpar(v & (unsigned)M3) << 3 : 0);
+    }
+    __device__ __forceinline__ int hi(unsigned v) const { return hic(v); }
+    // register part of the label bits of the outputs of butterfly RA at step J (a constant)
+    template <int J, int RA>
+    __host__ __device__ static constexpr int qc()
+    {
+        return hic((unsigned)((RA & ((1 << J) - 1)) | ((RA >> J) << (J + 5))));
     }
     template <int EW>
     __device__ __forceinline__ float get(const ERow<EW>& e, int i) const { return e.r[i]; }
 };
 
-// Runtime masks: same recursion, branch errors read from the shared-memory row.
+// Run-time masks: same recursion, branch errors read from the shared-memory row.
 template <int NL_>
 struct MaskRT {
     static constexpr int NL = NL_;
@@ -104,23 +128,37 @@ struct MaskRT {
         if (NL >= 32) r |= (__popc(v & m3) & 1) << 3;
         return r;
     }
+    template <int J, int RA>
+    __device__ __forceinline__ int q() const
+    {
+        return hi((unsigned)((RA & ((1 << J) - 1)) | ((RA >> J) << (J + 5))));
+    }
     template <int EW>
     __device__ __forceinline__ float get(const ERow<EW>& e, int i) const { return e.ptr[i]; }
 };
 
-// ------------------------------------------------------------------------------------------------
-// shared memory layout (host and device)
-// ------------------------------------------------------------------------------------------------
-struct SmemLayout {
-    int x, w, tab, tabhi, gain, gainhi, ce, gc, dp, err, tbw, tbg, st, sg, par, red, flag, total;
-};
+// full label of state s for nl subsets (src/cuda/tcq_viterbi.cu:85-95), run-time masks
+__device__ __forceinline__ int label_rt(int s, const VitParams& p)
+{
+    int lb = ((__popc((s >> 1) & p.m) & 1) << 1) | (s & 1);
+    if (p.nl >= 8) lb |= (__popc((s >> 1) & p.m2) & 1) << 2;
+    if (p.nl >= 16) lb |= (__popc((s >> 1) & p.m3) & 1) << 3;
+    if (p.nl >= 32) lb |= (__popc((s >> 1) & p.m4) & 1) << 4;
+    return lb;
+}
 
+// ------------------------------------------------------------------------------------------------
+// shared memory layouts (host and device)
+// ------------------------------------------------------------------------------------------------
 __host__ __device__ inline int al16(int v) { return (v + 15) & ~15; }
 
-__host__ __device__ inline SmemLayout smem_layout(int T, int G, int Gfull, int sub, int NL, int NP, int U, int U_hi,
-                                                  int W4, int NB)
+struct FwdSmem {
+    int x, w, tab, tabhi, gain, gainhi, ce, gc, dp, err, red, total;
+};
+
+__host__ __device__ inline FwdSmem fwd_smem(int T, int G, int Gfull, int sub, int NL, int NP, int U, int U_hi)
 {
-    SmemLayout L;
+    FwdSmem L;
     const int NV = NL / 2, EW = NL * NP;
     int o = 0;
     L.x = o; o = al16(o + 4 * T);
@@ -133,15 +171,33 @@ __host__ __device__ inline SmemLayout smem_layout(int T, int G, int Gfull, int s
     L.gc = o; o = al16(o + (T / sub) * G);
     L.dp = o; o = al16(o + 4 * NSP * G);
     L.err = o; o = al16(o + 4 * G * sub * NV * EW);
-    const int groups = (sub + 3) / 4 + 1;
-    L.tbw = o; o = al16(o + 4 * 32 * W4 * groups);
-    L.tbg = o; o = al16(o + 4 * 32 * NB);
-    L.st = o; o = al16(o + 2 * T);
-    L.sg = o; o = al16(o + T);
-    L.par = o; o = al16(o + T);
     L.red = o; o = al16(o + 8 * MAXG);
-    L.flag = o; o = al16(o + 16);
     L.total = o;
+    return L;
+}
+
+struct TbSmem {
+    int tab, tabhi, gain, gainhi, warp, tbw, tbg, st, sg, par, flag, per_warp, total;
+};
+
+__host__ __device__ inline TbSmem tb_smem(int T, int sub, int NL, int U, int U_hi, int W4, int NB, int warps)
+{
+    TbSmem L;
+    int o = 0;
+    L.tab = o; o = al16(o + 4 * NL * U);
+    L.tabhi = o; o = al16(o + 4 * NL * U_hi);
+    L.gain = o; o = al16(o + 4 * MAXG);
+    L.gainhi = o; o = al16(o + 4 * MAXG);
+    L.warp = o;
+    int q = 0;  // per-warp region, relative offsets
+    L.tbw = q; q = al16(q + 4 * 32 * W4 * ((sub + 3) / 4 + 1));
+    L.tbg = q; q = al16(q + 4 * 32 * NB);
+    L.st = q; q = al16(q + 2 * T);
+    L.sg = q; q = al16(q + T);
+    L.par = q; q = al16(q + T);
+    L.flag = q; q = al16(q + 16);
+    L.per_warp = q;
+    L.total = o + q * warps;
     return L;
 }
 
@@ -150,19 +206,14 @@ __host__ __device__ __forceinline__ int state_of(int j, int L, int r)
 {
     return (r & ((1 << j) - 1)) | (L << j) | ((r >> j) << (j + 5));
 }
-// exchange slot of state s: one pad word per 32 states.  For every layout j the address is a per-lane base
-// (L << j) + (L >> (5 - j)) plus a per-register constant, and the 32 lanes of a warp hit 32 distinct banks.
+// exchange slot of state s: one pad word per 32 states.  For every layout j the slot of register r of lane L is a
+// per-lane base (L << j) + (L >> (5 - j)) plus a per-register constant, and the 32 lanes of a warp hit 32 distinct banks.
 __device__ __forceinline__ int swz(int s) { return s + (s >> 5); }
+__device__ __forceinline__ int xbase(int j, int L) { return (L << j) + (L >> (5 - j)); }
+__host__ __device__ constexpr int xoff(int j, int r) { return (r & ((1 << j) - 1)) + (r >> j) * (33 << j); }
 
 // register index ra (0..15) of the butterfly whose outputs have (s >> 1) == b9, in layout j; lane = (b9 >> j) & 31
 __device__ __forceinline__ int bfly_of(int j, int b9) { return (b9 & ((1 << j) - 1)) | ((b9 >> (j + 5)) << j); }
-
-// label bits 1.. of the outputs of butterfly ra at step j, register part (the lane part is PLj[j])
-template <int J, class MP>
-__device__ __forceinline__ int qreg(const MP& mp, int ra)
-{
-    return mp.hi((unsigned)((ra & ((1 << J) - 1)) | ((ra >> J) << (J + 5))));
-}
 
 __device__ __forceinline__ uint32_t pushbit(float d, uint32_t acc)
 {
@@ -207,181 +258,161 @@ struct SvStream {
 };
 
 // ------------------------------------------------------------------------------------------------
+// branch error of the output with code bit C (and parity class P of NPc) of butterfly RA at step J
+// ------------------------------------------------------------------------------------------------
+template <class MP, int J, int RA, int C, int P, int NPc, int EW>
+__device__ __forceinline__ float errv(const MP& mp, const ERow<EW>& E)
+{
+    if constexpr (!MP::RT) {
+        constexpr int i = ((MP::template qc<J, RA>() << 1) | C) * NPc + P;
+        return E.r[i];
+    } else {
+        const int i = ((mp.template q<J, RA>() << 1) | C) * NPc + P;
+        return E.ptr[i];
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
 // trellis pairs: steps (J, J + 1), J in {0, 2}, processed as 8 radix-4 units per lane.
 // Unit u: step-J butterflies u and u + 8 -> intermediates 2u, 2u+1, 2u+16, 2u+17 -> step-(J+1) butterflies
 // 2u + 1, 2u -> outputs 4u .. 4u + 3.  Units run u = 7 .. 0 so every packed bit word is built in descending order.
-// INIT: the step-J inputs are the start of the tile (t = 0): no predecessor, only the successors of s0 are allowed.
 // ------------------------------------------------------------------------------------------------
-template <int J, bool INIT, class MP, int EW>
-__device__ __forceinline__ void pair_plain(const MP& mp, float (&cur)[32], const ERow<EW>& E0, const ERow<EW>& E1,
-                                           uint32_t& word, bool okL, int ok_ra)
+template <int J, class MP, int EW>
+__device__ __forceinline__ uint32_t pair_plain(const MP& mp, float (&cur)[32], const ERow<EW>& E0, const ERow<EW>& E1)
 {
     float nx[32];
     uint32_t alo = 0, ahi = 0, a2 = 0;
-#pragma unroll
-    for (int u = 7; u >= 0; u--) {
+    cfor<7, -1, -1>([&](auto UU) {
+        constexpr int u = decltype(UU)::value;
         float iv[4];
-#pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-            const int ra = u + 8 * hh;
-            const int q = qreg<J>(mp, ra);
-            if (INIT) {
-                const bool ok = okL && (ok_ra < 0 || ok_ra == ra);
-                iv[2 * hh] = ok ? mp.get(E0, q << 1) : BIG;
-                iv[2 * hh + 1] = ok ? mp.get(E0, (q << 1) | 1) : BIG;
-            } else {
-                const float va = cur[ra], vb = cur[ra + 16];
-                const float d = __fsub_rn(vb, va);
-                const float mn = fminf(va, vb);
-                if (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
-                iv[2 * hh] = __fadd_rn(mn, mp.get(E0, q << 1));
-                iv[2 * hh + 1] = __fadd_rn(mn, mp.get(E0, (q << 1) | 1));
-            }
-        }
-#pragma unroll
-        for (int c = 1; c >= 0; c--) {
-            const int x = 2 * u + c;
+        cfor<0, 2, 1>([&](auto HH) {
+            constexpr int hh = decltype(HH)::value, ra = u + 8 * hh;
+            const float va = cur[ra], vb = cur[ra + 16];
+            const float d = __fsub_rn(vb, va);
+            const float mn = fminf(va, vb);
+            if constexpr (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
+            iv[2 * hh] = __fadd_rn(mn, errv<MP, J, ra, 0, 0, 1>(mp, E0));
+            iv[2 * hh + 1] = __fadd_rn(mn, errv<MP, J, ra, 1, 0, 1>(mp, E0));
+        });
+        cfor<1, -1, -1>([&](auto CC) {
+            constexpr int c = decltype(CC)::value, x = 2 * u + c;
             const float va = iv[c], vb = iv[2 + c];
             const float d = __fsub_rn(vb, va);
             const float mn = fminf(va, vb);
             a2 = pushbit(d, a2);
-            const int q = qreg<J + 1>(mp, x);
-            nx[2 * x] = __fadd_rn(mn, mp.get(E1, q << 1));
-            nx[2 * x + 1] = __fadd_rn(mn, mp.get(E1, (q << 1) | 1));
-        }
-    }
-    word = INIT ? a2 : ((((ahi << 8) | alo) << 16) | a2);
+            nx[2 * x] = __fadd_rn(mn, errv<MP, J + 1, x, 0, 0, 1>(mp, E1));
+            nx[2 * x + 1] = __fadd_rn(mn, errv<MP, J + 1, x, 1, 0, 1>(mp, E1));
+        });
+    });
 #pragma unroll
     for (int r = 0; r < 32; r++) cur[r] = nx[r];
+    return (((ahi << 8) | alo) << 16) | a2;  // step-J decisions in the high half, step-(J+1) in the low half
 }
 
 // D2: pair (J, J+1); intermediates per parity class p, the output takes the class with the smaller metric (tie p=0).
 // Words: wi = step-J decisions (16 bits), wh = step-(J+1) decisions per class (p0 << 16 | p1), wc = class per output.
-template <int J, bool INIT, class MP, int EW>
+template <int J, class MP, int EW>
 __device__ __forceinline__ void pair_d2(const MP& mp, float (&cur)[32], const ERow<EW>& E0, const ERow<EW>& E1,
-                                        uint32_t& wi, uint32_t& wh, uint32_t& wc, bool okL, int ok_ra)
+                                        uint32_t& wi, uint32_t& wh, uint32_t& wc)
 {
     float nx[32];
     uint32_t alo = 0, ahi = 0, h0 = 0, h1 = 0, cc = 0;
-#pragma unroll
-    for (int u = 7; u >= 0; u--) {
+    cfor<7, -1, -1>([&](auto UU) {
+        constexpr int u = decltype(UU)::value;
         float iv[2][4];
-#pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-            const int ra = u + 8 * hh;
-            const int q = qreg<J>(mp, ra);
-            if (INIT) {
-                const bool ok = okL && (ok_ra < 0 || ok_ra == ra);
-#pragma unroll
-                for (int c = 0; c < 2; c++)
-#pragma unroll
-                    for (int p = 0; p < 2; p++) iv[p][2 * hh + c] = ok ? mp.get(E0, (((q << 1) | c) << 1) | p) : BIG;
-            } else {
-                const float va = cur[ra], vb = cur[ra + 16];
-                const float d = __fsub_rn(vb, va);
-                const float mn = fminf(va, vb);
-                if (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
-#pragma unroll
-                for (int c = 0; c < 2; c++)
-#pragma unroll
-                    for (int p = 0; p < 2; p++) iv[p][2 * hh + c] = __fadd_rn(mn, mp.get(E0, (((q << 1) | c) << 1) | p));
-            }
-        }
-#pragma unroll
-        for (int c = 1; c >= 0; c--) {
-            const int x = 2 * u + c;
-            const int q = qreg<J + 1>(mp, x);
+        cfor<0, 2, 1>([&](auto HH) {
+            constexpr int hh = decltype(HH)::value, ra = u + 8 * hh;
+            const float va = cur[ra], vb = cur[ra + 16];
+            const float d = __fsub_rn(vb, va);
+            const float mn = fminf(va, vb);
+            if constexpr (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
+            iv[0][2 * hh] = __fadd_rn(mn, errv<MP, J, ra, 0, 0, 2>(mp, E0));
+            iv[1][2 * hh] = __fadd_rn(mn, errv<MP, J, ra, 0, 1, 2>(mp, E0));
+            iv[0][2 * hh + 1] = __fadd_rn(mn, errv<MP, J, ra, 1, 0, 2>(mp, E0));
+            iv[1][2 * hh + 1] = __fadd_rn(mn, errv<MP, J, ra, 1, 1, 2>(mp, E0));
+        });
+        cfor<1, -1, -1>([&](auto CC) {
+            constexpr int c = decltype(CC)::value, x = 2 * u + c;
             float mnp[2];
-#pragma unroll
-            for (int p = 0; p < 2; p++) {
-                const float va = iv[p][c], vb = iv[p][2 + c];
-                const float d = __fsub_rn(vb, va);
-                mnp[p] = fminf(va, vb);
-                if (p) h1 = pushbit(d, h1); else h0 = pushbit(d, h0);
+            {
+                const float d0 = __fsub_rn(iv[0][2 + c], iv[0][c]);
+                mnp[0] = fminf(iv[0][c], iv[0][2 + c]);
+                h0 = pushbit(d0, h0);
+                const float d1 = __fsub_rn(iv[1][2 + c], iv[1][c]);
+                mnp[1] = fminf(iv[1][c], iv[1][2 + c]);
+                h1 = pushbit(d1, h1);
             }
-#pragma unroll
-            for (int c2 = 1; c2 >= 0; c2--) {
-                const int lb = (q << 1) | c2;
-                const float v0 = __fadd_rn(mnp[0], mp.get(E1, lb << 1));
-                const float v1 = __fadd_rn(mnp[1], mp.get(E1, (lb << 1) | 1));
+            cfor<1, -1, -1>([&](auto C2) {
+                constexpr int c2 = decltype(C2)::value;
+                const float v0 = __fadd_rn(mnp[0], errv<MP, J + 1, x, c2, 0, 2>(mp, E1));
+                const float v1 = __fadd_rn(mnp[1], errv<MP, J + 1, x, c2, 1, 2>(mp, E1));
                 cc = pushbit(__fsub_rn(v1, v0), cc);
                 nx[2 * x + c2] = fminf(v0, v1);
-            }
-        }
-    }
-    wi = INIT ? 0u : ((ahi << 8) | alo);
+            });
+        });
+    });
+    wi = (ahi << 8) | alo;
     wh = (h0 << 16) | h1;
     wc = cc;
 #pragma unroll
     for (int r = 0; r < 32; r++) cur[r] = nx[r];
 }
 
-// D4 / EQ phase A: steps (0, 1) of a group of 4.  Step 0 (or the tile start): intermediates per low bit b of the
-// first sample; step 1: outputs per class c = b0 ^ b1 (EQ: c = b0 = b1), best b per class (tie b = 0).
+// D4 / EQ phase A: steps (0, 1) of a group of 4.  Step 0: intermediates per low bit b of the first sample; step 1:
+// outputs per class c = b0 ^ b1 (EQ: c = b0 = b1), best b per class (tie b = 0).
 // Words: w0 = step-0 decisions, w1 = step-1 decisions per b (b0 << 16 | b1), w2 / w3 = chosen b of class 0 / 1.
-template <bool INIT, bool EQ, class MP, int EW>
+template <bool EQ, class MP, int EW>
 __device__ __forceinline__ void phase_a(const MP& mp, const float (&cur)[32], float (&o0)[32], float (&o1)[32],
-                                        const ERow<EW>& E0, const ERow<EW>& E1, uint32_t (&wd)[9], bool okL, int ok_ra)
+                                        const ERow<EW>& E0, const ERow<EW>& E1, uint32_t (&wd)[9])
 {
     uint32_t alo = 0, ahi = 0, hb0 = 0, hb1 = 0, bc0 = 0, bc1 = 0;
-#pragma unroll
-    for (int u = 7; u >= 0; u--) {
+    cfor<7, -1, -1>([&](auto UU) {
+        constexpr int u = decltype(UU)::value;
         float iv[2][4];
-#pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-            const int ra = u + 8 * hh;
-            const int q = qreg<0>(mp, ra);
-            if (INIT) {
-                const bool ok = okL && (ok_ra < 0 || ok_ra == ra);
-#pragma unroll
-                for (int c = 0; c < 2; c++)
-#pragma unroll
-                    for (int b = 0; b < 2; b++) iv[b][2 * hh + c] = ok ? mp.get(E0, (((q << 1) | c) << 1) | b) : BIG;
-            } else {
-                const float va = cur[ra], vb = cur[ra + 16];
-                const float d = __fsub_rn(vb, va);
-                const float mn = fminf(va, vb);
-                if (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
-#pragma unroll
-                for (int c = 0; c < 2; c++)
-#pragma unroll
-                    for (int b = 0; b < 2; b++) iv[b][2 * hh + c] = __fadd_rn(mn, mp.get(E0, (((q << 1) | c) << 1) | b));
-            }
-        }
-#pragma unroll
-        for (int c = 1; c >= 0; c--) {
-            const int x = 2 * u + c;
-            const int q = qreg<1>(mp, x);
+        cfor<0, 2, 1>([&](auto HH) {
+            constexpr int hh = decltype(HH)::value, ra = u + 8 * hh;
+            const float va = cur[ra], vb = cur[ra + 16];
+            const float d = __fsub_rn(vb, va);
+            const float mn = fminf(va, vb);
+            if constexpr (hh) ahi = pushbit(d, ahi); else alo = pushbit(d, alo);
+            iv[0][2 * hh] = __fadd_rn(mn, errv<MP, 0, ra, 0, 0, 2>(mp, E0));
+            iv[1][2 * hh] = __fadd_rn(mn, errv<MP, 0, ra, 0, 1, 2>(mp, E0));
+            iv[0][2 * hh + 1] = __fadd_rn(mn, errv<MP, 0, ra, 1, 0, 2>(mp, E0));
+            iv[1][2 * hh + 1] = __fadd_rn(mn, errv<MP, 0, ra, 1, 1, 2>(mp, E0));
+        });
+        cfor<1, -1, -1>([&](auto CC) {
+            constexpr int c = decltype(CC)::value, x = 2 * u + c;
             float mnb[2];
-#pragma unroll
-            for (int b = 0; b < 2; b++) {
-                const float va = iv[b][c], vb = iv[b][2 + c];
-                const float d = __fsub_rn(vb, va);
-                mnb[b] = fminf(va, vb);
-                if (b) hb1 = pushbit(d, hb1); else hb0 = pushbit(d, hb0);
+            {
+                const float d0 = __fsub_rn(iv[0][2 + c], iv[0][c]);
+                mnb[0] = fminf(iv[0][c], iv[0][2 + c]);
+                hb0 = pushbit(d0, hb0);
+                const float d1 = __fsub_rn(iv[1][2 + c], iv[1][c]);
+                mnb[1] = fminf(iv[1][c], iv[1][2 + c]);
+                hb1 = pushbit(d1, hb1);
             }
-#pragma unroll
-            for (int c2 = 1; c2 >= 0; c2--) {
-                const int lb = (q << 1) | c2;
-                if (EQ) {
-                    o0[2 * x + c2] = __fadd_rn(mnb[0], mp.get(E1, lb << 1));
-                    o1[2 * x + c2] = __fadd_rn(mnb[1], mp.get(E1, (lb << 1) | 1));
+            cfor<1, -1, -1>([&](auto C2) {
+                constexpr int c2 = decltype(C2)::value;
+                if constexpr (EQ) {
+                    o0[2 * x + c2] = __fadd_rn(mnb[0], errv<MP, 1, x, c2, 0, 2>(mp, E1));
+                    o1[2 * x + c2] = __fadd_rn(mnb[1], errv<MP, 1, x, c2, 1, 2>(mp, E1));
                     bc0 = bc0 << 1;
                     bc1 = (bc1 << 1) | 1u;
                 } else {
-#pragma unroll
-                    for (int cl = 0; cl < 2; cl++) {
-                        const float v0 = __fadd_rn(mnb[0], mp.get(E1, (lb << 1) | cl));        // b = 0: low bit 0 ^ cl
-                        const float v1 = __fadd_rn(mnb[1], mp.get(E1, (lb << 1) | (1 ^ cl)));  // b = 1
-                        const uint32_t dbit = __float_as_uint(__fsub_rn(v1, v0));
-                        if (cl) { bc1 = __funnelshift_l(dbit, bc1, 1); o1[2 * x + c2] = fminf(v0, v1); }
-                        else { bc0 = __funnelshift_l(dbit, bc0, 1); o0[2 * x + c2] = fminf(v0, v1); }
-                    }
+                    // class 0: b = 0 uses low bit 0, b = 1 low bit 1; class 1: b = 0 low bit 1, b = 1 low bit 0
+                    const float v00 = __fadd_rn(mnb[0], errv<MP, 1, x, c2, 0, 2>(mp, E1));
+                    const float v01 = __fadd_rn(mnb[1], errv<MP, 1, x, c2, 1, 2>(mp, E1));
+                    bc0 = pushbit(__fsub_rn(v01, v00), bc0);
+                    o0[2 * x + c2] = fminf(v00, v01);
+                    const float v10 = __fadd_rn(mnb[0], errv<MP, 1, x, c2, 1, 2>(mp, E1));
+                    const float v11 = __fadd_rn(mnb[1], errv<MP, 1, x, c2, 0, 2>(mp, E1));
+                    bc1 = pushbit(__fsub_rn(v11, v10), bc1);
+                    o1[2 * x + c2] = fminf(v10, v11);
                 }
-            }
-        }
-    }
-    wd[0] = INIT ? 0u : ((ahi << 8) | alo);
+            });
+        });
+    });
+    wd[0] = (ahi << 8) | alo;
     wd[1] = (hb0 << 16) | hb1;
     wd[2] = bc0;
     wd[3] = bc1;
@@ -395,56 +426,58 @@ template <bool EQ, class MP, int EW>
 __device__ __forceinline__ void phase_b(const MP& mp, const float (&o0)[32], const float (&o1)[32], float (&cur)[32],
                                         const ERow<EW>& E2, const ERow<EW>& E3, uint32_t (&wd)[9])
 {
-    uint32_t hlo[2] = {0, 0}, hhi[2] = {0, 0}, hbb[2][2] = {{0, 0}, {0, 0}}, S1 = 0, S2 = 0, S3 = 0;
-#pragma unroll
-    for (int u = 7; u >= 0; u--) {
-        float iv[2][2][4];
-#pragma unroll
-        for (int cl = 0; cl < 2; cl++) {
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                const int ra = u + 8 * hh;
-                const int q = qreg<2>(mp, ra);
+    uint32_t hlo0 = 0, hhi0 = 0, hlo1 = 0, hhi1 = 0, h00 = 0, h01 = 0, h10 = 0, h11 = 0, S1 = 0, S2 = 0, S3 = 0;
+    cfor<7, -1, -1>([&](auto UU) {
+        constexpr int u = decltype(UU)::value;
+        float iv[2][2][4];  // [class][low bit b][intermediate]
+        cfor<0, 2, 1>([&](auto CL) {
+            constexpr int cl = decltype(CL)::value;
+            cfor<0, 2, 1>([&](auto HH) {
+                constexpr int hh = decltype(HH)::value, ra = u + 8 * hh;
                 const float va = cl ? o1[ra] : o0[ra], vb = cl ? o1[ra + 16] : o0[ra + 16];
                 const float d = __fsub_rn(vb, va);
                 const float mn = fminf(va, vb);
-                if (hh) hhi[cl] = pushbit(d, hhi[cl]); else hlo[cl] = pushbit(d, hlo[cl]);
-#pragma unroll
-                for (int c = 0; c < 2; c++)
-#pragma unroll
-                    for (int b = 0; b < 2; b++)
-                        if (!EQ || b == cl)
-                            iv[cl][b][2 * hh + c] = __fadd_rn(mn, mp.get(E2, (((q << 1) | c) << 1) | b));
-            }
-        }
-#pragma unroll
-        for (int c = 1; c >= 0; c--) {
-            const int x = 2 * u + c;
-            const int q = qreg<3>(mp, x);
+                if constexpr (cl == 0) { if constexpr (hh) hhi0 = pushbit(d, hhi0); else hlo0 = pushbit(d, hlo0); }
+                else { if constexpr (hh) hhi1 = pushbit(d, hhi1); else hlo1 = pushbit(d, hlo1); }
+                cfor<0, 2, 1>([&](auto B) {
+                    constexpr int b = decltype(B)::value;
+                    if constexpr (!EQ || b == cl) {
+                        iv[cl][b][2 * hh] = __fadd_rn(mn, errv<MP, 2, ra, 0, b, 2>(mp, E2));
+                        iv[cl][b][2 * hh + 1] = __fadd_rn(mn, errv<MP, 2, ra, 1, b, 2>(mp, E2));
+                    }
+                });
+            });
+        });
+        cfor<1, -1, -1>([&](auto CC) {
+            constexpr int c = decltype(CC)::value, x = 2 * u + c;
             float mnx[2][2];
-#pragma unroll
-            for (int cl = 0; cl < 2; cl++)
-#pragma unroll
-                for (int b = 0; b < 2; b++) {
-                    if (EQ && b != cl) { hbb[cl][b] <<= 1; mnx[cl][b] = BIG; continue; }
-                    const float va = iv[cl][b][c], vb = iv[cl][b][2 + c];
-                    const float d = __fsub_rn(vb, va);
-                    mnx[cl][b] = fminf(va, vb);
-                    hbb[cl][b] = pushbit(d, hbb[cl][b]);
-                }
-#pragma unroll
-            for (int c2 = 1; c2 >= 0; c2--) {
-                const int lb = (q << 1) | c2;
-                if (EQ) {
-                    const float v0 = __fadd_rn(mnx[0][0], mp.get(E3, lb << 1));
-                    const float v1 = __fadd_rn(mnx[1][1], mp.get(E3, (lb << 1) | 1));
+            cfor<0, 2, 1>([&](auto CL) {
+                constexpr int cl = decltype(CL)::value;
+                cfor<0, 2, 1>([&](auto B) {
+                    constexpr int b = decltype(B)::value;
+                    uint32_t& hacc = cl ? (b ? h11 : h10) : (b ? h01 : h00);
+                    if constexpr (EQ && b != cl) {
+                        hacc <<= 1;
+                        mnx[cl][b] = BIG;
+                    } else {
+                        const float va = iv[cl][b][c], vb = iv[cl][b][2 + c];
+                        mnx[cl][b] = fminf(va, vb);
+                        hacc = pushbit(__fsub_rn(vb, va), hacc);
+                    }
+                });
+            });
+            cfor<1, -1, -1>([&](auto C2) {
+                constexpr int c2 = decltype(C2)::value;
+                if constexpr (EQ) {
+                    const float v0 = __fadd_rn(mnx[0][0], errv<MP, 3, x, c2, 0, 2>(mp, E3));
+                    const float v1 = __fadd_rn(mnx[1][1], errv<MP, 3, x, c2, 1, 2>(mp, E3));
                     S3 = pushbit(__fsub_rn(v1, v0), S3);
                     cur[2 * x + c2] = fminf(v0, v1);
                 } else {
-                    const float v00 = __fadd_rn(mnx[0][0], mp.get(E3, lb << 1));
-                    const float v01 = __fadd_rn(mnx[0][1], mp.get(E3, (lb << 1) | 1));
-                    const float v10 = __fadd_rn(mnx[1][0], mp.get(E3, (lb << 1) | 1));
-                    const float v11 = __fadd_rn(mnx[1][1], mp.get(E3, lb << 1));
+                    const float v00 = __fadd_rn(mnx[0][0], errv<MP, 3, x, c2, 0, 2>(mp, E3));
+                    const float v01 = __fadd_rn(mnx[0][1], errv<MP, 3, x, c2, 1, 2>(mp, E3));
+                    const float v10 = __fadd_rn(mnx[1][0], errv<MP, 3, x, c2, 1, 2>(mp, E3));
+                    const float v11 = __fadd_rn(mnx[1][1], errv<MP, 3, x, c2, 0, 2>(mp, E3));
                     float best = v00;
                     S1 = pushbit(__fsub_rn(v01, best), S1);
                     best = fminf(best, v01);
@@ -454,12 +487,12 @@ __device__ __forceinline__ void phase_b(const MP& mp, const float (&o0)[32], con
                     best = fminf(best, v11);
                     cur[2 * x + c2] = best;
                 }
-            }
-        }
-    }
-    wd[4] = (((hhi[0] << 8) | hlo[0]) << 16) | ((hhi[1] << 8) | hlo[1]);
-    wd[5] = (hbb[0][0] << 16) | (hbb[0][1] & 0xffffu);
-    wd[6] = (hbb[1][0] << 16) | (hbb[1][1] & 0xffffu);
+            });
+        });
+    });
+    wd[4] = (((hhi0 << 8) | hlo0) << 16) | ((hhi1 << 8) | hlo1);
+    wd[5] = (h00 << 16) | (h01 & 0xffffu);
+    wd[6] = (h10 << 16) | (h11 & 0xffffu);
     if (EQ) {
         wd[7] = S3;
         wd[8] = S3;
@@ -470,18 +503,43 @@ __device__ __forceinline__ void phase_b(const MP& mp, const float (&o0)[32], con
 }
 
 // ------------------------------------------------------------------------------------------------
-// the kernel
+// sub-block gain merge (src/cuda/tcq_viterbi.cu:185-201), in state space on the exchange regions of all G slots:
+// every state continues from its best slot (strict <, lowest slot wins); the winners are stored as bit planes of
+// state-indexed words (plane k, word s >> 5, bit s & 31).  Thread i of the CTA handles states i, i + 32 G, ...
+// Kept out of line: it runs once per sub-block and must not crowd the trellis loop out of the instruction cache.
 // ------------------------------------------------------------------------------------------------
+static __device__ __noinline__ void merge_slots(float* s_dp, int G, int NB, uint32_t* gw)
+{
+    const int tid = threadIdx.x, lane = tid & 31, nthr = 32 * G;
+    for (int s = tid; s < NS; s += nthr) {
+        const int a = swz(s);
+        float v = s_dp[a];
+        int bg = 0;
+        for (int gg = 1; gg < G; gg++) {
+            const float vv = s_dp[gg * NSP + a];
+            if (vv < v) { v = vv; bg = gg; }
+        }
+        for (int gg = 0; gg < G; gg++) s_dp[gg * NSP + a] = v;
+        for (int k = 0; k < NB; k++) {
+            const uint32_t w = __ballot_sync(0xffffffffu, (bg >> k) & 1);
+            if (lane == 0) gw[k * 32 + (s >> 5)] = w;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// forward kernel
 // SUB2: sub-block boundaries may fall in the middle of a 4-step group (sub = 2 mod 4; plain and D2 only).
+// ------------------------------------------------------------------------------------------------
 template <class MP, int MD, bool SUB2>
-__global__ void __launch_bounds__(256) vit_kernel(const VitParams p)
+__global__ void __launch_bounds__(256) vit_fwd_kernel(const VitParams p)
 {
     constexpr int NL = MP::NL, NP = MD ? 2 : 1, NV = NL / 2, EW = NL * NP;
     constexpr bool PP = MD == 1, G4 = MD >= 2, EQ = MD == 3;
     extern __shared__ __align__(16) unsigned char smem[];
     const int T = p.T, G = p.G, sub = p.sub, nsub = T / sub, U = p.U, U_hi = p.U_hi, mix = p.mix, Gf = p.Gfull;
     const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, g = tid >> 5, nthr = blockDim.x;
-    const SmemLayout SL = smem_layout(T, G, Gf, sub, NL, NP, U, U_hi, p.W4, p.NB);
+    const FwdSmem SL = fwd_smem(T, G, Gf, sub, NL, NP, U, U_hi);
     float* s_x = reinterpret_cast<float*>(smem + SL.x);
     float* s_w = reinterpret_cast<float*>(smem + SL.w);
     float* s_tab = reinterpret_cast<float*>(smem + SL.tab);
@@ -492,14 +550,8 @@ __global__ void __launch_bounds__(256) vit_kernel(const VitParams p)
     uint8_t* s_gc = smem + SL.gc;
     float* s_dp = reinterpret_cast<float*>(smem + SL.dp);
     float* s_err = reinterpret_cast<float*>(smem + SL.err);
-    uint32_t* s_tbw = reinterpret_cast<uint32_t*>(smem + SL.tbw);
-    uint32_t* s_tbg = reinterpret_cast<uint32_t*>(smem + SL.tbg);
-    uint16_t* s_st = reinterpret_cast<uint16_t*>(smem + SL.st);
-    uint8_t* s_sg = smem + SL.sg;
-    uint8_t* s_par = smem + SL.par;
     float* red_v = reinterpret_cast<float*>(smem + SL.red);
     int* red_i = reinterpret_cast<int*>(smem + SL.red + 4 * MAXG);
-    int* s_flag = reinterpret_cast<int*>(smem + SL.flag);
     const MP mp(p);
 
     // ---- tile inputs (sample t is element (t + rot) % ld), tables, gains ----
@@ -546,12 +598,10 @@ __global__ void __launch_bounds__(256) vit_kernel(const VitParams p)
     int PLj[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) PLj[j] = mp.hi((unsigned)((lane << j) & 511));
-    const int s0 = p.init_st ? p.init_st[n] : -1;
-    const bool okL = s0 < 0 || lane == (s0 & 31);
-    const int ok_ra = s0 < 0 ? -1 : ((s0 >> 5) & 15);
     const SvStream sv{p.svA + ((size_t)n * G + g) * (size_t)p.capA, p.svB + ((size_t)n * G + g) * (size_t)p.capB,
                       p.capA};
     float* myerr = s_err + (size_t)g * sub * NV * EW;
+    float* mydp = s_dp + (size_t)g * NSP;
 
     // branch-error table of sub-block sb for this warp's gain slot, NV label variants per step (src/cuda/tcq_viterbi.cu:202-213)
     auto build_err = [&](int sb) {
@@ -572,124 +622,104 @@ __global__ void __launch_bounds__(256) vit_kernel(const VitParams p)
         }
         __syncwarp();
     };
-    auto row = [&](int t, int j) -> const float* {
-        return myerr + ((size_t)(t % sub) * NV + PLj[j]) * EW;
-    };
-
-    float* mydp = s_dp + (size_t)g * NSP;
-    // metrics of layout jf -> shared -> layout jt; with merge: min over all G slots (strict <, lowest g), slot 0
-    // records the winner per state (src/cuda/tcq_viterbi.cu:185-201)
-    auto exchange = [&](float (&cur)[32], int jf, int jt, bool merge, int sb) {
+    // metrics of layout jf -> shared -> layout jt; with merge every state first takes the best of all G slots
+    auto exchange = [&](float (&cur)[32], auto JF, auto JT, bool merge, int sb) {
+        constexpr int jf = decltype(JF)::value, jt = decltype(JT)::value;
+        float* wp = mydp + xbase(jf, lane);
         __syncwarp();
-#pragma unroll
-        for (int r = 0; r < 32; r++) mydp[swz(state_of(jf, lane, r))] = cur[r];
-        if (!merge) {
+        cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; wp[xoff(jf, r)] = cur[r]; });
+        if (merge) {
+            __syncthreads();
+            merge_slots(s_dp, G, p.NB, p.gsw + ((size_t)n * nsub + sb) * p.NB * 32);
+            __syncthreads();
+        } else {
             __syncwarp();
-#pragma unroll
-            for (int r = 0; r < 32; r++) cur[r] = mydp[swz(state_of(jt, lane, r))];
-            return;
         }
-        __syncthreads();
-        uint32_t gw0 = 0, gw1 = 0, gw2 = 0, gw3 = 0;
-#pragma unroll
-        for (int r = 31; r >= 0; r--) {
-            const int a = swz(state_of(jt, lane, r));
-            float v = s_dp[a];
-            if (g == 0) {
-                int bg = 0;
-                for (int gg = 1; gg < G; gg++) {
-                    const float vv = s_dp[(size_t)gg * NSP + a];
-                    if (vv < v) { v = vv; bg = gg; }
-                }
-                gw0 = (gw0 << 1) | (uint32_t)(bg & 1);
-                gw1 = (gw1 << 1) | (uint32_t)((bg >> 1) & 1);
-                gw2 = (gw2 << 1) | (uint32_t)((bg >> 2) & 1);
-                gw3 = (gw3 << 1) | (uint32_t)((bg >> 3) & 1);
-            } else {
-                for (int gg = 1; gg < G; gg++) v = fminf(v, s_dp[(size_t)gg * NSP + a]);
-            }
-            cur[r] = v;
-        }
-        if (g == 0) {
-            uint32_t* gp = p.gsw + ((size_t)n * nsub + sb) * p.NB * 32 + lane;
-            gp[0] = gw0;
-            if (p.NB > 1) gp[32] = gw1;
-            if (p.NB > 2) { gp[64] = gw2; gp[96] = gw3; }
-        }
-        __syncthreads();
+        const float* rp = mydp + xbase(jt, lane);
+        cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; cur[r] = rp[xoff(jt, r)]; });
     };
 
-    // ---- forward ----
+    // ---- virtual step before the tile start, layout 0: metric 0 for predecessors of the start state's successors ----
     float cur[32];
-    for (int t4 = 0; t4 < T; t4 += 4) {
-        const long long kbase = (long long)(t4 >> 2) * p.W4 * 32 + lane;
-        uint32_t wd[9];
+    {
+        const int s0 = p.init_st ? p.init_st[n] : -1;
 #pragma unroll
-        for (int k = 0; k < 9; k++) wd[k] = 0;
-        // pair / phase A: steps t4, t4 + 1
+        for (int r = 0; r < 32; r++) {
+            const int s = state_of(0, lane, r);
+            cur[r] = (s0 < 0 || (s & 511) == (s0 & 511)) ? 0.f : BIG;
+        }
+    }
+
+    // ---- forward: groups of 4 steps, one exchange per group ----
+    int sb = 0, tt = 0;  // sub-block of the next step, its offset in the sub-block
+    long long kbase = lane;
+    auto row = [&](int off, int j) -> const float* { return myerr + ((size_t)(tt + off) * NV + PLj[j]) * EW; };
+    for (int t4 = 0; t4 < T; t4 += 4, kbase += (long long)p.W4 * 32) {
         if (t4 == 0) {
             build_err(0);
+        } else if (tt == sub) {  // sub-block boundary
+            sb++;
+            tt = 0;
+            exchange(cur, IC<4>{}, IC<0>{}, G > 1, sb);
+            build_err(sb);
         } else {
-            const bool bnd = (t4 % sub) == 0;
-            exchange(cur, 4, 0, bnd && G > 1, t4 / sub);
-            if (bnd) build_err(t4 / sub);
+            exchange(cur, IC<4>{}, IC<0>{}, false, sb);
         }
         ERow<EW> E0, E1;
-        load_row<MP>(E0, row(t4, 0));
-        load_row<MP>(E1, row(t4 + 1, 1));
-        float o0[G4 ? 32 : 1], o1[G4 ? 32 : 1];
-        if (!MD) {
-            if (t4 == 0) pair_plain<0, true>(mp, cur, E0, E1, wd[0], okL, ok_ra);
-            else pair_plain<0, false>(mp, cur, E0, E1, wd[0], okL, ok_ra);
-        } else if (PP) {
-            uint32_t wi;
-            if (t4 == 0) pair_d2<0, true>(mp, cur, E0, E1, wi, wd[1], wd[2], okL, ok_ra);
-            else pair_d2<0, false>(mp, cur, E0, E1, wi, wd[1], wd[2], okL, ok_ra);
-            wd[0] = wi << 16;  // step-0 decisions in the high half, step-2 decisions in the low half
-        } else {
-            if constexpr (G4) {
-                if (t4 == 0) phase_a<true, EQ>(mp, cur, o0, o1, E0, E1, wd, okL, ok_ra);
-                else phase_a<false, EQ>(mp, cur, o0, o1, E0, E1, wd, okL, ok_ra);
-            }
+        load_row<MP>(E0, row(0, 0));
+        load_row<MP>(E1, row(1, 1));
+        uint32_t wd[9];
+        if constexpr (MD == 0) {
+            wd[0] = pair_plain<0>(mp, cur, E0, E1);
+        } else if constexpr (PP) {
+            pair_d2<0>(mp, cur, E0, E1, wd[0], wd[1], wd[2]);
+            wd[0] <<= 16;  // step-0 decisions in the high half, step-2 decisions in the low half
         }
-        // pair / phase B: steps t4 + 2, t4 + 3
-        if (t4 + 2 < T) {
+        float o0[G4 ? 32 : 1], o1[G4 ? 32 : 1];
+        if constexpr (G4) phase_a<EQ>(mp, cur, o0, o1, E0, E1, wd);
+        tt += 2;
+        const bool full = t4 + 2 < T;
+        if (full) {
             if constexpr (SUB2 && !G4) {
-                if (((t4 + 2) % sub) == 0) {  // sub-block boundary inside the group
-                    if (G > 1) exchange(cur, 2, 2, true, (t4 + 2) / sub);
-                    build_err((t4 + 2) / sub);
+                if (tt == sub) {  // sub-block boundary inside the group
+                    sb++;
+                    tt = 0;
+                    if (G > 1) exchange(cur, IC<2>{}, IC<2>{}, true, sb);
+                    build_err(sb);
                 }
             }
             ERow<EW> E2, E3;
-            load_row<MP>(E2, row(t4 + 2, 2));
-            load_row<MP>(E3, row(t4 + 3, 3));
-            if (!MD) {
-                uint32_t w1;
-                pair_plain<2, false>(mp, cur, E2, E3, w1, okL, ok_ra);
-                wd[1] = w1;
-            } else if (PP) {
+            load_row<MP>(E2, row(0, 2));
+            load_row<MP>(E3, row(1, 3));
+            if constexpr (MD == 0) {
+                wd[1] = pair_plain<2>(mp, cur, E2, E3);
+            } else if constexpr (PP) {
                 uint32_t wi;
-                pair_d2<2, false>(mp, cur, E2, E3, wi, wd[3], wd[4], okL, ok_ra);
+                pair_d2<2>(mp, cur, E2, E3, wi, wd[3], wd[4]);
                 wd[0] |= wi;
             } else {
-                if constexpr (G4) phase_b<EQ>(mp, o0, o1, cur, E2, E3, wd);
+                phase_b<EQ>(mp, o0, o1, cur, E2, E3, wd);
             }
+            tt += 2;
         }
         // survivor words of this group (the last group of T = 2 mod 4 keeps only its first pair's words)
-        const int nw = (t4 + 2 < T) ? p.W4 : (MD == 0 ? 1 : 3);
-        if (!MD) {
+        if constexpr (MD == 0) {
             sv.put(kbase, wd[0]);
-            if (nw > 1) sv.put(kbase + 32, wd[1]);
+            if (full) sv.put(kbase + 32, wd[1]);
+        } else if constexpr (PP) {
+            sv.put(kbase, wd[0]);
+            sv.put(kbase + 32, wd[1]);
+            sv.put(kbase + 64, wd[2]);
+            if (full) { sv.put(kbase + 96, wd[3]); sv.put(kbase + 128, wd[4]); }
         } else {
 #pragma unroll
-            for (int k = 0; k < 9; k++)
-                if (k < nw) sv.put(kbase + 32 * k, wd[k]);
+            for (int k = 0; k < 9; k++) sv.put(kbase + 32 * k, wd[k]);
         }
     }
 
     // ---- final argmin over (slot, state), tail-biting keeps s == s0 (src/cuda/tcq_viterbi.cu:561-579) ----
     const int jend = ((T - 1) & 3) + 1;
-    const int s_end = p.tail ? s0 : -1;
+    const int s_end = (p.tail && p.init_st) ? p.init_st[n] : -1;
     float bv = BIG;
     int bi = 0x7fffffff;
 #pragma unroll
@@ -707,113 +737,138 @@ __global__ void __launch_bounds__(256) vit_kernel(const VitParams p)
     }
     if (lane == 0) { red_v[g] = bv; red_i[g] = bi; }
     __syncthreads();
+    if (tid == 0) {
+        for (int k = 1; k < G; k++)
+            if (red_v[k] < bv || (red_v[k] == bv && red_i[k] < bi)) { bv = red_v[k]; bi = red_i[k]; }
+        p.best[n] = bi;
+        if (p.end_st) p.end_st[n] = bi % NS;
+    }
+}
 
-    // ---- traceback (warp 0): one sub-block chunk at a time, chunk survivors staged in shared memory ----
-    if (g == 0) {
-        if (lane == 0) {
-            for (int k = 1; k < G; k++)
-                if (red_v[k] < bv || (red_v[k] == bv && red_i[k] < bi)) { bv = red_v[k]; bi = red_i[k]; }
-            p.best[n] = bi;
-            if (p.end_st) p.end_st[n] = bi % NS;
-            s_flag[0] = bi % NS;  // state
-            s_flag[1] = bi / NS;  // slot
-            s_flag[2] = 0;        // stopped at the first-pass middle
+// ------------------------------------------------------------------------------------------------
+// traceback, reconstruction and codes (src/cuda/tcq_viterbi.cu:580-682), one warp per tile
+// ------------------------------------------------------------------------------------------------
+template <int MD>
+__global__ void __launch_bounds__(32 * TB_WARPS) vit_tb_kernel(const VitParams p)
+{
+    constexpr bool PP = MD == 1, EQ = MD == 3;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int T = p.T, G = p.G, sub = p.sub, nsub = T / sub, U = p.U, U_hi = p.U_hi, mix = p.mix, NL = p.nl;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+    const int n = blockIdx.x * wpb + warp;
+    const TbSmem SL = tb_smem(T, sub, NL, U, U_hi, p.W4, p.NB, wpb);
+    float* s_tab = reinterpret_cast<float*>(smem + SL.tab);
+    float* s_tabhi = reinterpret_cast<float*>(smem + SL.tabhi);
+    float* s_gain = reinterpret_cast<float*>(smem + SL.gain);
+    float* s_gainhi = reinterpret_cast<float*>(smem + SL.gainhi);
+    unsigned char* wbase = smem + SL.warp + (size_t)warp * SL.per_warp;
+    uint32_t* s_tbw = reinterpret_cast<uint32_t*>(wbase + SL.tbw);
+    uint32_t* s_tbg = reinterpret_cast<uint32_t*>(wbase + SL.tbg);
+    uint16_t* s_st = reinterpret_cast<uint16_t*>(wbase + SL.st);
+    uint8_t* s_sg = wbase + SL.sg;
+    uint8_t* s_par = wbase + SL.par;
+    int* s_flag = reinterpret_cast<int*>(wbase + SL.flag);
+    for (int i = threadIdx.x; i < NL * U; i += blockDim.x) s_tab[i] = p.tab[i];
+    for (int i = threadIdx.x; i < NL * U_hi; i += blockDim.x) s_tabhi[i] = p.tab_hi[i];
+    if (threadIdx.x < p.Gfull) { s_gain[threadIdx.x] = p.gains[threadIdx.x]; s_gainhi[threadIdx.x] = p.gains_hi[threadIdx.x]; }
+    __syncthreads();
+    if (n >= p.N) return;
+
+    if (lane == 0) {
+        const int bi = p.best[n];
+        s_flag[0] = bi % NS;  // state
+        s_flag[1] = bi / NS;  // slot
+        s_flag[2] = 0;        // stopped at the first-pass middle
+    }
+    __syncwarp();
+    for (int lo = T - sub; lo >= 0; lo -= sub) {
+        const int gc = s_flag[1];
+        const int grp0 = lo >> 2, grp1 = (lo + sub - 1) >> 2;
+        const SvStream svg{p.svA + ((size_t)n * G + gc) * (size_t)p.capA, p.svB + ((size_t)n * G + gc) * (size_t)p.capB,
+                           p.capA};
+        for (int grp = grp0; grp <= grp1; grp++) {
+            const int nw = (grp * 4 + 2 < T) ? p.W4 : (MD == 0 ? 1 : 3);
+            for (int k = 0; k < nw; k++)
+                s_tbw[((grp - grp0) * p.W4 + k) * 32 + lane] = svg.get(((long long)grp * p.W4 + k) * 32 + lane);
         }
+        if (G > 1 && lo > 0)
+            for (int k = 0; k < p.NB; k++)
+                s_tbg[k * 32 + lane] = p.gsw[(((size_t)n * nsub + lo / sub) * p.NB + k) * 32 + lane];
         __syncwarp();
-        for (int lo = T - sub; lo >= 0; lo -= sub) {
-            const int gc = s_flag[1];
-            const int grp0 = lo >> 2, grp1 = (lo + sub - 1) >> 2;
-            const SvStream svg{p.svA + ((size_t)n * G + gc) * (size_t)p.capA,
-                               p.svB + ((size_t)n * G + gc) * (size_t)p.capB, p.capA};
-            for (int grp = grp0; grp <= grp1; grp++) {
-                const int nw = (grp * 4 + 2 < T) ? p.W4 : (MD == 0 ? 1 : 3);
-                for (int k = 0; k < nw; k++)
-                    s_tbw[((grp - grp0) * p.W4 + k) * 32 + lane] = svg.get(((long long)grp * p.W4 + k) * 32 + lane);
-            }
-            if (G > 1 && lo > 0)
-                for (int k = 0; k < p.NB; k++)
-                    s_tbg[k * 32 + lane] = p.gsw[(((size_t)n * nsub + lo / sub) * p.NB + k) * 32 + lane];
-            __syncwarp();
-            if (lane == 0) {
-                int st = s_flag[0], gs = s_flag[1], pcur = 0, cstar = 0;
-                bool stop = false;
-                for (int t = lo + sub - 1; t >= lo; t--) {
-                    s_st[t] = (uint16_t)st;
-                    s_sg[t] = (uint8_t)gs;
-                    const int j = t & 3;
-                    const int b9 = st >> 1;
-                    const int L = (b9 >> j) & 31;
-                    const int bi4 = bfly_of(j, b9);
-                    const uint32_t* W = s_tbw + ((t >> 2) - grp0) * p.W4 * 32 + L;  // word k of this group: W[32 k]
-                    if (PP && (t & 1)) {
-                        pcur = (W[32 * (j == 1 ? 2 : 4)] >> ((bi4 << 1) | (st & 1))) & 1;
-                        s_par[t] = s_par[t - 1] = (uint8_t)pcur;
-                    }
-                    if (p.mid_st && t == p.mid_t - 1) { p.mid_st[n] = st; stop = true; break; }
-                    if (t == 0) break;
-                    int h;
-                    if (!MD) {
-                        h = (W[32 * (j >> 1)] >> ((j & 1) ? bi4 : 16 + bi4)) & 1;
-                    } else if (PP) {
-                        if (j & 1) h = (W[32 * (j == 1 ? 1 : 3)] >> (pcur ? bi4 : 16 + bi4)) & 1;
-                        else h = (W[0] >> ((j == 0) ? 16 + bi4 : bi4)) & 1;
-                    } else {
-                        const int ro = (bi4 << 1) | (st & 1);  // output register of st at steps j = 1, 3
-                        if (j == 3) {
-                            cstar = (W[32 * 7] >> ro) & 1;
-                            const int bb = (W[32 * 8] >> ro) & 1;
-                            h = (W[32 * (5 + cstar)] >> (bb ? bi4 : 16 + bi4)) & 1;
-                            if (EQ) {
-                                s_par[t] = s_par[t - 1] = s_par[t - 2] = s_par[t - 3] = (uint8_t)cstar;
-                            } else {
-                                s_par[t] = (uint8_t)(bb ^ cstar);
-                                s_par[t - 1] = (uint8_t)bb;
-                            }
-                        } else if (j == 2) {
-                            h = (W[32 * 4] >> (cstar ? bi4 : 16 + bi4)) & 1;
-                        } else if (j == 1) {
-                            const int bb = (W[32 * (2 + cstar)] >> ro) & 1;
-                            h = (W[32 * 1] >> (bb ? bi4 : 16 + bi4)) & 1;
-                            if (!EQ) {
-                                s_par[t] = (uint8_t)(bb ^ cstar);
-                                s_par[t - 1] = (uint8_t)bb;
-                            }
+        if (lane == 0) {
+            int st = s_flag[0], gs = s_flag[1], pcur = 0, cstar = 0;
+            bool stop = false;
+            for (int t = lo + sub - 1; t >= lo; t--) {
+                s_st[t] = (uint16_t)st;
+                s_sg[t] = (uint8_t)gs;
+                const int j = t & 3;
+                const int b9 = st >> 1;
+                const int L = (b9 >> j) & 31;
+                const int bi4 = bfly_of(j, b9);
+                const uint32_t* W = s_tbw + ((t >> 2) - grp0) * p.W4 * 32 + L;  // word k of this group: W[32 k]
+                if (PP && (t & 1)) {
+                    pcur = (W[32 * (j == 1 ? 2 : 4)] >> ((bi4 << 1) | (st & 1))) & 1;
+                    s_par[t] = s_par[t - 1] = (uint8_t)pcur;
+                }
+                if (p.mid_st && t == p.mid_t - 1) { p.mid_st[n] = st; stop = true; break; }
+                if (t == 0) break;
+                int h;
+                if (MD == 0) {
+                    h = (W[32 * (j >> 1)] >> ((j & 1) ? bi4 : 16 + bi4)) & 1;
+                } else if (PP) {
+                    if (j & 1) h = (W[32 * (j == 1 ? 1 : 3)] >> (pcur ? bi4 : 16 + bi4)) & 1;
+                    else h = (W[0] >> ((j == 0) ? 16 + bi4 : bi4)) & 1;
+                } else {
+                    const int ro = (bi4 << 1) | (st & 1);  // output register of st at steps j = 1, 3
+                    if (j == 3) {
+                        cstar = (W[32 * 7] >> ro) & 1;
+                        const int bb = (W[32 * 8] >> ro) & 1;
+                        h = (W[32 * (5 + cstar)] >> (bb ? bi4 : 16 + bi4)) & 1;
+                        if (EQ) {
+                            s_par[t] = s_par[t - 1] = s_par[t - 2] = s_par[t - 3] = (uint8_t)cstar;
                         } else {
-                            h = (W[0] >> bi4) & 1;
+                            s_par[t] = (uint8_t)(bb ^ cstar);
+                            s_par[t - 1] = (uint8_t)bb;
                         }
-                    }
-                    st = (h << 9) | b9;
-                    if (G > 1 && t == lo) {  // sub-block boundary: slot of the previous sub-block
-                        const int jm = lo & 3;
-                        const int Lg = (st >> jm) & 31;
-                        const int rg = (st & ((1 << jm) - 1)) | ((st >> (jm + 5)) << jm);
-                        int v = 0;
-                        for (int k = 0; k < p.NB; k++) v |= (int)((s_tbg[k * 32 + Lg] >> rg) & 1u) << k;
-                        gs = v;
+                    } else if (j == 2) {
+                        h = (W[32 * 4] >> (cstar ? bi4 : 16 + bi4)) & 1;
+                    } else if (j == 1) {
+                        const int bb = (W[32 * (2 + cstar)] >> ro) & 1;
+                        h = (W[32 * 1] >> (bb ? bi4 : 16 + bi4)) & 1;
+                        if (!EQ) {
+                            s_par[t] = (uint8_t)(bb ^ cstar);
+                            s_par[t - 1] = (uint8_t)bb;
+                        }
+                    } else {
+                        h = (W[0] >> bi4) & 1;
                     }
                 }
-                s_flag[0] = st;
-                s_flag[1] = gs;
-                if (stop) s_flag[2] = 1;
+                st = (h << 9) | b9;
+                if (G > 1 && t == lo) {  // sub-block boundary: slot of the previous sub-block
+                    int v = 0;
+                    for (int k = 0; k < p.NB; k++) v |= (int)((s_tbg[k * 32 + (st >> 5)] >> (st & 31)) & 1u) << k;
+                    gs = v;
+                }
             }
-            __syncwarp();
-            if (s_flag[2]) break;
+            s_flag[0] = st;
+            s_flag[1] = gs;
+            if (stop) s_flag[2] = 1;
         }
+        __syncwarp();
+        if (s_flag[2]) return;  // first tail-biting pass: only the middle state was needed
     }
-    __syncthreads();
-    if (s_flag[2]) return;  // first tail-biting pass: only the middle state was needed
 
-    // ---- reconstruction and codes (src/cuda/tcq_viterbi.cu:662-682) ----
     float* rn = p.rec + (size_t)n * p.ld;
-    for (int t = tid; t < T; t += nthr) {
+    for (int t = lane; t < T; t += 32) {
         const int stt = s_st[t], gg = s_sg[t];
-        const int lb = (stt & 1) | (mp.hi((unsigned)(stt >> 1)) << 1);
+        const int lb = label_rt(stt, p);
         const bool hi = mix > 0 && ((t / mix) & 1);
         const int Ut = hi ? U_hi : U;
-        const int gi = p.cand ? (int)s_gc[(t / sub) * G + gg] : gg;
+        const int gi = p.cand ? (int)p.gcand[((size_t)n * nsub + t / sub) * G + gg] : gg;
         const float gt = hi ? s_gainhi[gi] : s_gain[gi];
         const float* tt = (hi ? s_tabhi : s_tab) + lb * Ut;
-        const float xt = s_x[t];
+        const int tp = (t + p.rot) % p.ld;
+        const float xt = p.x[(size_t)n * p.ld + tp];
         float bestd = BIG, val = 0.f;
         int bu = 0;
         for (int u = MD ? s_par[t] : 0; u < Ut; u += MD ? 2 : 1) {
@@ -822,7 +877,6 @@ __global__ void __launch_bounds__(256) vit_kernel(const VitParams p)
             const float dd = __fmul_rn(d, d);
             if (dd < bestd) { bestd = dd; val = v; bu = u; }
         }
-        const int tp = (t + p.rot) % p.ld;
         rn[tp] = val;
         if (p.code) p.code[(size_t)n * p.ld + tp] = (gi << 16) | (lb * Ut + bu);
     }

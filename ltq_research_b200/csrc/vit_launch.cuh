@@ -7,11 +7,11 @@ namespace ltqb {
 
 // Raise the kernel's dynamic shared-memory limit to the device maximum once per (kernel, device).  The limit is
 // always set to the same value, so concurrent callers on other host threads cannot lower it under a launch.
+// `done` is the caller's per-kernel flag array (one static array per kernel instantiation).
 template <class K>
-inline int ensure_smem(K kernel, int smem)
+inline int ensure_smem(K kernel, int smem, std::atomic<int>* done)
 {
     if (smem <= 48 * 1024) return 0;
-    static std::atomic<int> done[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
     if (done[dev].load(std::memory_order_acquire)) return 0;
@@ -28,8 +28,9 @@ inline int ensure_smem(K kernel, int smem)
 template <class MP, int MD, bool SUB2 = false>
 inline int launch_one(const VitParams& p, int smem, cudaStream_t st)
 {
-    auto k = vit_kernel<MP, MD, SUB2>;
-    if (ensure_smem(k, smem) != 0) return -1;
+    auto k = vit_fwd_kernel<MP, MD, SUB2>;
+    static std::atomic<int> done[64];
+    if (ensure_smem(k, smem, done) != 0) return -1;
     k<<<p.N, 32 * p.G, smem, st>>>(p);
     return 0;
 }
@@ -67,5 +68,6 @@ int launch_ct_m359_211_397(const VitParams& p, int md, int smem, cudaStream_t st
 int launch_ct_m359_40_475(const VitParams& p, int md, int smem, cudaStream_t st);   // 16
 int launch_rt(const VitParams& p, int md, int smem, cudaStream_t st);               // any masks, nl 4 / 8 / 16
 int launch_rt_sub2(const VitParams& p, int md, int smem, cudaStream_t st);          // any masks, sub = 2 mod 4
+int launch_tb(const VitParams& p, int md, cudaStream_t st);                          // traceback + reconstruction
 
 }  // namespace ltqb
