@@ -62,6 +62,23 @@ int ltq_viterbi_tb(const float* x, const float* w, int w_stride, const float* ta
                    int tb_passes, int tb_cand1, int tb_window, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/*
+ * Allocation-free tail-biting Viterbi.  No counterpart in the reference (the reference's Python wrapper allocates all
+ * scratch with torch); added for callers that cannot allocate device memory while they quantize — an engine that plans
+ * its device memory at start-up and forbids allocation afterwards, or a binding (cgo / JNI / N-API / ctypes) that only
+ * holds device pointers to its inputs and outputs.  Same arguments and results as ltq_viterbi_tb without the
+ * workspace: the scratch is a 64 MiB array inside the library's device memory (ltq_viterbi_tb_noalloc_capacity()),
+ * held on every GPU that loads the library until the process exits.  Returns -2 when
+ * ltq_viterbi_tb_workspace_bytes(...) exceeds that capacity.  Every call on a device shares the array: calls that
+ * overlap on the GPU race and must be serialised.  The first call on a device looks up the array's address (make it
+ * before any stream capture).  Calls no allocator.
+ */
+size_t ltq_viterbi_tb_noalloc_capacity(void);
+int ltq_viterbi_tb_noalloc(const float* x, const float* w, int w_stride, const float* tab, const float* gains,
+                           const float* tab_hi, const float* gains_hi, float* rec, int* code, int N, int T, int nu,
+                           int K, int m, const int* m_extra, int n_extra, int Gfull, int n_cand, int sub, int U_hi,
+                           int mix, int pp, int tb_passes, int tb_cand1, int tb_window, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,6 +25,9 @@ SIGNATURES = {
     "tcq_viterbi": (I, [P] * 15 + [I] * 18 + [P, I, P]),
     "ltq_viterbi_tb_workspace_bytes": (SZ, [I] * 8),
     "ltq_viterbi_tb": (I, [P, P, I, P, P, P, P, P, P] + [I] * 5 + [P] + [I] * 10 + [P, SZ, P]),
+    # allocation-free variant (scratch inside the library): same arguments without the workspace
+    "ltq_viterbi_tb_noalloc_capacity": (SZ, []),
+    "ltq_viterbi_tb_noalloc": (I, [P, P, I, P, P, P, P, P, P] + [I] * 5 + [P] + [I] * 10 + [P]),
 }
 
 
