@@ -88,7 +88,6 @@ extern "C" int tcq_viterbi(const float* x, const float* w, const float* tab, con
     const long long capA = (long long)T * 32;
     const long long capB = pp == 1 ? (long long)(T / 2) * 32 : (pp >= 2 ? (long long)(T / 4) * 9 * 32 : 0);
     if (sv_words(T, pp) > capA + capB) return -1;
-    if ((long long)gsel_planes(G) * 32 * 4 > 1024) return -1;
     VitParams p{};
     p.x = x; p.w = w; p.tab = tab; p.gains = gains; p.tab_hi = tab_hi ? tab_hi : tab; p.gains_hi = gains_hi ? gains_hi : gains;
     p.rec = rec; p.code = code; p.init_st = init_st; p.end_st = end_st; p.mid_st = mid_st; p.best = best; p.gcand = gcand;
@@ -97,7 +96,7 @@ extern "C" int tcq_viterbi(const float* x, const float* w, const float* tab, con
     p.mid_t = mid_t; p.tail = tail; p.N = N; p.T = T; p.U = U; p.G = G; p.Gfull = Gfull; p.sub = sub; p.U_hi = U_hi;
     p.mix = mix; p.ld = ld; p.ldw = ld; p.rot = rot; p.m = m; p.m2 = m2; p.m3 = m3; p.m4 = m4; p.nl = nl;
     p.cand = gcand != nullptr;
-    // gsel bytes per tile in the reference layout: (T / sub) * 1024; ours: (T / sub) * NB * 128 — fits
+    // gsel bytes per tile in the reference layout: (T / sub) * 1024; ours: (T / sub) * 512 — fits
     const int rc = run_pass(p, pp, (cudaStream_t)stream);
     if (rc != 0) return rc;
     return (int)cudaGetLastError();
@@ -113,7 +112,7 @@ extern "C" size_t ltq_viterbi_tb_workspace_bytes(int N, int T, int Gfull, int n_
     (void)tb_window;
     size_t b = 0;
     b += al256((size_t)N * Gm * (size_t)sv_words(T, pp) * 4);           // survivors
-    b += al256((size_t)N * (T / sub) * gsel_planes(Gm) * 32 * 4);        // gain-merge decisions
+    b += al256((size_t)N * (T / sub) * 512);                             // gain-merge winners
     b += al256((size_t)N * (T / sub) * Gm);                              // gain candidates
     b += al256((size_t)N * 4) * 2;                                       // middle state, best end
     return b;
@@ -145,7 +144,7 @@ extern "C" int ltq_viterbi_tb(const float* x, const float* w, int w_stride, cons
     uint32_t* sv = reinterpret_cast<uint32_t*>(ws);
     ws += al256((size_t)N * Gm * (size_t)sv_words(T, pp) * 4);
     uint32_t* gsw = reinterpret_cast<uint32_t*>(ws);
-    ws += al256((size_t)N * (T / sub) * gsel_planes(Gm) * 32 * 4);
+    ws += al256((size_t)N * (T / sub) * 512);
     uint8_t* gc = reinterpret_cast<uint8_t*>(ws);
     ws += al256((size_t)N * (T / sub) * Gm);
     int* mid = reinterpret_cast<int*>(ws);

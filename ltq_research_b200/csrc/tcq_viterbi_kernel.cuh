@@ -34,7 +34,7 @@ namespace ltqb {
 
 constexpr float BIG = 3.4e38f;  // the reference's "infinite" path metric (src/cuda/tcq_viterbi.cu:48, :227)
 constexpr int NS = 1024;        // trellis states (10-bit memory)
-constexpr int NSP = NS + NS / 32;  // exchange slots per gain slot (padded)
+constexpr int NSP = NS;         // exchange slots per gain slot
 constexpr int MAXG = 16, MAXU = 128, MAXSUBS = 32, MAXT = 512;
 constexpr int TB_WARPS = 8;     // tiles (warps) per traceback CTA
 
@@ -46,7 +46,7 @@ struct VitParams {
     int *end_st, *mid_st, *best;
     uint8_t* gcand;
     uint32_t *svA, *svB;   // survivor word stream: first capA words of each (tile, slot) in A, the rest in B
-    uint32_t* gsw;         // gain-merge winners: [N][T/sub][NB planes][32 words], bit s & 31 of word s >> 5
+    uint32_t* gsw;         // gain-merge winners: [N][T/sub][128 words], 4 bits per state: word s >> 3, nibble s & 7
     long long capA, capB;  // words per (tile, slot) in A / B
     int mid_t, tail;
     int N, T, U, G, Gfull, sub, U_hi, mix, ld, ldw, rot;
@@ -169,7 +169,7 @@ __host__ __device__ inline FwdSmem fwd_smem(int T, int G, int Gfull, int sub, in
     L.gainhi = o; o = al16(o + 4 * MAXG);
     L.ce = o; o = al16(o + 4 * (T / sub) * Gfull);
     L.gc = o; o = al16(o + (T / sub) * G);
-    L.dp = o; o = al16(o + 4 * NSP * G);
+    L.dp = o; o = al16(o + 4 * NSP * (G + 1));  // one region per slot + the merged region
     L.err = o; o = al16(o + 4 * G * sub * NV * EW);
     L.red = o; o = al16(o + 8 * MAXG);
     L.total = o;
@@ -191,7 +191,7 @@ __host__ __device__ inline TbSmem tb_smem(int T, int sub, int NL, int U, int U_h
     L.warp = o;
     int q = 0;  // per-warp region, relative offsets
     L.tbw = q; q = al16(q + 4 * 32 * W4 * ((sub + 3) / 4 + 1));
-    L.tbg = q; q = al16(q + 4 * 32 * NB);
+    L.tbg = q; q = al16(q + 4 * (NS / 8));
     L.st = q; q = al16(q + 2 * T);
     L.sg = q; q = al16(q + T);
     L.par = q; q = al16(q + T);
@@ -206,11 +206,10 @@ __host__ __device__ __forceinline__ int state_of(int j, int L, int r)
 {
     return (r & ((1 << j) - 1)) | (L << j) | ((r >> j) << (j + 5));
 }
-// exchange slot of state s: one pad word per 32 states.  For every layout j the slot of register r of lane L is a
-// per-lane base (L << j) + (L >> (5 - j)) plus a per-register constant, and the 32 lanes of a warp hit 32 distinct banks.
-__device__ __forceinline__ int swz(int s) { return s + (s >> 5); }
-__device__ __forceinline__ int xbase(int j, int L) { return (L << j) + (L >> (5 - j)); }
-__host__ __device__ constexpr int xoff(int j, int r) { return (r & ((1 << j) - 1)) + (r >> j) * (33 << j); }
+// exchange slot of state s: chunks of 4 consecutive states (16 bytes); chunk c = s >> 2 is stored at c ^ ((c >> 3) & 3).
+// Reads of layout 0 (lane L, register r: state L + 32 r) hit 32 distinct banks; writes of layout 4 (lane L holds the
+// chunks 4L .. 4L + 3 and 128 + 4L .. 128 + 4L + 3) are 16-byte stores whose quarter-warp phases hit distinct banks.
+__host__ __device__ constexpr int swz(int s) { return ((((s >> 2) ^ ((s >> 5) & 3))) << 2) | (s & 3); }
 
 // register index ra (0..15) of the butterfly whose outputs have (s >> 1) == b9, in layout j; lane = (b9 >> j) & 31
 __device__ __forceinline__ int bfly_of(int j, int b9) { return (b9 & ((1 << j) - 1)) | ((b9 >> (j + 5)) << j); }
@@ -503,36 +502,82 @@ __device__ __forceinline__ void phase_b(const MP& mp, const float (&o0)[32], con
 }
 
 // ------------------------------------------------------------------------------------------------
-// sub-block gain merge (src/cuda/tcq_viterbi.cu:185-201), in state space on the exchange regions of all G slots:
-// every state continues from its best slot (strict <, lowest slot wins); the winners are stored as bit planes of
-// state-indexed words (plane k, word s >> 5, bit s & 31).  Thread i of the CTA handles states i, i + 32 G, ...
-// Kept out of line: it runs once per sub-block and must not crowd the trellis loop out of the instruction cache.
+// sub-block gain merge (src/cuda/tcq_viterbi.cu:185-201), in state space over the exchange regions of all G slots:
+// every state continues from its best slot (strict <, lowest slot wins).  The merged metrics go to one region that
+// every slot reads next; the winners are 4-bit codes, 8 states per word (word s >> 3, nibble s & 7).  Thread i of the
+// CTA handles states 8i .. 8i + 7 (two 16-byte chunks per region).  Kept out of line: it runs once per sub-block.
 // ------------------------------------------------------------------------------------------------
-static __device__ __noinline__ void merge_slots(float* s_dp, int G, int NB, uint32_t* gw)
+template <int G>
+static __device__ __noinline__ void merge_slots(const float* s_dp, float* s_mg, uint32_t* gw)
 {
-    const int tid = threadIdx.x, lane = tid & 31, nthr = 32 * G;
-    for (int s = tid; s < NS; s += nthr) {
-        const int a = swz(s);
-        float v = s_dp[a];
-        int bg = 0;
+    for (int i = threadIdx.x; i < NS / 8; i += 32 * G) {
+        const int a0 = swz(8 * i), a1 = swz(8 * i + 4);
+        float v[8];
+        uint32_t code = 0;
+        {
+            const float4 x0 = *reinterpret_cast<const float4*>(s_dp + a0);
+            const float4 x1 = *reinterpret_cast<const float4*>(s_dp + a1);
+            v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w; v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+        }
+#pragma unroll
         for (int gg = 1; gg < G; gg++) {
-            const float vv = s_dp[gg * NSP + a];
-            if (vv < v) { v = vv; bg = gg; }
+            const float4 x0 = *reinterpret_cast<const float4*>(s_dp + gg * NSP + a0);
+            const float4 x1 = *reinterpret_cast<const float4*>(s_dp + gg * NSP + a1);
+            const float w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (w[k] < v[k]) { v[k] = w[k]; code = (code & ~(15u << (4 * k))) | ((uint32_t)gg << (4 * k)); }
         }
-        for (int gg = 0; gg < G; gg++) s_dp[gg * NSP + a] = v;
-        for (int k = 0; k < NB; k++) {
-            const uint32_t w = __ballot_sync(0xffffffffu, (bg >> k) & 1);
-            if (lane == 0) gw[k * 32 + (s >> 5)] = w;
-        }
+        *reinterpret_cast<float4*>(s_mg + a0) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(s_mg + a1) = make_float4(v[4], v[5], v[6], v[7]);
+        gw[i] = code;
     }
+}
+
+static __device__ __forceinline__ void merge_any(int G, const float* s_dp, float* s_mg, uint32_t* gw)
+{
+    switch (G) {
+        case 2: merge_slots<2>(s_dp, s_mg, gw); break;
+        case 3: merge_slots<3>(s_dp, s_mg, gw); break;
+        case 4: merge_slots<4>(s_dp, s_mg, gw); break;
+        case 8: merge_slots<8>(s_dp, s_mg, gw); break;
+        default: break;
+    }
+}
+
+// branch-error table of one sub-block for one gain slot (src/cuda/tcq_viterbi.cu:202-213): for each step, label and
+// parity class, w * min_u (x - g tab[u])^2, written in the NV label variants err'[P][v] = err[v ^ (P << 1)]
+template <int NL, int NP, bool MD>
+static __device__ __noinline__ void build_err(float* myerr, const float* s_x, const float* s_w, const float* s_tab,
+                                              const float* s_tabhi, float gain, float gainhi, int t0, int sub, int U,
+                                              int U_hi, int mix, int lane)
+{
+    constexpr int NV = NL / 2, EW = NL * NP;
+    __syncwarp();
+    for (int it = lane; it < sub * NL * NP; it += 32) {
+        const int tt = it / (NL * NP), lb = (it / NP) % NL, pc = it % NP;
+        const int t = t0 + tt;
+        const bool hi = !MD && mix > 0 && ((t / mix) & 1);
+        const float x = s_x[t];
+        float e;
+        if (MD) e = branch_err(x, gain, s_tab + lb * U, pc, 2, U);
+        else if (hi) e = branch_err(x, gainhi, s_tabhi + lb * U_hi, 0, 1, U_hi);
+        else e = branch_err(x, gain, s_tab + lb * U, 0, 1, U);
+        e = __fmul_rn(e, s_w[t]);
+        float* dst = myerr + (size_t)tt * NV * EW + pc;
+#pragma unroll
+        for (int P = 0; P < NV; P++) dst[P * EW + (lb ^ (P << 1)) * NP] = e;
+    }
+    __syncwarp();
 }
 
 // ------------------------------------------------------------------------------------------------
 // forward kernel
 // SUB2: sub-block boundaries may fall in the middle of a 4-step group (sub = 2 mod 4; plain and D2 only).
 // ------------------------------------------------------------------------------------------------
+// Plain mode is capped at 85 registers (3 x 256 threads per SM) so that 6 four-slot tiles fit per SM.
 template <class MP, int MD, bool SUB2>
-__global__ void __launch_bounds__(256) vit_fwd_kernel(const VitParams p)
+__global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const VitParams p)
 {
     constexpr int NL = MP::NL, NP = MD ? 2 : 1, NV = NL / 2, EW = NL * NP;
     constexpr bool PP = MD == 1, G4 = MD >= 2, EQ = MD == 3;
@@ -602,69 +647,66 @@ __global__ void __launch_bounds__(256) vit_fwd_kernel(const VitParams p)
                       p.capA};
     float* myerr = s_err + (size_t)g * sub * NV * EW;
     float* mydp = s_dp + (size_t)g * NSP;
-
-    // branch-error table of sub-block sb for this warp's gain slot, NV label variants per step (src/cuda/tcq_viterbi.cu:202-213)
-    auto build_err = [&](int sb) {
-        const int t0 = sb * sub;
+    float* s_mg = s_dp + (size_t)G * NSP;  // merged metrics after a sub-block boundary
+    auto build = [&](int sb) {
         const int gi = p.cand ? (int)s_gc[sb * G + g] : g;
-        __syncwarp();
-        for (int it = lane; it < sub * NL * NP; it += 32) {
-            const int tt = it / (NL * NP), lb = (it / NP) % NL, pc = it % NP;
-            const int t = t0 + tt;
-            const bool hi = mix > 0 && ((t / mix) & 1);
-            float e;
-            if (MD) e = branch_err(s_x[t], s_gain[gi], s_tab + lb * U, pc, 2, U);
-            else if (hi) e = branch_err(s_x[t], s_gainhi[gi], s_tabhi + lb * U_hi, 0, 1, U_hi);
-            else e = branch_err(s_x[t], s_gain[gi], s_tab + lb * U, 0, 1, U);
-            e = __fmul_rn(e, s_w[t]);
-#pragma unroll
-            for (int P = 0; P < NV; P++) myerr[((size_t)tt * NV + P) * EW + ((lb ^ (P << 1)) * NP + pc)] = e;
-        }
-        __syncwarp();
+        build_err<NL, NP, MD != 0>(myerr, s_x, s_w, s_tab, s_tabhi, s_gain[gi], s_gainhi[gi], sb * sub, sub, U, U_hi, mix,
+                                   lane);
     };
-    // metrics of layout jf -> shared -> layout jt; with merge every state first takes the best of all G slots
-    auto exchange = [&](float (&cur)[32], auto JF, auto JT, bool merge, int sb) {
+    // per-lane exchange addresses: layout-0 reads (4 bases, by r & 3) and layout-4 chunk writes (4 bases, by chunk)
+    int rbase[4], wbase[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        rbase[q] = 4 * ((lane >> 2) ^ q) + (lane & 3);
+        wbase[q] = 16 * lane + 4 * (q ^ ((lane >> 1) & 3));
+    }
+    auto read0 = [&](float (&cur)[32], const float* src) {
+        cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; cur[r] = src[rbase[r & 3] + 32 * r]; });
+    };
+    auto write4 = [&](const float (&cur)[32], float* dst) {
+        cfor<0, 8, 1>([&](auto K) {
+            constexpr int k = decltype(K)::value, r = 4 * k;
+            *reinterpret_cast<float4*>(dst + wbase[k & 3] + (k >> 2) * 512) =
+                make_float4(cur[r], cur[r + 1], cur[r + 2], cur[r + 3]);
+        });
+    };
+    // generic scalar exchange (sub-blocks that end in the middle of a group): layout jf -> layout jt through the
+    // regions, with the gain merge
+    auto exchange_merge = [&](float (&cur)[32], auto JF, auto JT, int sb) {
         constexpr int jf = decltype(JF)::value, jt = decltype(JT)::value;
-        float* wp = mydp + xbase(jf, lane);
         __syncwarp();
-        cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; wp[xoff(jf, r)] = cur[r]; });
-        if (merge) {
-            __syncthreads();
-            merge_slots(s_dp, G, p.NB, p.gsw + ((size_t)n * nsub + sb) * p.NB * 32);
-            __syncthreads();
-        } else {
-            __syncwarp();
-        }
-        const float* rp = mydp + xbase(jt, lane);
-        cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; cur[r] = rp[xoff(jt, r)]; });
+        cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; mydp[swz(state_of(jf, lane, r))] = cur[r]; });
+        __syncthreads();
+        merge_any(G, s_dp, s_mg, p.gsw + ((size_t)n * nsub + sb) * (NS / 8));
+        __syncthreads();
+        cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; cur[r] = s_mg[swz(state_of(jt, lane, r))]; });
     };
 
-    // ---- virtual step before the tile start, layout 0: metric 0 for predecessors of the start state's successors ----
-    float cur[32];
+    // ---- virtual step before the tile start, layout 0: metric 0 for predecessors of the start state's successors,
+    // written to this slot's exchange region; every group of 4 steps reads its metrics from a region (layout 0) and
+    // writes them back (layout 4), so no path metric stays in registers across groups ----
     {
         const int s0 = p.init_st ? p.init_st[n] : -1;
-#pragma unroll
-        for (int r = 0; r < 32; r++) {
-            const int s = state_of(0, lane, r);
-            cur[r] = (s0 < 0 || (s & 511) == (s0 & 511)) ? 0.f : BIG;
-        }
+        cfor<0, 32, 1>([&](auto R) {
+            constexpr int r = decltype(R)::value;
+            const int st = state_of(0, lane, r);
+            mydp[rbase[r & 3] + 32 * r] = (s0 < 0 || (st & 511) == (s0 & 511)) ? 0.f : BIG;
+        });
     }
+    build(0);
 
-    // ---- forward: groups of 4 steps, one exchange per group ----
+    // ---- forward: groups of 4 steps ----
     int sb = 0, tt = 0;  // sub-block of the next step, its offset in the sub-block
-    long long kbase = lane;
     auto row = [&](int off, int j) -> const float* { return myerr + ((size_t)(tt + off) * NV + PLj[j]) * EW; };
-    for (int t4 = 0; t4 < T; t4 += 4, kbase += (long long)p.W4 * 32) {
-        if (t4 == 0) {
-            build_err(0);
-        } else if (tt == sub) {  // sub-block boundary
-            sb++;
-            tt = 0;
-            exchange(cur, IC<4>{}, IC<0>{}, G > 1, sb);
-            build_err(sb);
-        } else {
-            exchange(cur, IC<4>{}, IC<0>{}, false, sb);
-        }
+    const float* src = mydp;
+    // survivor words: groups that fit entirely in region A are stored through a plain pointer
+    const long long gw4 = (long long)p.W4 * 32;
+    const int ngA = (int)(p.capA / gw4 < (1 << 30) ? p.capA / gw4 : (1 << 30));
+    uint32_t* svp = sv.a + lane;
+    float cur[32];
+    for (int t4 = 0, grp = 0;; t4 += 4, grp++, svp += gw4) {
+        __syncwarp();
+        read0(cur, src);
         ERow<EW> E0, E1;
         load_row<MP>(E0, row(0, 0));
         load_row<MP>(E1, row(1, 1));
@@ -684,8 +726,8 @@ __global__ void __launch_bounds__(256) vit_fwd_kernel(const VitParams p)
                 if (tt == sub) {  // sub-block boundary inside the group
                     sb++;
                     tt = 0;
-                    if (G > 1) exchange(cur, IC<2>{}, IC<2>{}, true, sb);
-                    build_err(sb);
+                    if (G > 1) exchange_merge(cur, IC<2>{}, IC<2>{}, sb);
+                    build(sb);
                 }
             }
             ERow<EW> E2, E3;
@@ -703,17 +745,32 @@ __global__ void __launch_bounds__(256) vit_fwd_kernel(const VitParams p)
             tt += 2;
         }
         // survivor words of this group (the last group of T = 2 mod 4 keeps only its first pair's words)
-        if constexpr (MD == 0) {
-            sv.put(kbase, wd[0]);
-            if (full) sv.put(kbase + 32, wd[1]);
-        } else if constexpr (PP) {
-            sv.put(kbase, wd[0]);
-            sv.put(kbase + 32, wd[1]);
-            sv.put(kbase + 64, wd[2]);
-            if (full) { sv.put(kbase + 96, wd[3]); sv.put(kbase + 128, wd[4]); }
-        } else {
+        const int nw = full ? p.W4 : (MD == 0 ? 1 : 3);
+        if (grp < ngA) {
 #pragma unroll
-            for (int k = 0; k < 9; k++) sv.put(kbase + 32 * k, wd[k]);
+            for (int k = 0; k < (MD == 0 ? 2 : (PP ? 5 : 9)); k++)
+                if (k < nw) svp[32 * k] = wd[k];
+        } else {
+            const long long kb = (long long)grp * gw4 + lane;
+#pragma unroll
+            for (int k = 0; k < (MD == 0 ? 2 : (PP ? 5 : 9)); k++)
+                if (k < nw) sv.put(kb + 32 * k, wd[k]);
+        }
+        if (t4 + 4 >= T) break;  // the last group's metrics stay in registers for the argmin
+        // metrics (layout 4) back to this slot's region; at a sub-block boundary all slots merge first
+        __syncwarp();
+        write4(cur, mydp);
+        src = mydp;
+        if (tt == sub) {
+            sb++;
+            tt = 0;
+            if (G > 1) {
+                __syncthreads();
+                merge_any(G, s_dp, s_mg, p.gsw + ((size_t)n * nsub + sb) * (NS / 8));
+                __syncthreads();
+                src = s_mg;
+            }
+            build(sb);
         }
     }
 
@@ -792,8 +849,7 @@ __global__ void __launch_bounds__(32 * TB_WARPS) vit_tb_kernel(const VitParams p
                 s_tbw[((grp - grp0) * p.W4 + k) * 32 + lane] = svg.get(((long long)grp * p.W4 + k) * 32 + lane);
         }
         if (G > 1 && lo > 0)
-            for (int k = 0; k < p.NB; k++)
-                s_tbg[k * 32 + lane] = p.gsw[(((size_t)n * nsub + lo / sub) * p.NB + k) * 32 + lane];
+            for (int k = lane; k < NS / 8; k += 32) s_tbg[k] = p.gsw[((size_t)n * nsub + lo / sub) * (NS / 8) + k];
         __syncwarp();
         if (lane == 0) {
             int st = s_flag[0], gs = s_flag[1], pcur = 0, cstar = 0;
@@ -845,9 +901,7 @@ __global__ void __launch_bounds__(32 * TB_WARPS) vit_tb_kernel(const VitParams p
                 }
                 st = (h << 9) | b9;
                 if (G > 1 && t == lo) {  // sub-block boundary: slot of the previous sub-block
-                    int v = 0;
-                    for (int k = 0; k < p.NB; k++) v |= (int)((s_tbg[k * 32 + (st >> 5)] >> (st & 31)) & 1u) << k;
-                    gs = v;
+                    gs = (int)((s_tbg[st >> 3] >> (4 * (st & 7))) & 15u);
                 }
             }
             s_flag[0] = st;

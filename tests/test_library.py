@@ -61,7 +61,7 @@ def test_workspace_size():
     b = L.ltq_viterbi_tb_workspace_bytes(65536, 256, 4, 0, 16, 0, 0, 0)
     # survivors: 64 groups x 2 words x 32 lanes x 4 B per slot -> 16 KiB per slot, 4 slots
     assert b >= 65536 * 4 * 16384
-    assert b < 65536 * 4 * 16384 * 1.1
+    assert b < 65536 * 4 * 16384 * 1.15  # + gain-merge winners: 16 boundaries x 512 B per tile
     assert L.ltq_viterbi_tb_workspace_bytes(0, 256, 4, 0, 16, 0, 0, 0) == 0
 
 
