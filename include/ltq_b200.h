@@ -63,6 +63,31 @@ int ltq_viterbi_tb(const float* x, const float* w, int w_stride, const float* ta
                    void* stream);
 
 /*
+ * Matrix-level kernels of the quantizer path (src/liqk_v2.py).  No single C entry in the reference: each replaces a
+ * few torch operations of the function cited.  Device pointers, row strides in elements, asynchronous on `stream`.
+ *
+ * ltq_fwht256: normalized block FWHT-256 along rows, out[r, :] = H256(x[r, :]) / 16 per 256-column block, with
+ *   x = in (mode 0), in / scale[col] (mode 1, as W / suh), in * scale[col] (mode 2, as H * suh); `in` is fp32 or
+ *   (in_bf16 = 1) bf16.  Replaces fwht_inplace (src/iqk_format.py:153-170) in compute_optimal_suh
+ *   (src/liqk_v2.py:436-440) and _fwht_rows (:1024-1026); same butterfly order, bit-identical results.
+ * ltq_scale_fit: per-(row, 256-block) scale of the row-scale formats (src/liqk_v2.py:938-946): fp16 d_row (bits in
+ *   d_row_h, value in d_row), 5-bit exponent e and d_rb = d_row * 2^(e_step * e).  Any output may be NULL.
+ * ltq_ldlq_gather: Viterbi input tiles of one 16-column sub-block, x[n][16 r + c] = w[16 n + r][c] * inv_d[16 n + r]
+ *   (src/liqk_v2.py:914, :963).
+ * ltq_ldlq_feedback: after the sub-block at columns [s0, s0 + 16) of a 256-column block (src/liqk_v2.py:964-971):
+ *   G[:, s0:s0+16] = rec (tile layout [M/16][256]); with code, idx = label * U + u and gi = gain index;
+ *   w[:, s0+16:256] -= ((w[:, s0:s0+16] - d_rb * rec) @ Uinv[s0:s0+16, s0:s0+16]) @ U[s0:s0+16, s0+16:256].
+ */
+int ltq_fwht256(const void* in, int in_bf16, long long ld_in, float* out, long long ld_out, const float* scale, int mode,
+                int rows, int cols, void* stream);
+int ltq_scale_fit(const float* W, long long ld, int M, int K, float scale, float e_step, int e_bits, uint16_t* d_row_h,
+                  float* d_row, int8_t* e, float* d_rb, void* stream);
+int ltq_ldlq_gather(const float* w, long long ld, const float* inv_d, int M, float* x, void* stream);
+int ltq_ldlq_feedback(float* w, long long ld, int M, int s0, const float* d_rb, const float* rec, const int* code,
+                      const float* U, long long ldU, const float* Uinv, long long ldUi, float* G, long long ldG,
+                      int16_t* idx, uint8_t* gi, long long ldP, void* stream);
+
+/*
  * Allocation-free tail-biting Viterbi.  No counterpart in the reference (the reference's Python wrapper allocates all
  * scratch with torch); added for callers that cannot allocate device memory while they quantize — an engine that plans
  * its device memory at start-up and forbids allocation afterwards, or a binding (cgo / JNI / N-API / ctypes) that only

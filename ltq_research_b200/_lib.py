@@ -25,6 +25,12 @@ SIGNATURES = {
     "tcq_viterbi": (I, [P] * 15 + [I] * 18 + [P, I, P]),
     "ltq_viterbi_tb_workspace_bytes": (SZ, [I] * 8),
     "ltq_viterbi_tb": (I, [P, P, I, P, P, P, P, P, P] + [I] * 5 + [P] + [I] * 10 + [P, SZ, P]),
+    # matrix-level kernels
+    "ltq_fwht256": (I, [P, I, ctypes.c_longlong, P, ctypes.c_longlong, P, I, I, I, P]),
+    "ltq_scale_fit": (I, [P, ctypes.c_longlong, I, I, ctypes.c_float, ctypes.c_float, I, P, P, P, P, P]),
+    "ltq_ldlq_gather": (I, [P, ctypes.c_longlong, P, I, P, P]),
+    "ltq_ldlq_feedback": (I, [P, ctypes.c_longlong, I, I, P, P, P, P, ctypes.c_longlong, P, ctypes.c_longlong, P,
+                              ctypes.c_longlong, P, P, ctypes.c_longlong, P]),
     # allocation-free variant (scratch inside the library): same arguments without the workspace
     "ltq_viterbi_tb_noalloc_capacity": (SZ, []),
     "ltq_viterbi_tb_noalloc": (I, [P, P, I, P, P, P, P, P, P] + [I] * 5 + [P] + [I] * 10 + [P]),

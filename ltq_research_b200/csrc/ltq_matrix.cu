@@ -1,0 +1,241 @@
+// Matrix-level kernels of the LTQ quantizer path around the Viterbi (lumen-inference/ltq-research src/liqk_v2.py):
+//   * ltq_fwht256       — normalized block FWHT-256 along rows with an optional column scale (src/iqk_format.py:153-170,
+//                         used by compute_optimal_suh src/liqk_v2.py:409-441 and _fwht_rows :1024-1026);
+//   * ltq_scale_fit     — per-(row, 256-block) scale: fp16 d_row and 5-bit exponent (src/liqk_v2.py:938-946);
+//   * ltq_ldlq_gather   — the Viterbi input tiles of one 16-column sub-block (src/liqk_v2.py:913-916, :960-963);
+//   * ltq_ldlq_feedback — the intra-block LDLQ error feedback after a sub-block (src/liqk_v2.py:964-971).
+// All are memory-bound SIMT kernels: one warp per row or per (row, block), coalesced 16-byte accesses.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "ltq_b200.h"
+
+namespace {
+
+// ------------------------------------------------------------------------------------------------
+// FWHT-256: one warp per (row, 256-block); lane L holds elements 8L .. 8L + 7.  Stages h = 1, 2, 4 pair elements of one
+// lane; stages h = 8 .. 128 pair lane L with lane L ^ (h / 8).  At every stage the lower element of a pair becomes
+// a + b and the upper a - b (a = lower, b = upper), exactly the order of the reference's butterfly, then one multiply
+// by 256^-1/2 = 1/16.
+// ------------------------------------------------------------------------------------------------
+template <bool BF16>
+__global__ void __launch_bounds__(256) fwht256_kernel(const void* __restrict__ in, long long ld_in, float* __restrict__ out,
+                                                      long long ld_out, const float* __restrict__ s, int mode, int rows,
+                                                      int nblk)
+{
+    const long long wid = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (wid >= (long long)rows * nblk) return;
+    const int lane = threadIdx.x & 31;
+    const long long r = wid / nblk;
+    const int b = (int)(wid % nblk);
+    const int c0 = b * 256 + 8 * lane;
+    float v[8];
+    if (BF16) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(in) + r * ld_in + c0);
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = __bfloat162float(h[k]);
+    } else {
+        const float* src = reinterpret_cast<const float*>(in) + r * ld_in + c0;
+        const float4 a = *reinterpret_cast<const float4*>(src), c = *reinterpret_cast<const float4*>(src + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    }
+    if (mode == 1) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = __fdiv_rn(v[k], s[c0 + k]);
+    } else if (mode == 2) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = __fmul_rn(v[k], s[c0 + k]);
+    }
+#pragma unroll
+    for (int h = 1; h < 8; h <<= 1)
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if (!(k & h)) {
+                const float a = v[k], bb = v[k + h];
+                v[k] = __fadd_rn(a, bb);
+                v[k + h] = __fsub_rn(a, bb);
+            }
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const bool upper = lane & m;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[k], m);
+            v[k] = upper ? __fsub_rn(o, v[k]) : __fadd_rn(v[k], o);
+        }
+    }
+    float* dst = out + r * ld_out + c0;
+    *reinterpret_cast<float4*>(dst) = make_float4(v[0] * 0.0625f, v[1] * 0.0625f, v[2] * 0.0625f, v[3] * 0.0625f);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4] * 0.0625f, v[5] * 0.0625f, v[6] * 0.0625f, v[7] * 0.0625f);
+}
+
+// ------------------------------------------------------------------------------------------------
+// scale fit, one warp per row: rms_rb = sqrt(mean_256(x^2)) clamped to 1e-10, times the format scale;
+// d_row = fp16(exp(mean_b log rms_rb)) clamped to 1e-8; e = clamp(round(log2(rms_rb / d_row) / e_step), -e_max, e_max-1);
+// d_rb = d_row * 2^(e_step * e).  Block sums: each lane adds 8 squares, then a fixed xor-tree over the warp.
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) scale_fit_kernel(const float* __restrict__ W, long long ld, int M, int nblk,
+                                                        float scale, float e_step, int e_max, __half* d_row_h,
+                                                        float* d_row, int8_t* e_out, float* d_rb)
+{
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= M) return;
+    const int lane = threadIdx.x & 31;
+    extern __shared__ float sm_rms[];
+    float* rms = sm_rms + (threadIdx.x >> 5) * nblk;
+    float logsum = 0.f;
+    for (int b = 0; b < nblk; b++) {
+        const float* src = W + (long long)row * ld + b * 256 + 8 * lane;
+        const float4 a = *reinterpret_cast<const float4*>(src), c = *reinterpret_cast<const float4*>(src + 4);
+        float acc = __fmul_rn(a.x, a.x);
+        acc = __fadd_rn(acc, __fmul_rn(a.y, a.y));
+        acc = __fadd_rn(acc, __fmul_rn(a.z, a.z));
+        acc = __fadd_rn(acc, __fmul_rn(a.w, a.w));
+        acc = __fadd_rn(acc, __fmul_rn(c.x, c.x));
+        acc = __fadd_rn(acc, __fmul_rn(c.y, c.y));
+        acc = __fadd_rn(acc, __fmul_rn(c.z, c.z));
+        acc = __fadd_rn(acc, __fmul_rn(c.w, c.w));
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+        const float r = __fmul_rn(fmaxf(sqrtf(__fdiv_rn(acc, 256.f)), 1e-10f), scale);
+        if (lane == 0) rms[b] = r;
+        logsum = __fadd_rn(logsum, logf(r));
+    }
+    // the mean over blocks multiplies by the reciprocal of the count, as torch's mean does
+    const float dr = fmaxf(__half2float(__float2half_rn(expf(__fmul_rn(logsum, 1.0f / (float)nblk)))), 1e-8f);
+    __syncwarp();
+    if (lane == 0) {
+        if (d_row_h) d_row_h[row] = __float2half_rn(dr);
+        if (d_row) d_row[row] = dr;
+    }
+    for (int b = lane; b < nblk; b += 32) {
+        float e = rintf(__fdiv_rn(log2f(__fdiv_rn(rms[b], dr)), e_step));
+        e = fminf(fmaxf(e, (float)-e_max), (float)(e_max - 1));
+        if (e_out) e_out[(long long)row * nblk + b] = (int8_t)e;
+        if (d_rb) d_rb[(long long)row * nblk + b] = __fmul_rn(dr, exp2f(__fmul_rn(e_step, e)));
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// LDLQ sub-block tiles: x[n][16 r + c] = w[16 n + r][c] * inv_d[16 n + r]   (w is a [M, 16] column slice, stride ld)
+// ------------------------------------------------------------------------------------------------
+__global__ void ldlq_gather_kernel(const float* __restrict__ w, long long ld, const float* __restrict__ inv_d, int M,
+                                   float* __restrict__ x)
+{
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per 4 elements
+    if (i >= (long long)M * 4) return;
+    const int row = (int)(i >> 2), c = (int)(i & 3) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(w + row * ld + c);
+    const float s = inv_d[row];
+    *reinterpret_cast<float4*>(x + (long long)row * 16 + c) =
+        make_float4(__fmul_rn(v.x, s), __fmul_rn(v.y, s), __fmul_rn(v.z, s), __fmul_rn(v.w, s));
+}
+
+// ------------------------------------------------------------------------------------------------
+// LDLQ feedback after the sub-block at columns [s0, s0 + 16) of a 256-column block, one warp per row:
+//   G[:, s0:s1] = g (the Viterbi reconstruction; with code: idx = label * U + u, gi = gain index);
+//   err = (w[:, s0:s1] - d * g) @ Uinv[s0:s1, s0:s1];   w[:, s1:256] -= err @ U[s0:s1, s1:256]
+// The 16 x (256 - s1) slice of U is staged in shared memory once per CTA.  Each dot product is a sequential fma chain.
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) ldlq_feedback_kernel(float* __restrict__ w, long long ld, int M, int s0,
+                                                            const float* __restrict__ d_rb,
+                                                            const float* __restrict__ rec, const int* __restrict__ code,
+                                                            const float* __restrict__ U, long long ldU,
+                                                            const float* __restrict__ Uinv, long long ldUi,
+                                                            float* __restrict__ G, long long ldG, int16_t* __restrict__ idx,
+                                                            uint8_t* __restrict__ gi, long long ldP)
+{
+    __shared__ float sU[16 * 256];
+    __shared__ float sUi[16 * 16];
+    const int s1 = s0 + 16, ncol = 256 - s1;
+    for (int i = threadIdx.x; i < 16 * ncol; i += blockDim.x) sU[i] = U[(long long)(s0 + i / ncol) * ldU + s1 + i % ncol];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) sUi[i] = Uinv[(long long)(s0 + i / 16) * ldUi + s0 + i % 16];
+    __syncthreads();
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= M) return;
+    const int lane = threadIdx.x & 31;
+    float* wr = w + (long long)row * ld;
+    // lanes 0..15: column s0 + lane of this row
+    float e = 0.f;
+    if (lane < 16) {
+        const float g = rec[(long long)row * 16 + lane];
+        G[(long long)row * ldG + s0 + lane] = g;
+        if (code) {
+            const int cd = code[(long long)row * 16 + lane];
+            idx[(long long)row * ldP + s0 + lane] = (int16_t)(cd & 0xffff);
+            gi[(long long)row * ldP + s0 + lane] = (uint8_t)(cd >> 16);
+        }
+        e = __fsub_rn(wr[s0 + lane], __fmul_rn(d_rb[row], g));
+    }
+    if (ncol == 0) return;
+    // err[k] = sum_i e[i] * Uinv[i][k], i ascending
+    float err = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        const float ei = __shfl_sync(0xffffffffu, e, i);
+        if (lane < 16) err = __fmaf_rn(ei, sUi[i * 16 + lane], err);
+    }
+    // w[s1 + j] -= sum_k err[k] * U[k][j], k ascending
+    float ek[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) ek[k] = __shfl_sync(0xffffffffu, err, k);
+    for (int j = lane; j < ncol; j += 32) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; k++) acc = __fmaf_rn(ek[k], sU[k * ncol + j], acc);
+        wr[s1 + j] = __fsub_rn(wr[s1 + j], acc);
+    }
+}
+
+}  // namespace
+
+extern "C" int ltq_fwht256(const void* in, int in_bf16, long long ld_in, float* out, long long ld_out, const float* scale,
+                           int mode, int rows, int cols, void* stream)
+{
+    if (rows < 0 || cols < 0 || cols % 256 || mode < 0 || mode > 2 || (mode && !scale) || ld_in < cols || ld_out < cols ||
+        (ld_in % 8) || (ld_out % 4))
+        return -1;
+    if (rows == 0 || cols == 0) return 0;
+    const long long warps = (long long)rows * (cols / 256);
+    const int blocks = (int)((warps + 7) / 8);
+    if (in_bf16)
+        fwht256_kernel<true><<<blocks, 256, 0, (cudaStream_t)stream>>>(in, ld_in, out, ld_out, scale, mode, rows, cols / 256);
+    else
+        fwht256_kernel<false><<<blocks, 256, 0, (cudaStream_t)stream>>>(in, ld_in, out, ld_out, scale, mode, rows, cols / 256);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_scale_fit(const float* W, long long ld, int M, int K, float scale, float e_step, int e_bits,
+                             uint16_t* d_row_h, float* d_row, int8_t* e, float* d_rb, void* stream)
+{
+    if (M < 0 || K <= 0 || K % 256 || ld < K || (ld % 4) || e_bits < 1 || e_bits > 8 || !(e_step > 0.f)) return -1;
+    if (M == 0) return 0;
+    const int nblk = K / 256;
+    const int smem = 8 * nblk * 4;
+    if (smem > 48 * 1024) return -1;
+    scale_fit_kernel<<<(M + 7) / 8, 256, smem, (cudaStream_t)stream>>>(W, ld, M, nblk, scale, e_step, 1 << (e_bits - 1),
+                                                                       reinterpret_cast<__half*>(d_row_h), d_row, e, d_rb);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_ldlq_gather(const float* w, long long ld, const float* inv_d, int M, float* x, void* stream)
+{
+    if (M < 0 || M % 16 || (ld % 4) || ((uintptr_t)w & 15)) return -1;
+    if (M == 0) return 0;
+    const long long n = (long long)M * 4;
+    ldlq_gather_kernel<<<(int)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(w, ld, inv_d, M, x);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_ldlq_feedback(float* w, long long ld, int M, int s0, const float* d_rb, const float* rec,
+                                 const int* code, const float* U, long long ldU, const float* Uinv, long long ldUi,
+                                 float* G, long long ldG, int16_t* idx, uint8_t* gi, long long ldP, void* stream)
+{
+    if (M < 0 || s0 < 0 || s0 > 240 || s0 % 16 || (code && (!idx || !gi))) return -1;
+    if (M == 0) return 0;
+    ldlq_feedback_kernel<<<(M + 7) / 8, 256, 0, (cudaStream_t)stream>>>(w, ld, M, s0, d_rb, rec, code, U, ldU, Uinv, ldUi,
+                                                                       G, ldG, idx, gi, ldP);
+    return (int)cudaGetLastError();
+}

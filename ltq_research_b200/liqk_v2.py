@@ -1,0 +1,309 @@
+"""Matrix quantizer of the LTQ TCQ formats on B200: the TCQ path of the reference's ``quantize_matrix_liqk_v2``.
+
+Mirrors lumen-inference/ltq-research src/liqk_v2.py (same names, arguments, return values and ``PACK`` side channel):
+  * ``compute_optimal_suh`` (:409-441) — column scale suh and the FWHT-256 rotations of W and H (ltq_fwht256 kernel);
+  * ``_quantize_rows_tcq_ldlq`` (:872-1021, row-scale branch :956-980) — scale fit (ltq_scale_fit kernel), then per
+    256-column block 16 sub-blocks of tail-biting Viterbi (ltq_viterbi_tb) with the intra-block error feedback
+    (ltq_ldlq_gather / ltq_ldlq_feedback kernels) and the inter-block feedback GEMM (cuBLAS fp32 through torch);
+  * ``quantize_matrix_liqk_v2`` (:1029-1198) — damping, Cholesky factorisation (cuSOLVER through torch), row groups,
+    c_row and suh refits, PACK emission.
+Only the tail-biting row-scale formats of TCQ_CONFIG (the .ltq formats) are handled; the reference's other quantizers
+(.liqk v2 banks, E8) are out of this path.  Everything runs on CUDA; there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import ptr
+from .formats import LIQK_V2_SPECS, QK_K, SUBBLOCK_SIZE, TCQ_CONFIG  # noqa: F401
+from .tcq_proto import make_gains
+
+NUM_SUBBLOCKS = QK_K // SUBBLOCK_SIZE
+# Packing mode for .ltq: if not None, the quantizer stores each matrix's tile codes, d_row, e and suh in
+# PACK["matrix"] (src/liqk_v2.py:72-74)
+PACK: Optional[dict] = None
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise RuntimeError(f"{what}: CUDA error code {rc}")
+
+
+def _stream(dev) -> int:
+    return _lib.stream_ptr(dev)
+
+
+def make_rademacher_signs(dim: int, seed: int, device) -> torch.Tensor:
+    """Deterministic +-1 signs from a CPU generator (src/iqk_format.py:173-179)."""
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(seed)
+    bits = torch.randint(0, 2, (dim,), generator=gen, dtype=torch.int64)
+    return (bits * 2 - 1).to(dtype=torch.float32, device=device)
+
+
+def fwht_rows_scaled(x: torch.Tensor, scale: Optional[torch.Tensor] = None, mode: int = 0,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FWHT-256 of every 256-block of every row of x [R, C] (fp32 or bf16), after dividing (mode 1) or multiplying
+    (mode 2) column c by scale[c]: the normalized transform of src/iqk_format.py:153-170, bit for bit."""
+    dev = _lib.require_cuda(x)
+    R, C = x.shape
+    if x.stride(1) != 1 or x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float().contiguous()
+    out = torch.empty((R, C), dtype=torch.float32, device=dev) if out is None else out
+    s = scale.float().contiguous() if scale is not None else None
+    _check(_lib.lib().ltq_fwht256(ptr(x), int(x.dtype == torch.bfloat16), x.stride(0), ptr(out), out.stride(0), ptr(s),
+                                  mode, R, C, _stream(dev)), "ltq_fwht256")
+    return out
+
+
+def fwht_inplace(x: torch.Tensor, block_size: int = 256) -> torch.Tensor:
+    """src/iqk_format.py:153-170 for block_size 256 (any leading shape); returns the transformed tensor."""
+    assert block_size == QK_K
+    shp = x.shape
+    return fwht_rows_scaled(x.reshape(-1, shp[-1])).view(shp)
+
+
+def _fwht_rows(X: torch.Tensor) -> torch.Tensor:
+    """Block FWHT-256 over rows (along the first dimension), src/liqk_v2.py:1024-1026."""
+    return fwht_rows_scaled(X.T.contiguous()).T.contiguous()
+
+
+@torch.no_grad()
+def compute_optimal_suh(W: torch.Tensor, H: torch.Tensor, seed: int = 1337,
+                        row_weights: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """src/liqk_v2.py:409-441: suh = fp16(sign * clamp(col_rms^0.5 * h_std^-0.25, 0.25, 4));
+    W_rot = FWHT(W / suh), H_rot = FWHT(FWHT(H * suh)^T * suh)^T."""
+    device = W.device
+    M, K = W.shape
+    signs = make_rademacher_signs(K, seed=seed, device=device)
+    Wf = W.float()
+    if row_weights is not None:
+        rw = row_weights.float().clamp(min=float(row_weights.mean().item()) * 0.1)
+        rw = (rw / rw.mean().clamp(min=1e-12)).clamp(0.25, 4.0)
+        col_rms = ((Wf.square() * rw.unsqueeze(1)).mean(dim=0)).sqrt().clamp(min=1e-6)
+    else:
+        col_rms = Wf.square().mean(dim=0).sqrt().clamp(min=1e-6)
+    col_rms = col_rms / col_rms.mean().clamp(min=1e-6)
+    h_std = torch.diagonal(H.float()).clamp(min=1e-8).sqrt()
+    h_std = h_std / h_std.mean().clamp(min=1e-6)
+    scale = ((col_rms ** 0.5) * (h_std ** -0.25)).clamp(0.25, 4.0)
+    suh = (signs * scale).to(torch.float16).to(torch.float32)
+    W_rot = fwht_rows_scaled(W if W.dtype in (torch.float32, torch.bfloat16) else Wf, suh, mode=1)
+    H_tmp = fwht_rows_scaled(H.float(), suh, mode=2)
+    H_rot = fwht_rows_scaled(H_tmp.T.contiguous(), suh, mode=2).T
+    return W_rot, H_rot, suh
+
+
+class _TcqRunner:
+    """Per-format state of the sub-block Viterbi calls: tables, gains, buffers and workspace reused across calls."""
+
+    def __init__(self, spec: str, M: int, device):
+        cfg = TCQ_CONFIG[spec]
+        self.cfg = cfg
+        self.dev = device
+        self.nt = M // 16
+        self.lut = torch.tensor(cfg["lut"], dtype=torch.float32, device=device)
+        self.gains = make_gains(cfg["h"], cfg["step"], device).float().contiguous()
+        self.K = cfg["K"]
+        self.sub = cfg.get("sub", SUBBLOCK_SIZE)
+        self.pp = int(cfg.get("pp", 0))
+        self.m_extra = tuple(cfg.get("m_extra", ()))
+        self.me = torch.tensor(list(self.m_extra) + [0], dtype=torch.int32)
+        self.n_cand = int(os.environ.get("TCQ_NCAND", cfg.get("n_cand", 0)))
+        self.tb_window = int(os.environ.get("TCQ_TB_WIN", "32"))
+        self.x = torch.empty((self.nt, 256), dtype=torch.float32, device=device)
+        self.rec = torch.empty_like(self.x)
+        self.code = torch.empty((self.nt, 256), dtype=torch.int32, device=device)
+        L = _lib.lib()
+        wsb = L.ltq_viterbi_tb_workspace_bytes(self.nt, 256, self.gains.numel(), self.n_cand, self.sub, self.pp,
+                                              self.tb_window, 0)
+        self.ws = torch.empty(max(int(wsb), 256), dtype=torch.uint8, device=device)
+
+    def run(self, dw256: torch.Tensor):
+        """Tail-biting Viterbi of self.x (tiles of the current sub-block) with per-position weights dw256 [256]."""
+        L = _lib.lib()
+        c = self.cfg
+        _check(L.ltq_viterbi_tb(ptr(self.x), ptr(dw256), 0, ptr(self.lut), ptr(self.gains), None, None, ptr(self.rec),
+                                ptr(self.code), self.nt, 256, c["nu"], self.K, c["m"],
+                                ctypes.cast(self.me.data_ptr(), ctypes.c_void_p), len(self.m_extra), self.gains.numel(),
+                                self.n_cand, self.sub, 1 << (self.K - 1), 0, self.pp, 2, 0, self.tb_window,
+                                ptr(self.ws), self.ws.numel(), _stream(self.dev)), "tcq_viterbi")
+
+
+@torch.no_grad()
+def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: torch.Tensor, diag_w: torch.Tensor,
+                            spec_name: str, n_pass: int = 2) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Block16-LDLQ with TCQ tiles, row-scale formats (src/liqk_v2.py:872-1021): returns (d_full fp16 [M, K/256],
+    W_hat_rot [M, K]); with PACK set, appends the group's codes to PACK["groups"]."""
+    cfg = TCQ_CONFIG[spec_name]
+    if not (cfg.get("row_scale") and cfg.get("tb")):
+        raise ValueError(f"{spec_name}: only the tail-biting row-scale (.ltq) TCQ formats are on this path")
+    device = W_rot.device
+    L = _lib.lib()
+    st = _stream(device)
+    M, K = W_rot.shape
+    assert M % 16 == 0, "TCQ: number of rows must be divisible by 16"
+    nblocks = K // QK_K
+    W_work = W_rot.float().contiguous().clone()
+    W_hat_rot = torch.empty_like(W_work)
+    d_full = torch.empty((M, nblocks), dtype=torch.float16, device=device)
+    G = torch.empty((M, K), dtype=torch.float32, device=device)
+    idx = torch.empty((M, K), dtype=torch.int16, device=device)
+    gi = torch.empty((M, K), dtype=torch.uint8, device=device)
+
+    # d(row, block) = d_row * 2^(0.25 e), e 5-bit in [-16, 15]; d_row fp16 = geometric mean of the row's block rms
+    e_step, e_bits = cfg.get("e_step", 0.25), cfg.get("e_bits", 5)
+    d_row = torch.empty(M, dtype=torch.float32, device=device)
+    e_rb = torch.empty((M, nblocks), dtype=torch.int8, device=device)
+    d_rb_all = torch.empty((M, nblocks), dtype=torch.float32, device=device)
+    _check(L.ltq_scale_fit(ptr(W_work), W_work.stride(0), M, K, float(cfg.get("scale", 1.0)), float(e_step), int(e_bits),
+                           None, ptr(d_row), ptr(e_rb), ptr(d_rb_all), st), "ltq_scale_fit")
+
+    run = _TcqRunner(spec_name, M, device)
+    Uc = U.contiguous()
+    for ibl in range(nblocks):
+        c0, c1 = ibl * QK_K, (ibl + 1) * QK_K
+        w_blk_start = W_work[:, c0:c1].clone()
+        w_sub_work = w_blk_start.clone()
+        U_blk_inv = U_blks_inv[ibl].contiguous()
+        diag_w_blk = diag_w[c0:c1]
+        d_rb = d_rb_all[:, ibl].clamp(min=1e-8).contiguous()
+        inv_d = (1.0 / d_rb).contiguous()
+        dw_all = diag_w_blk.float().view(NUM_SUBBLOCKS, SUBBLOCK_SIZE).repeat(1, 16).contiguous()  # [16, 256]
+        for ib in range(NUM_SUBBLOCKS):
+            s0 = ib * SUBBLOCK_SIZE
+            _check(L.ltq_ldlq_gather(ptr(w_sub_work) + 4 * s0, w_sub_work.stride(0), ptr(inv_d), M, ptr(run.x), st),
+                   "ltq_ldlq_gather")
+            run.run(dw_all[ib])
+            _check(L.ltq_ldlq_feedback(ptr(w_sub_work), w_sub_work.stride(0), M, s0, ptr(d_rb), ptr(run.rec),
+                                       ptr(run.code), ptr(Uc) + 4 * (c0 * K + c0), K, ptr(U_blk_inv), QK_K,
+                                       ptr(G) + 4 * c0, K, ptr(idx) + 2 * c0, ptr(gi) + c0, K, st), "ltq_ldlq_feedback")
+        best_what_row = d_rb.unsqueeze(1) * G[:, c0:c1]
+        W_hat_rot[:, c0:c1] = best_what_row
+        d_full[:, ibl] = d_rb.to(torch.float16)
+        if c1 < K:
+            err_blk = (w_blk_start - best_what_row) @ U_blk_inv
+            W_work[:, c1:] -= err_blk @ Uc[c0:c1, c1:]
+    if PACK is not None:
+        PACK["groups"].append({"spec": spec_name, "d_row": d_row, "e": e_rb, "idx": idx, "gi": gi, "G": G})
+    return d_full, W_hat_rot
+
+
+@torch.no_grad()
+def quantize_matrix_liqk_v2(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
+                            row_weights: Optional[torch.Tensor] = None, cd_sweeps: int = 2, out_rot: bool = False):
+    """src/liqk_v2.py:1029-1198 for the TCQ formats: returns (qdata, W_hat [M, K] fp32, rel_loss); with PACK set,
+    PACK["matrix"] holds the .ltq fields (row_slices, idx, gi, G, d_row fp16, e int8, suh fp16)."""
+    _lib.require_cuda(W, H)
+    if out_rot:
+        s_out = make_rademacher_signs(W.shape[0], seed=seed + 7919, device=W.device)
+        rw = None
+        if row_weights is not None:
+            rw = row_weights.float().view(-1, QK_K).mean(dim=1, keepdim=True).expand(-1, QK_K).reshape(-1)
+        q_res, w_hat_r, rel = quantize_matrix_liqk_v2(_fwht_rows(W.float() * s_out.unsqueeze(1)), H, spec_or_row_specs,
+                                                      seed=seed, damp=damp, row_weights=rw, cd_sweeps=cd_sweeps)
+        q_res["s_out"] = s_out.to(torch.int8)
+        return q_res, _fwht_rows(w_hat_r) * s_out.unsqueeze(1), rel
+
+    W_f32 = W.float()
+    H_f32 = H.float()
+    M, K = W_f32.shape
+    nblocks = K // QK_K
+    specs_used = [spec_or_row_specs] if isinstance(spec_or_row_specs, str) else [sp for _, _, sp in spec_or_row_specs]
+    for sp in specs_used:
+        if sp not in TCQ_CONFIG:
+            raise ValueError(f"{sp}: not a TCQ (.ltq) format; this path quantizes the TCQ formats only")
+    damp *= float(os.environ.get("TCQ_DAMP_MULT", "10"))
+
+    W_rot, H_rot, suh = compute_optimal_suh(W, H_f32, seed=seed, row_weights=row_weights)
+
+    H_reg = H_rot.float().clone()
+    diag_mean = H_reg.diagonal().mean().clamp(min=1e-8)
+    H_reg.diagonal().add_(damp * diag_mean)
+    L_flip = torch.linalg.cholesky(H_reg.flip(0, 1))
+    del H_rot, H_reg
+    U = torch.linalg.solve_triangular(L_flip, torch.eye(K, dtype=L_flip.dtype, device=L_flip.device), upper=False)
+    U = U.flip(0, 1)
+    del L_flip
+    diag_w = 1.0 / (torch.diagonal(U) ** 2).clamp(min=1e-12)
+    eye256 = torch.eye(QK_K, dtype=torch.float32, device=W.device).unsqueeze(0).expand(nblocks, -1, -1)
+    U_blks = torch.stack([U[b * QK_K:(b + 1) * QK_K, b * QK_K:(b + 1) * QK_K] for b in range(nblocks)], dim=0)
+    U_blks_inv = torch.linalg.solve_triangular(U_blks, eye256, upper=True)
+
+    row_slices = [(0, M, spec_or_row_specs)] if isinstance(spec_or_row_specs, str) else spec_or_row_specs
+    by_spec: Dict[str, List[Tuple[int, int]]] = {}
+    for r0, r1, sp in row_slices:
+        by_spec.setdefault(sp, []).append((r0, r1))
+
+    W_hat_rot = torch.empty_like(W_rot)
+    d_full = torch.empty((M, nblocks), dtype=torch.float16, device=W.device)
+    if PACK is not None:
+        PACK["groups"] = []
+        pm = {"idx": torch.empty((M, K), dtype=torch.int16, device=W.device),
+              "gi": torch.empty((M, K), dtype=torch.uint8, device=W.device),
+              "G": torch.empty((M, K), dtype=torch.float32, device=W.device), "d_row": torch.empty(M, device=W.device),
+              "e": torch.empty((M, nblocks), dtype=torch.int8, device=W.device)}
+    for sp, ranges in by_spec.items():
+        rows_idx = torch.cat([torch.arange(r0, r1, device=W.device) for r0, r1 in ranges], dim=0)
+        d_sub, Wh_sub = _quantize_rows_tcq_ldlq(W_rot[rows_idx], U, U_blks_inv, diag_w, sp)
+        W_hat_rot[rows_idx] = Wh_sub
+        d_full[rows_idx] = d_sub
+        if PACK is not None:
+            g = PACK["groups"].pop()
+            for k in ("idx", "gi", "G", "d_row", "e"):
+                pm[k][rows_idx] = g[k].to(pm[k].dtype)
+
+    U_base = fwht_inplace(W_hat_rot.clone(), block_size=QK_K)
+    W_hat_eff = U_base * suh.unsqueeze(0)
+    c_pack = torch.ones((M,), dtype=torch.float32, device=W.device)
+    HW = W_f32 @ H_f32
+    HQ = W_hat_eff @ H_f32
+    c_row = (W_hat_eff * HW).sum(dim=1) / (W_hat_eff * HQ).sum(dim=1).clamp(min=1e-12)
+    c_row = torch.where(torch.isfinite(c_row) & (c_row > 0.5) & (c_row < 2.0), c_row, torch.ones_like(c_row))
+    d_new = (d_full.float() * c_row.unsqueeze(1)).to(torch.float16)
+    c_eff = (d_new.float() / d_full.float().clamp(min=1e-12)).mean(dim=1, keepdim=True)
+    U_scaled = U_base * c_eff
+    if row_weights is not None:
+        rw = row_weights.float().clamp(min=float(row_weights.mean().item()) * 0.1)
+        rw = (rw / rw.mean().clamp(min=1e-12)).clamp(0.25, 4.0)
+        U_w = U_scaled * rw.unsqueeze(1)
+    else:
+        rw = torch.ones((M,), dtype=torch.float32, device=W.device)
+        U_w = U_scaled
+    A_in = (U_w.T @ U_scaled) * H_f32
+    b_in = (U_w * HW).sum(dim=0)
+    A_in.diagonal().add_(1e-3 * A_in.diagonal().mean().clamp(min=1e-12))
+    try:
+        suh_cand = torch.linalg.solve(A_in, b_in).to(torch.float16).to(torch.float32)
+        valid_s = torch.isfinite(suh_cand) & (suh_cand.abs() > 0.05) & (suh_cand.abs() < 10.0)
+        suh_cand = torch.where(valid_s, suh_cand, suh)
+        W_hat_cand = U_scaled * suh_cand.unsqueeze(0)
+        HQ_cand = W_hat_cand @ H_f32
+        diff_base = W_f32 - W_hat_eff
+        diff_cand = W_f32 - W_hat_cand
+        loss_base = float((((HW - HQ) * diff_base).sum(dim=1) * rw).sum().item())
+        loss_cand = float((((HW - HQ_cand) * diff_cand).sum(dim=1) * rw).sum().item())
+        if loss_cand < loss_base:
+            W_hat_eff, d_full, suh, HQ, c_pack = W_hat_cand, d_new, suh_cand, HQ_cand, c_eff.squeeze(1)
+    except RuntimeError:
+        pass
+    if PACK is not None:
+        d_row_p = (pm["d_row"] * c_pack).to(torch.float16)
+        suh_p = suh.to(torch.float16)
+        scale = d_row_p.float().unsqueeze(1) * torch.exp2(0.25 * pm["e"].float())
+        Wq_rot = (scale.unsqueeze(2) * pm["G"].view(M, nblocks, QK_K)).view(M, K)
+        W_hat_eff = fwht_inplace(Wq_rot, block_size=QK_K) * suh_p.float().unsqueeze(0)
+        HQ = W_hat_eff @ H_f32
+        PACK["matrix"] = {"row_slices": row_slices, "idx": pm["idx"], "gi": pm["gi"], "G": pm["G"], "d_row": d_row_p,
+                          "e": pm["e"], "suh": suh_p}
+    diff = W_f32 - W_hat_eff
+    num_loss = float(((HW - HQ) * diff).sum().item())
+    den_loss = float((HW * W_f32).sum().clamp(min=1e-12).item())
+    rel_loss = num_loss / den_loss
+    qdata_out = {"d": d_full, "suh": suh.to(torch.float16), "row_slices": row_slices}
+    return qdata_out, W_hat_eff, rel_loss

@@ -1,0 +1,191 @@
+"""GPU parity of the matrix path (src/liqk_v2.py): FWHT-256, scale fit, LDLQ feedback and the whole
+quantize_matrix_liqk_v2 (TCQ formats, PACK mode).
+
+Bit-exact where the operation order is the reference's (FWHT butterflies, per-element scaling, the Viterbi itself).
+Where the reference relies on a library reduction or GEMM whose summation order is not part of its definition (column
+and block means, the LDLQ feedback products, cuBLAS / CPU BLAS), results are compared within the tolerances written in
+each test; the codes of the whole quantizer are compared against the reference run (tests/golden/matrix_quant.npz).
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import vit_cases as VC
+from tests.golden.matrix_inputs import CASES, synth
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def test_fwht_bit_exact(cuda_dev):
+    from ltq_research_b200.liqk_v2 import fwht_rows_scaled
+    z = np.load(GOLDEN / "fwht.npz")
+    y = fwht_rows_scaled(torch.from_numpy(z["x"]).to(cuda_dev)).cpu().numpy()
+    assert np.array_equal(y.view(np.uint32), z["y"].view(np.uint32))
+    # column scaling modes and bf16 input against the restated butterfly
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(40, 1024, generator=g) * 3
+    s = (torch.rand(1024, generator=g) + 0.25).to(torch.float16).float()
+    for mode, xin in ((1, x / s), (2, x * s)):
+        got = fwht_rows_scaled(x.to(cuda_dev), s.to(cuda_dev), mode=mode).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), O.fwht(xin.numpy()).view(np.uint32)), mode
+    xb = x.to(torch.bfloat16)
+    got = fwht_rows_scaled(xb.to(cuda_dev), s.to(cuda_dev), mode=1).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), O.fwht((xb.float() / s).numpy()).view(np.uint32))
+
+
+def test_scale_fit_matches_reference_ops(cuda_dev):
+    """ltq_scale_fit vs the reference's torch expression (src/liqk_v2.py:938-946) on the same device.  The block sums
+    are reductions whose order torch leaves open: rms values agree to 2 ulp, d_row / e / d_rb are equal except where a
+    rounding boundary falls between the two orders (at most 1 % of rows here)."""
+    from ltq_research_b200 import _lib
+    g = torch.Generator().manual_seed(5)
+    M, K = 512, 2048
+    W = (torch.randn(M, K, generator=g) * torch.exp(torch.randn(M, 1, generator=g))).to(cuda_dev)
+    W[:, 7] *= 40
+    nb = K // 256
+    scale = 1.1
+    rms_rb = W.view(M, nb, 256).square().mean(dim=2).sqrt().clamp(min=1e-10) * scale
+    d_row = torch.exp(torch.log(rms_rb).mean(dim=1)).to(torch.float16).to(torch.float32).clamp(min=1e-8)
+    e_rb = torch.round(torch.log2(rms_rb / d_row.unsqueeze(1)) / 0.25).clamp(-16, 15)
+    d_rb = d_row.unsqueeze(1) * torch.exp2(0.25 * e_rb)
+    o_d = torch.empty(M, device=cuda_dev)
+    o_e = torch.empty((M, nb), dtype=torch.int8, device=cuda_dev)
+    o_drb = torch.empty((M, nb), device=cuda_dev)
+    rc = _lib.lib().ltq_scale_fit(W.data_ptr(), K, M, K, scale, 0.25, 5, None, o_d.data_ptr(), o_e.data_ptr(),
+                                  o_drb.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert (o_d == d_row).float().mean() >= 0.99
+    assert (o_e.float() == e_rb).float().mean() >= 0.99
+    same = (o_d == d_row).unsqueeze(1) & (o_e.float() == e_rb)
+    assert torch.equal(o_drb[same], d_rb[same])
+
+
+def test_ldlq_feedback_matches_reference_ops(cuda_dev):
+    """One sub-block of feedback vs the reference's torch ops (src/liqk_v2.py:964-971), fp32 tolerance 1e-5
+    relative to the row norm (the 16-term dot products use fma chains; torch uses its GEMM)."""
+    from ltq_research_b200 import _lib
+    g = torch.Generator().manual_seed(9)
+    M = 256
+    w = torch.randn(M, 256, generator=g).to(cuda_dev)
+    # U as the pipeline builds it: upper Cholesky factor of the inverse of a damped Gram matrix (src/liqk_v2.py:1074-1088)
+    X = torch.randn(1024, 256, generator=g) * torch.exp(torch.randn(1, 256, generator=g) * 0.5)
+    Hm = (X.T @ X / 1024).double()
+    Hm += 0.2 * Hm.diagonal().mean() * torch.eye(256, dtype=torch.float64)
+    Lf = torch.linalg.cholesky(Hm.flip(0, 1))
+    Ub = torch.linalg.solve_triangular(Lf, torch.eye(256, dtype=torch.float64), upper=False).flip(0, 1).float().contiguous().to(cuda_dev)
+    Ui = torch.linalg.solve_triangular(Ub, torch.eye(256, device=cuda_dev), upper=True).contiguous()
+    d = (torch.rand(M, generator=g) + 0.5).to(cuda_dev)
+    for s0 in (0, 112, 240):
+        rec = torch.randn(M // 16, 256, generator=g).to(cuda_dev)
+        code = torch.randint(0, 1 << 20, (M // 16, 256), generator=g, dtype=torch.int32).to(cuda_dev)
+        G = torch.zeros(M, 256, device=cuda_dev)
+        idx = torch.zeros(M, 256, dtype=torch.int16, device=cuda_dev)
+        gi = torch.zeros(M, 256, dtype=torch.uint8, device=cuda_dev)
+        wk = w.clone()
+        rc = _lib.lib().ltq_ldlq_feedback(wk.data_ptr(), 256, M, s0, d.data_ptr(), rec.data_ptr(), code.data_ptr(),
+                                          Ub.data_ptr(), 256, Ui.data_ptr(), 256, G.data_ptr(), 256, idx.data_ptr(),
+                                          gi.data_ptr(), 256, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert rc == 0
+        g_sub = rec.view(M, 16)
+        s1 = s0 + 16
+        assert torch.equal(G[:, s0:s1], g_sub)
+        assert torch.equal(idx[:, s0:s1].int() & 0xFFFF, (code.view(M, 16) & 0xFFFF).short().int() & 0xFFFF)
+        assert torch.equal(gi[:, s0:s1].int(), (code.view(M, 16) >> 16) & 0xFF)
+        want = w.clone()
+        err = (want[:, s0:s1] - d.unsqueeze(1) * g_sub) @ Ui[s0:s1, s0:s1]
+        want[:, s1:] -= err @ Ub[s0:s1, s1:]
+        assert torch.equal(wk[:, :s1], want[:, :s1])
+        if s1 < 256:
+            rel = ((wk - want).norm(dim=1) / want.norm(dim=1)).max().item()
+            assert rel < 1e-5, rel
+
+
+def _patch_cpu_gains(monkeypatch):
+    """The reference run made its gain tables on the CPU; use the same values (the format stores them explicitly)."""
+    import ltq_research_b200.liqk_v2 as L
+    from ltq_research_b200.tcq_proto import make_gains as mg
+
+    def cpu_gains(h, step, device="cuda"):
+        return mg(h, step, "cpu").to(device)
+    monkeypatch.setattr(L, "make_gains", cpu_gains)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_quantize_matrix_vs_reference_run(case, cuda_dev, monkeypatch):
+    """quantize_matrix_liqk_v2 on the B200 vs the reference's own function (CPU, oracle Viterbi) on the same inputs.
+    Before the refits (tight): the rotation's suh and the rows' fp16 d_row equal in >= 98 % of entries (a column or
+    block mean taken in another order can cross an fp16 rounding boundary), the 5-bit exponents in >= 99 %.
+    The codes: >= 90 % of weights equal (the LDLQ feedback inputs differ in the last bits between two BLAS orders, and a
+    Viterbi decision near a tie then differs).  After the refits (c_row, and suh from a K x K solve whose CPU and GPU
+    results differ beyond fp16 resolution): suh within 5 % in >= 95 % of columns, rel_loss within 5 % relative."""
+    import ltq_research_b200.liqk_v2 as L
+    _patch_cpu_gains(monkeypatch)
+    z = np.load(GOLDEN / "matrix_quant.npz")
+    meta = {m["name"]: m for m in json.loads(bytes(z["meta"]).decode())}
+    name, M, K, spec, seed = case
+    spec = spec if isinstance(spec, str) else [tuple(s) for s in spec]
+    W, H = synth(M, K, seed)
+    Wd, Hd = W.to(cuda_dev), H.to(cuda_dev)
+    groups = []
+    orig = L._quantize_rows_tcq_ldlq
+
+    def hook(*a, **k):
+        out = orig(*a, **k)
+        groups.append(L.PACK["groups"][-1]["d_row"].clone())
+        return out
+    monkeypatch.setattr(L, "_quantize_rows_tcq_ldlq", hook)
+    L.PACK = {}
+    try:
+        q, w_hat, rel = L.quantize_matrix_liqk_v2(Wd, Hd, spec, seed=1337, damp=0.02)
+        pm = {k: v for k, v in L.PACK["matrix"].items()}
+    finally:
+        L.PACK = None
+    _, _, suh0 = L.compute_optimal_suh(Wd, Hd.float(), seed=1337)
+    specs = [(0, M, spec)] if isinstance(spec, str) else spec
+    by = {}
+    for r0, r1, sp in specs:
+        by.setdefault(sp, []).append(torch.arange(r0, r1))
+    d0 = torch.zeros(M)
+    for rows, dr in zip([torch.cat(v) for v in by.values()], groups):
+        d0[rows] = dr.cpu()
+    stats = {
+        "suh0_eq": float((suh0.to(torch.float16).cpu().view(torch.int16).numpy() == z[f"{name}/suh0"]).mean()),
+        "d_row0_eq": float((d0.numpy() == z[f"{name}/d_row0"]).mean()),
+        "e_eq": float((pm["e"].cpu().numpy() == z[f"{name}/e"]).mean()),
+        "codes_eq": float(((pm["idx"].cpu().numpy() == z[f"{name}/idx"]) & (pm["gi"].cpu().numpy() == z[f"{name}/gi"])).mean()),
+        "rel_loss": rel, "rel_loss_ref": meta[name]["rel_loss"],
+    }
+    suh = pm["suh"].cpu().float().numpy()
+    suh_ref = z[f"{name}/suh"].view(np.float16).astype(np.float32)
+    stats["suh_within_5pct"] = float((np.abs(suh - suh_ref) <= 0.05 * np.abs(suh_ref)).mean())
+    print(name, json.dumps(stats))
+    assert stats["suh0_eq"] >= 0.98 and stats["d_row0_eq"] >= 0.98 and stats["e_eq"] >= 0.99, stats
+    assert stats["codes_eq"] >= 0.90, stats
+    assert stats["suh_within_5pct"] >= 0.95, stats
+    assert abs(rel - stats["rel_loss_ref"]) <= 0.05 * abs(stats["rel_loss_ref"]), stats
+    # the reconstruction rebuilt from the packed fields is the returned W_hat (src/liqk_v2.py:1182-1190)
+    G = pm["G"]
+    for r0, r1, sp in specs:
+        cfg = L.TCQ_CONFIG[sp]
+        lut = torch.tensor(cfg["lut"], device=cuda_dev)
+        gains = L.make_gains(cfg["h"], cfg["step"], cuda_dev)
+        assert torch.equal(G[r0:r1], gains[pm["gi"][r0:r1].long()] * lut[pm["idx"][r0:r1].long()]), sp
+
+
+def test_make_gains_cpu_vs_cuda(cuda_dev):
+    """Informative: the gain tables evaluated on CPU and on the B200 (the format stores whichever the quantizer used)."""
+    from ltq_research_b200.tcq_proto import make_gains
+    diff = 0
+    for name in VC.MENU:
+        c = VC.F[name]
+        a = make_gains(c["h"], c["step"], "cpu")
+        b = make_gains(c["h"], c["step"], cuda_dev).cpu()
+        diff += int((a != b).sum())
+    assert diff >= 0
