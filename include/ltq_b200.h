@@ -88,6 +88,27 @@ int ltq_ldlq_feedback(float* w, long long ld, int M, int s0, const float* d_rb, 
                       int16_t* idx, uint8_t* gi, long long ldP, void* stream);
 
 /*
+ * One 256-column block of the row-scale TCQ LDLQ quantizer in one launch (src/liqk_v2.py:956-971 with quant_sub
+ * :913-936): for each of the block's 16 sub-blocks, the gather, the two-pass tail-biting Viterbi of
+ * viterbi_ub_cuda(..., tail_biting=True, tb_window=W) (src/tcq_proto.py:584-609) on the M/16 tiles, and the intra-block
+ * feedback — the same results, bit for bit, as ltq_ldlq_gather + ltq_viterbi_tb + ltq_ldlq_feedback per sub-block.
+ *   w_blk [M, 256] (row stride ld_w): the block of the working matrix at the block's start (read only);
+ *   d_rb: the rows' block scale at d_rb[row * ld_d] (clamped to 1e-8 inside); dw [256]: diag_w of the block's columns;
+ *   U / Uinv: U[c0:c0+256, c0:c0+256] and its inverse, row strides ldU / ldUi;
+ *   out: G [M, 256] (stride ldG) reconstruction levels, idx (label * U + u) and gi (gain index) [M, 256] (stride ldP);
+ *   the table, gains, masks, K, Gfull, n_cand, sub and pp of the format as for ltq_viterbi_tb (nu = 10, T = 256).
+ * workspace: at least ltq_ldlq_block_workspace_bytes(M, ...) bytes, 256-byte aligned.  The inter-block update after the
+ * block (src/liqk_v2.py:972-979) stays with the caller (a GEMM).  Limits: M % 16 == 0, sub % 4 == 0, at most 4 gain
+ * slots in the search (n_cand <= 4 or Gfull <= 4).
+ */
+size_t ltq_ldlq_block_workspace_bytes(int M, int Gfull, int n_cand, int sub, int pp, int tb_window);
+int ltq_ldlq_block(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* dw,
+                   const float* U, long long ldU, const float* Uinv, long long ldUi, float* G, long long ldG,
+                   int16_t* idx, uint8_t* gi, long long ldP, int M, const float* tab, const float* gains, int K, int m,
+                   const int* m_extra, int n_extra, int Gfull, int n_cand, int sub, int pp, int tb_window,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Allocation-free tail-biting Viterbi.  No counterpart in the reference (the reference's Python wrapper allocates all
  * scratch with torch); added for callers that cannot allocate device memory while they quantize — an engine that plans
  * its device memory at start-up and forbids allocation afterwards, or a binding (cgo / JNI / N-API / ctypes) that only

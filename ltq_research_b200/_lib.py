@@ -17,6 +17,7 @@ _LOCK = threading.Lock()
 P = ctypes.c_void_p
 I = ctypes.c_int
 SZ = ctypes.c_size_t
+LL = ctypes.c_longlong
 
 # name -> (restype, argtypes); mirrors include/ltq_b200.h
 SIGNATURES = {
@@ -31,6 +32,8 @@ SIGNATURES = {
     "ltq_ldlq_gather": (I, [P, ctypes.c_longlong, P, I, P, P]),
     "ltq_ldlq_feedback": (I, [P, ctypes.c_longlong, I, I, P, P, P, P, ctypes.c_longlong, P, ctypes.c_longlong, P,
                               ctypes.c_longlong, P, P, ctypes.c_longlong, P]),
+    "ltq_ldlq_block_workspace_bytes": (SZ, [I] * 6),
+    "ltq_ldlq_block": (I, [P, LL, P, LL, P, P, LL, P, LL, P, LL, P, P, LL, I, P, P, I, I, P] + [I] * 6 + [P, SZ, P]),
     # allocation-free variant (scratch inside the library): same arguments without the workspace
     "ltq_viterbi_tb_noalloc_capacity": (SZ, []),
     "ltq_viterbi_tb_noalloc": (I, [P, P, I, P, P, P, P, P, P] + [I] * 5 + [P] + [I] * 10 + [P]),

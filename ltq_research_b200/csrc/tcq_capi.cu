@@ -62,6 +62,7 @@ static int run_pass(VitParams p, int pp, cudaStream_t st)
 {
     p.W4 = words_per_group(pp);
     p.NB = gsel_planes(p.G);
+    p.nsl = p.T / p.sub;
     if (p.N <= 0) return (int)cudaErrorInvalidConfiguration;  // the reference launches an empty grid: error 9
     const int rc = dispatch(p, pp, st);
     if (rc != 0) return rc;
@@ -178,5 +179,120 @@ extern "C" int ltq_viterbi_tb(const float* x, const float* w, int w_stride, cons
         rc = run_pass(q, pp, st);
         if (rc != 0) return rc;
     }
+    return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------
+// fused LDLQ block (ldlq_block_kernel): workspace layout per tile group and the C ABI
+// ------------------------------------------------------------------------------------------------
+namespace ltqb {
+
+struct LdlqWs {
+    size_t sv, gsw, gc, mid, best, x, rec, code, wsub, dwr, total;
+};
+
+static LdlqWs ldlq_ws(int N, int Gm, int sub, int pp)
+{
+    LdlqWs L{};
+    size_t o = 0;
+    L.sv = o; o += al256((size_t)N * Gm * (size_t)sv_words(256, pp) * 4);
+    L.gsw = o; o += al256((size_t)N * (256 / sub) * 512);
+    L.gc = o; o += al256((size_t)N * (256 / sub) * Gm);
+    L.mid = o; o += al256((size_t)N * 4);
+    L.best = o; o += al256((size_t)N * 4);
+    L.x = o; o += al256((size_t)N * 256 * 4);
+    L.rec = o; o += al256((size_t)N * 256 * 4);
+    L.code = o; o += al256((size_t)N * 256 * 4);
+    L.wsub = o; o += al256((size_t)N * 16 * 256 * 4);
+    L.dwr = o; o += al256(16 * 256 * 4);
+    L.total = o;
+    return L;
+}
+
+static int ldlq_dispatch(const LdlqParams& q, int pp, int smem, int grid, cudaStream_t st)
+{
+    const VitParams& p = q.p2;
+    if (p.m == 359) {
+        if (p.nl == 4) return ldlq_ct_m359(q, pp, smem, grid, st);
+        if (p.nl == 8) {
+            if (p.m2 == 241) return ldlq_ct_m359_241(q, pp, smem, grid, st);
+            if (p.m2 == 462) return ldlq_ct_m359_462(q, pp, smem, grid, st);
+            if (p.m2 == 146) return ldlq_ct_m359_146(q, pp, smem, grid, st);
+        }
+        if (p.nl == 16) {
+            if (p.m2 == 58 && p.m3 == 299) return ldlq_ct_m359_58_299(q, pp, smem, grid, st);
+            if (p.m2 == 211 && p.m3 == 397) return ldlq_ct_m359_211_397(q, pp, smem, grid, st);
+            if (p.m2 == 40 && p.m3 == 475) return ldlq_ct_m359_40_475(q, pp, smem, grid, st);
+        }
+    }
+    return ldlq_rt(q, pp, smem, grid, st);
+}
+
+}  // namespace ltqb
+
+extern "C" size_t ltq_ldlq_block_workspace_bytes(int M, int Gfull, int n_cand, int sub, int pp, int tb_window)
+{
+    (void)tb_window;
+    if (M <= 0 || M % 16 || sub <= 0 || Gfull <= 0) return 0;
+    const int G = (n_cand > 0 && n_cand < Gfull) ? n_cand : Gfull;
+    return ldlq_ws(M / 16, G, sub, pp).total;
+}
+
+extern "C" int ltq_ldlq_block(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* dw,
+                              const float* U, long long ldU, const float* Uinv, long long ldUi, float* G, long long ldG,
+                              int16_t* idx, uint8_t* gi, long long ldP, int M, const float* tab, const float* gains,
+                              int K, int m, const int* m_extra, int n_extra, int Gfull, int n_cand, int sub, int pp,
+                              int tb_window, void* workspace, size_t workspace_bytes, void* stream)
+{
+    constexpr int T = 256, h = T / 2;
+    if (M < 0 || M % 16 || K < 1 || K > 8 || n_extra < 0 || n_extra > 2 || (n_extra > 0 && !m_extra) ||
+        tb_window < 0 || tb_window > h || !w_blk || !d_rb || !dw || !U || !Uinv || !G || !idx || !gi || !tab ||
+        !gains || ld_w < T || ld_d < 1 || ldU < T || ldUi < T || ldG < T || ldP < T || ((uintptr_t)w_blk & 15) ||
+        (ld_w % 4) || sub % 4)
+        return -1;
+    const int U_ = 1 << (K - 1), nl = 4 << n_extra;
+    const int Gr = (n_cand > 0 && n_cand < Gfull) ? n_cand : Gfull;
+    const int T1 = tb_window ? 2 * tb_window : T;
+    if (Gr > 4) return -1;  // one CTA of at most 4 warps per tile group
+    if (!valid(1, T, 1024, U_, Gr, Gfull, Gr < Gfull, sub, U_, 0, nl, T, pp)) return -1;
+    if (!valid(1, T1, 1024, U_, Gr, Gfull, Gr < Gfull, sub, U_, 0, nl, T, pp)) return -1;
+    if (M == 0) return 0;
+    const int N = M / 16;
+    const LdlqWs L = ldlq_ws(N, Gr, sub, pp);
+    if (!workspace || workspace_bytes < L.total || ((uintptr_t)workspace & 255)) return -1;
+    char* ws = static_cast<char*>(workspace);
+    cudaStream_t st = (cudaStream_t)stream;
+
+    VitParams p{};
+    p.tab = tab; p.gains = gains; p.tab_hi = tab; p.gains_hi = gains;
+    p.best = reinterpret_cast<int*>(ws + L.best);
+    p.gsw = reinterpret_cast<uint32_t*>(ws + L.gsw);
+    p.N = N; p.T = T; p.U = U_; p.Gfull = Gfull; p.sub = sub; p.U_hi = U_; p.mix = 0; p.ld = T; p.ldw = 0;
+    p.m = m; p.m2 = n_extra > 0 ? m_extra[0] : 0; p.m3 = n_extra > 1 ? m_extra[1] : 0; p.m4 = 0; p.nl = nl;
+    p.svA = reinterpret_cast<uint32_t*>(ws + L.sv); p.svB = p.svA; p.capA = sv_words(T, pp); p.capB = 0;
+    p.W4 = words_per_group(pp); p.NB = gsel_planes(Gr);
+    p.nsl = T / sub;  // both passes index gsw / gcand rows with the full tile's stride
+    p.G = Gr; p.cand = Gr < Gfull; p.gcand = p.cand ? reinterpret_cast<uint8_t*>(ws + L.gc) : nullptr;
+    p.x = reinterpret_cast<float*>(ws + L.x);
+    p.rec = reinterpret_cast<float*>(ws + L.rec);
+    int* mid = reinterpret_cast<int*>(ws + L.mid);
+
+    LdlqParams q{};
+    q.p1 = p;  // free start; the window [h - W, h + W), or the whole tile when W = 0
+    q.p1.T = T1; q.p1.rot = tb_window ? h - tb_window : 0; q.p1.mid_t = tb_window ? tb_window : h; q.p1.mid_st = mid;
+    q.p1.init_st = nullptr; q.p1.tail = 0; q.p1.code = nullptr;
+    q.p2 = p;  // rotated by h, start = end = the middle state
+    q.p2.rot = h; q.p2.init_st = mid; q.p2.tail = 1; q.p2.mid_st = nullptr; q.p2.mid_t = 0;
+    q.p2.code = reinterpret_cast<int*>(ws + L.code);
+    q.wblk = w_blk; q.ldw = ld_w; q.wsub = reinterpret_cast<float*>(ws + L.wsub);
+    q.d_rb = d_rb; q.ldd = ld_d; q.dwrows = reinterpret_cast<float*>(ws + L.dwr);
+    q.U = U; q.ldU = ldU; q.Ui = Uinv; q.ldUi = ldUi; q.G = G; q.ldG = ldG; q.idx = idx; q.gi = gi; q.ldP = ldP;
+    q.xbuf = reinterpret_cast<float*>(ws + L.x); q.recbuf = reinterpret_cast<float*>(ws + L.rec);
+    q.codebuf = reinterpret_cast<int*>(ws + L.code);
+    const int smem = ldlq_smem(q.p1, q.p2, pp ? 2 : 1, &q.fb_off);
+
+    ldlq_dwrows_kernel<<<16, 256, 0, st>>>(dw, const_cast<float*>(q.dwrows));
+    const int rc = ldlq_dispatch(q, pp, smem, N, st);
+    if (rc != 0) return rc;
     return (int)cudaGetLastError();
 }

@@ -54,6 +54,7 @@ struct VitParams {
     int W4;                // survivor words per 4-step group
     int NB;                // gsel bit planes
     int cand;
+    int nsl;               // row stride of gsw and gcand in sub-blocks per tile (>= T / sub)
 };
 
 // ------------------------------------------------------------------------------------------------
@@ -575,15 +576,16 @@ static __device__ __noinline__ void build_err(float* myerr, const float* s_x, co
 // forward kernel
 // SUB2: sub-block boundaries may fall in the middle of a 4-step group (sub = 2 mod 4; plain and D2 only).
 // ------------------------------------------------------------------------------------------------
-// Plain mode is capped at 85 registers (3 x 256 threads per SM) so that 6 four-slot tiles fit per SM.
+// One forward pass over tile n by the CTA's G warps (blockDim.x = 32 G).  The tile's samples are xrow[(t + rot) % ld]
+// and its weights wrow[(t + rot) % ld].  Ends with p.best[n] written by thread 0 (no trailing barrier).
 template <class MP, int MD, bool SUB2>
-__global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const VitParams p)
+__device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, unsigned char* smem, const float* xrow,
+                                             const float* wrow)
 {
     constexpr int NL = MP::NL, NP = MD ? 2 : 1, NV = NL / 2, EW = NL * NP;
     constexpr bool PP = MD == 1, G4 = MD >= 2, EQ = MD == 3;
-    extern __shared__ __align__(16) unsigned char smem[];
     const int T = p.T, G = p.G, sub = p.sub, nsub = T / sub, U = p.U, U_hi = p.U_hi, mix = p.mix, Gf = p.Gfull;
-    const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, g = tid >> 5, nthr = blockDim.x;
+    const int tid = threadIdx.x, lane = tid & 31, g = tid >> 5, nthr = blockDim.x;
     const FwdSmem SL = fwd_smem(T, G, Gf, sub, NL, NP, U, U_hi);
     float* s_x = reinterpret_cast<float*>(smem + SL.x);
     float* s_w = reinterpret_cast<float*>(smem + SL.w);
@@ -602,8 +604,8 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const Vit
     // ---- tile inputs (sample t is element (t + rot) % ld), tables, gains ----
     for (int i = tid; i < T; i += nthr) {
         const int j = (i + p.rot) % p.ld;
-        s_x[i] = p.x[(size_t)n * p.ld + j];
-        s_w[i] = p.w[(size_t)n * p.ldw + j];
+        s_x[i] = xrow[j];
+        s_w[i] = wrow[j];
     }
     for (int i = tid; i < NL * U; i += nthr) s_tab[i] = p.tab[i];
     for (int i = tid; i < NL * U_hi; i += nthr) s_tabhi[i] = p.tab_hi[i];
@@ -633,7 +635,7 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const Vit
                     if (!((used >> gi) & 1u) && s_ce[tid * Gf + gi] < be) { be = s_ce[tid * Gf + gi]; bg = gi; }
                 used |= 1u << bg;
                 s_gc[tid * G + c] = (uint8_t)bg;
-                p.gcand[((size_t)n * nsub + tid) * G + c] = (uint8_t)bg;
+                p.gcand[((size_t)n * p.nsl + tid) * G + c] = (uint8_t)bg;
             }
         }
         __syncthreads();
@@ -677,7 +679,7 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const Vit
         __syncwarp();
         cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; mydp[swz(state_of(jf, lane, r))] = cur[r]; });
         __syncthreads();
-        merge_any(G, s_dp, s_mg, p.gsw + ((size_t)n * nsub + sb) * (NS / 8));
+        merge_any(G, s_dp, s_mg, p.gsw + ((size_t)n * p.nsl + sb) * (NS / 8));
         __syncthreads();
         cfor<0, 32, 1>([&](auto R) { constexpr int r = decltype(R)::value; cur[r] = s_mg[swz(state_of(jt, lane, r))]; });
     };
@@ -766,7 +768,7 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const Vit
             tt = 0;
             if (G > 1) {
                 __syncthreads();
-                merge_any(G, s_dp, s_mg, p.gsw + ((size_t)n * nsub + sb) * (NS / 8));
+                merge_any(G, s_dp, s_mg, p.gsw + ((size_t)n * p.nsl + sb) * (NS / 8));
                 __syncthreads();
                 src = s_mg;
             }
@@ -802,34 +804,34 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const Vit
     }
 }
 
+// Plain mode is capped at 85 registers (3 x 256 threads per SM) so that 6 four-slot tiles fit per SM.
+template <class MP, int MD, bool SUB2>
+__global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const VitParams p)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int n = blockIdx.x;
+    vit_fwd_tile<MP, MD, SUB2>(p, n, smem, p.x + (size_t)n * p.ld, p.w + (size_t)n * p.ldw);
+}
+
 // ------------------------------------------------------------------------------------------------
 // traceback, reconstruction and codes (src/cuda/tcq_viterbi.cu:580-682), one warp per tile
 // ------------------------------------------------------------------------------------------------
+// Traceback of tile n by one warp.  Tables and gains are in shared memory (s_tab ...); `wbase` is the warp's region of
+// the TbSmem per-warp layout; the tile's samples are xrow[(t + rot) % ld].
 template <int MD>
-__global__ void __launch_bounds__(32 * TB_WARPS) vit_tb_kernel(const VitParams p)
+__device__ __forceinline__ void vit_tb_tile(const VitParams& p, const int n, const int lane, const float* s_tab,
+                                            const float* s_tabhi, const float* s_gain, const float* s_gainhi,
+                                            unsigned char* wbase, const float* xrow)
 {
     constexpr bool PP = MD == 1, EQ = MD == 3;
-    extern __shared__ __align__(16) unsigned char smem[];
     const int T = p.T, G = p.G, sub = p.sub, nsub = T / sub, U = p.U, U_hi = p.U_hi, mix = p.mix, NL = p.nl;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
-    const int n = blockIdx.x * wpb + warp;
-    const TbSmem SL = tb_smem(T, sub, NL, U, U_hi, p.W4, p.NB, wpb);
-    float* s_tab = reinterpret_cast<float*>(smem + SL.tab);
-    float* s_tabhi = reinterpret_cast<float*>(smem + SL.tabhi);
-    float* s_gain = reinterpret_cast<float*>(smem + SL.gain);
-    float* s_gainhi = reinterpret_cast<float*>(smem + SL.gainhi);
-    unsigned char* wbase = smem + SL.warp + (size_t)warp * SL.per_warp;
+    const TbSmem SL = tb_smem(T, sub, NL, U, U_hi, p.W4, p.NB, 1);
     uint32_t* s_tbw = reinterpret_cast<uint32_t*>(wbase + SL.tbw);
     uint32_t* s_tbg = reinterpret_cast<uint32_t*>(wbase + SL.tbg);
     uint16_t* s_st = reinterpret_cast<uint16_t*>(wbase + SL.st);
     uint8_t* s_sg = wbase + SL.sg;
     uint8_t* s_par = wbase + SL.par;
     int* s_flag = reinterpret_cast<int*>(wbase + SL.flag);
-    for (int i = threadIdx.x; i < NL * U; i += blockDim.x) s_tab[i] = p.tab[i];
-    for (int i = threadIdx.x; i < NL * U_hi; i += blockDim.x) s_tabhi[i] = p.tab_hi[i];
-    if (threadIdx.x < p.Gfull) { s_gain[threadIdx.x] = p.gains[threadIdx.x]; s_gainhi[threadIdx.x] = p.gains_hi[threadIdx.x]; }
-    __syncthreads();
-    if (n >= p.N) return;
 
     if (lane == 0) {
         const int bi = p.best[n];
@@ -849,7 +851,7 @@ __global__ void __launch_bounds__(32 * TB_WARPS) vit_tb_kernel(const VitParams p
                 s_tbw[((grp - grp0) * p.W4 + k) * 32 + lane] = svg.get(((long long)grp * p.W4 + k) * 32 + lane);
         }
         if (G > 1 && lo > 0)
-            for (int k = lane; k < NS / 8; k += 32) s_tbg[k] = p.gsw[((size_t)n * nsub + lo / sub) * (NS / 8) + k];
+            for (int k = lane; k < NS / 8; k += 32) s_tbg[k] = p.gsw[((size_t)n * p.nsl + lo / sub) * (NS / 8) + k];
         __syncwarp();
         if (lane == 0) {
             int st = s_flag[0], gs = s_flag[1], pcur = 0, cstar = 0;
@@ -918,11 +920,11 @@ __global__ void __launch_bounds__(32 * TB_WARPS) vit_tb_kernel(const VitParams p
         const int lb = label_rt(stt, p);
         const bool hi = mix > 0 && ((t / mix) & 1);
         const int Ut = hi ? U_hi : U;
-        const int gi = p.cand ? (int)p.gcand[((size_t)n * nsub + t / sub) * G + gg] : gg;
+        const int gi = p.cand ? (int)p.gcand[((size_t)n * p.nsl + t / sub) * G + gg] : gg;
         const float gt = hi ? s_gainhi[gi] : s_gain[gi];
         const float* tt = (hi ? s_tabhi : s_tab) + lb * Ut;
         const int tp = (t + p.rot) % p.ld;
-        const float xt = p.x[(size_t)n * p.ld + tp];
+        const float xt = xrow[tp];
         float bestd = BIG, val = 0.f;
         int bu = 0;
         for (int u = MD ? s_par[t] : 0; u < Ut; u += MD ? 2 : 1) {
@@ -934,6 +936,26 @@ __global__ void __launch_bounds__(32 * TB_WARPS) vit_tb_kernel(const VitParams p
         rn[tp] = val;
         if (p.code) p.code[(size_t)n * p.ld + tp] = (gi << 16) | (lb * Ut + bu);
     }
+}
+
+template <int MD>
+__global__ void __launch_bounds__(32 * TB_WARPS) vit_tb_kernel(const VitParams p)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+    const int n = blockIdx.x * wpb + warp;
+    const TbSmem SL = tb_smem(p.T, p.sub, p.nl, p.U, p.U_hi, p.W4, p.NB, wpb);
+    float* s_tab = reinterpret_cast<float*>(smem + SL.tab);
+    float* s_tabhi = reinterpret_cast<float*>(smem + SL.tabhi);
+    float* s_gain = reinterpret_cast<float*>(smem + SL.gain);
+    float* s_gainhi = reinterpret_cast<float*>(smem + SL.gainhi);
+    for (int i = threadIdx.x; i < p.nl * p.U; i += blockDim.x) s_tab[i] = p.tab[i];
+    for (int i = threadIdx.x; i < p.nl * p.U_hi; i += blockDim.x) s_tabhi[i] = p.tab_hi[i];
+    if (threadIdx.x < p.Gfull) { s_gain[threadIdx.x] = p.gains[threadIdx.x]; s_gainhi[threadIdx.x] = p.gains_hi[threadIdx.x]; }
+    __syncthreads();
+    if (n >= p.N) return;
+    vit_tb_tile<MD>(p, n, lane, s_tab, s_tabhi, s_gain, s_gainhi, smem + SL.warp + (size_t)warp * SL.per_warp,
+                    p.x + (size_t)n * p.ld);
 }
 
 }  // namespace ltqb

@@ -1,6 +1,7 @@
 // Launch helpers for the Viterbi kernel instantiations (one translation unit per label-mask set).
 #pragma once
 #include <atomic>
+#include "ldlq_block_kernel.cuh"
 #include "tcq_viterbi_kernel.cuh"
 
 namespace ltqb {
@@ -58,6 +59,29 @@ inline int launch_md(const VitParams& p, int md, int smem, cudaStream_t st)
     }
 }
 
+// fused LDLQ block (one CTA of 32 G threads per 16-row tile group)
+template <class MP, int MD>
+inline int launch_ldlq_one(const LdlqParams& q, int smem, int grid, cudaStream_t st)
+{
+    auto k = ldlq_block_kernel<MP, MD>;
+    static std::atomic<int> done[64];
+    if (ensure_smem(k, smem, done) != 0) return -1;
+    k<<<grid, 32 * q.p2.G, smem, st>>>(q);
+    return 0;
+}
+
+template <class MP>
+inline int launch_ldlq_md(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st)
+{
+    switch (md) {
+        case 0: return launch_ldlq_one<MP, 0>(q, smem, grid, st);
+        case 1: return launch_ldlq_one<MP, 1>(q, smem, grid, st);
+        case 2: return launch_ldlq_one<MP, 2>(q, smem, grid, st);
+        case 3: return launch_ldlq_one<MP, 3>(q, smem, grid, st);
+        default: return -1;
+    }
+}
+
 // label-mask sets with compiled-in masks (every set used by the reference's format tables; primary mask 359)
 int launch_ct_m359(const VitParams& p, int md, int smem, cudaStream_t st);          // 4 subsets
 int launch_ct_m359_241(const VitParams& p, int md, int smem, cudaStream_t st);      // 8
@@ -69,5 +93,14 @@ int launch_ct_m359_40_475(const VitParams& p, int md, int smem, cudaStream_t st)
 int launch_rt(const VitParams& p, int md, int smem, cudaStream_t st);               // any masks, nl 4 / 8 / 16
 int launch_rt_sub2(const VitParams& p, int md, int smem, cudaStream_t st);          // any masks, sub = 2 mod 4
 int launch_tb(const VitParams& p, int md, cudaStream_t st);                          // traceback + reconstruction
+// fused LDLQ block, per label-mask set (same sets as the forward kernel)
+int ldlq_ct_m359(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
+int ldlq_ct_m359_241(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
+int ldlq_ct_m359_462(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
+int ldlq_ct_m359_146(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
+int ldlq_ct_m359_58_299(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
+int ldlq_ct_m359_211_397(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
+int ldlq_ct_m359_40_475(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
+int ldlq_rt(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
 
 }  // namespace ltqb

@@ -135,11 +135,46 @@ class _TcqRunner:
                                 ptr(self.ws), self.ws.numel(), _stream(self.dev)), "tcq_viterbi")
 
 
+class _BlockRunner:
+    """Per-format state of the fused block kernel (ltq_ldlq_block): tables, gains, masks and workspace."""
+
+    def __init__(self, spec: str, M: int, device):
+        cfg = TCQ_CONFIG[spec]
+        self.cfg = cfg
+        self.dev = device
+        self.M = M
+        self.lut = torch.tensor(cfg["lut"], dtype=torch.float32, device=device)
+        self.gains = make_gains(cfg["h"], cfg["step"], device).float().contiguous()
+        self.K = cfg["K"]
+        self.sub = cfg.get("sub", SUBBLOCK_SIZE)
+        self.pp = int(cfg.get("pp", 0))
+        self.m_extra = tuple(cfg.get("m_extra", ()))
+        self.me = torch.tensor(list(self.m_extra) + [0], dtype=torch.int32)
+        self.n_cand = int(os.environ.get("TCQ_NCAND", cfg.get("n_cand", 0)))
+        self.tb_window = int(os.environ.get("TCQ_TB_WIN", "32"))
+        wsb = _lib.lib().ltq_ldlq_block_workspace_bytes(M, self.gains.numel(), self.n_cand, self.sub, self.pp,
+                                                        self.tb_window)
+        self.ws = torch.empty(max(int(wsb), 256), dtype=torch.uint8, device=device)
+
+    def run(self, W_work, c0: int, d_rb_all, ibl: int, diag_w, Uc, U_blk_inv, G, idx, gi):
+        """Block [c0, c0 + 256): G / idx / gi of the block's columns (W_work is read, not written)."""
+        K = W_work.shape[1]
+        c = self.cfg
+        _check(_lib.lib().ltq_ldlq_block(
+            ptr(W_work) + 4 * c0, W_work.stride(0), ptr(d_rb_all) + 4 * ibl, d_rb_all.stride(0), ptr(diag_w) + 4 * c0,
+            ptr(Uc) + 4 * (c0 * Uc.stride(0) + c0), Uc.stride(0), ptr(U_blk_inv), U_blk_inv.stride(0),
+            ptr(G) + 4 * c0, G.stride(0), ptr(idx) + 2 * c0, ptr(gi) + c0, K, self.M, ptr(self.lut), ptr(self.gains),
+            self.K, c["m"], ctypes.cast(self.me.data_ptr(), ctypes.c_void_p), len(self.m_extra), self.gains.numel(),
+            self.n_cand, self.sub, self.pp, self.tb_window, ptr(self.ws), self.ws.numel(), _stream(self.dev)),
+            "ltq_ldlq_block")
+
+
 @torch.no_grad()
 def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: torch.Tensor, diag_w: torch.Tensor,
-                            spec_name: str, n_pass: int = 2) -> Tuple[torch.Tensor, torch.Tensor]:
+                            spec_name: str, n_pass: int = 2, fused: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
     """Block16-LDLQ with TCQ tiles, row-scale formats (src/liqk_v2.py:872-1021): returns (d_full fp16 [M, K/256],
-    W_hat_rot [M, K]); with PACK set, appends the group's codes to PACK["groups"]."""
+    W_hat_rot [M, K]); with PACK set, appends the group's codes to PACK["groups"].  fused: one ltq_ldlq_block launch per
+    256-column block; otherwise a gather, a two-pass Viterbi and a feedback launch per 16-column sub-block (same bits)."""
     cfg = TCQ_CONFIG[spec_name]
     if not (cfg.get("row_scale") and cfg.get("tb")):
         raise ValueError(f"{spec_name}: only the tail-biting row-scale (.ltq) TCQ formats are on this path")
@@ -164,8 +199,26 @@ def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: to
     _check(L.ltq_scale_fit(ptr(W_work), W_work.stride(0), M, K, float(cfg.get("scale", 1.0)), float(e_step), int(e_bits),
                            None, ptr(d_row), ptr(e_rb), ptr(d_rb_all), st), "ltq_scale_fit")
 
-    run = _TcqRunner(spec_name, M, device)
     Uc = U.contiguous()
+    if fused:
+        brun = _BlockRunner(spec_name, M, device)
+        dwc = diag_w.float().contiguous()
+        for ibl in range(nblocks):
+            c0, c1 = ibl * QK_K, (ibl + 1) * QK_K
+            U_blk_inv = U_blks_inv[ibl].contiguous()
+            brun.run(W_work, c0, d_rb_all, ibl, dwc, Uc, U_blk_inv, G, idx, gi)
+            d_rb = d_rb_all[:, ibl].clamp(min=1e-8)
+            best_what_row = d_rb.unsqueeze(1) * G[:, c0:c1]
+            W_hat_rot[:, c0:c1] = best_what_row
+            d_full[:, ibl] = d_rb.to(torch.float16)
+            if c1 < K:
+                err_blk = (W_work[:, c0:c1] - best_what_row) @ U_blk_inv
+                W_work[:, c1:] -= err_blk @ Uc[c0:c1, c1:]
+        if PACK is not None:
+            PACK["groups"].append({"spec": spec_name, "d_row": d_row, "e": e_rb, "idx": idx, "gi": gi, "G": G})
+        return d_full, W_hat_rot
+
+    run = _TcqRunner(spec_name, M, device)
     for ibl in range(nblocks):
         c0, c1 = ibl * QK_K, (ibl + 1) * QK_K
         w_blk_start = W_work[:, c0:c1].clone()

@@ -189,3 +189,54 @@ def test_make_gains_cpu_vs_cuda(cuda_dev):
         b = make_gains(c["h"], c["step"], cuda_dev).cpu()
         diff += int((a != b).sum())
     assert diff >= 0
+
+
+def _ldlq_inputs(M, K, seed, dev, damp=0.2):
+    """W_rot, U, U_blks_inv, diag_w as quantize_matrix_liqk_v2 prepares them (src/liqk_v2.py:1064-1088)."""
+    from ltq_research_b200.liqk_v2 import compute_optimal_suh
+    W, H = synth(M, K, seed)
+    W_rot, H_rot, _ = compute_optimal_suh(W.to(dev), H.to(dev).float(), seed=1337)
+    H_reg = H_rot.float().clone()
+    H_reg.diagonal().add_(damp * H_reg.diagonal().mean().clamp(min=1e-8))
+    Lf = torch.linalg.cholesky(H_reg.flip(0, 1))
+    U = torch.linalg.solve_triangular(Lf, torch.eye(K, device=dev), upper=False).flip(0, 1)
+    diag_w = 1.0 / (torch.diagonal(U) ** 2).clamp(min=1e-12)
+    nb = K // 256
+    U_blks = torch.stack([U[b * 256:(b + 1) * 256, b * 256:(b + 1) * 256] for b in range(nb)])
+    U_blks_inv = torch.linalg.solve_triangular(U_blks, torch.eye(256, device=dev).expand(nb, -1, -1), upper=True)
+    return W_rot, U, U_blks_inv, diag_w
+
+
+FUSED_FORMATS = ["TCQ2X0", "TCQ2X", "TCQ3X", "TCQ3X3", "TCQ4W2", "TCQ25X", "TCQ275X2", "TCQ225X", "TCQ3Y2", "TCQ5X",
+                 "RT_MASK"]
+
+
+@pytest.mark.parametrize("spec", FUSED_FORMATS)
+def test_ldlq_fused_block_equals_per_subblock(spec, cuda_dev, monkeypatch):
+    """The fused block kernel (ltq_ldlq_block, one launch per 256 columns) against the per-sub-block launches
+    (ltq_ldlq_gather + ltq_viterbi_tb + ltq_ldlq_feedback): codes, levels, scales and W_hat bit-identical.  Formats cover
+    G = 1 / 2 / 4, gain candidates (4 of 8, 4 of 16), sub = 32, D2 / D4 / EQ, 4 / 8 / 16 subsets and run-time masks."""
+    import ltq_research_b200.liqk_v2 as L
+    if spec == "RT_MASK":  # label masks outside the compiled sets take the run-time-mask instantiation
+        cfg = dict(L.TCQ_CONFIG["TCQ3X"])
+        cfg["m_extra"] = (123,)
+        monkeypatch.setitem(L.TCQ_CONFIG, spec, cfg)
+    M, K = 64, 512
+    W_rot, U, Ubi, dw = _ldlq_inputs(M, K, 11, cuda_dev)
+    outs = []
+    for fused in (True, False):
+        L.PACK = {"groups": []}
+        try:
+            d_full, W_hat = L._quantize_rows_tcq_ldlq(W_rot, U, Ubi, dw, spec, fused=fused)
+            g = L.PACK["groups"][-1]
+        finally:
+            L.PACK = None
+        outs.append((d_full, W_hat, g["idx"], g["gi"], g["G"], g["e"], g["d_row"]))
+    for a, b, what in zip(outs[0], outs[1], ("d_full", "W_hat", "idx", "gi", "G", "e", "d_row")):
+        assert torch.equal(a, b), (spec, what)
+    # the codes decode to the levels (gain table x lut)
+    cfg = L.TCQ_CONFIG[spec]
+    lut = torch.tensor(cfg["lut"], device=cuda_dev)
+    gains = L.make_gains(cfg["h"], cfg["step"], cuda_dev)
+    idx, gi, G = outs[0][2], outs[0][3], outs[0][4]
+    assert torch.equal(G, gains[gi.long()] * lut[idx.long()])
