@@ -109,6 +109,27 @@ int ltq_ldlq_block(const float* w_blk, long long ld_w, const float* d_rb, long l
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * .ltq tile packing and spec decode (src/ltq_file.py:54-148; tile fields src/ltq_format.py:104-147).  A row slice
+ * [R, K] (R, K multiples of 16) is (R/16)(K/16) tiles of 16 x 16; the packed slice is four structure-of-arrays regions
+ * (codes, planes, lsb, gains), each at a multiple of 64 bytes — byte for byte what the reference's pack_slice writes.
+ *   kbits: K of the format (2..8); frac: 0 none, 1 D2, 2 D4; h: gain-index bits (0..4); sub: weights per gain (16/32).
+ * ltq_slice_bytes: bytes of a packed slice (0 for unsupported parameters).
+ * ltq_pack_slice (replaces pack_slice, src/ltq_file.py:79-102): idx (label * U + u) int16 and gi uint8, [R, K] with row
+ *   stride ld (multiple of 8; idx 16-byte and gi 8-byte aligned) -> out (64-byte aligned, >= ltq_slice_bytes bytes).
+ * ltq_decode_slice (replaces decode_slice, src/ltq_file.py:119-148): the spec decode of a packed slice, value
+ *   gain_tab[g] * lut[label * U + u] with labels from the tail-biting code-bit states and the format's masks
+ *   (masks[0 .. n_masks-1], the primary mask first).  out [R, K] (stride ld_out) may be NULL; with ref (stride ld_ref),
+ *   adds to *mismatches the number of positions whose value differs from ref (the verify of LtqWriter.add_matrix,
+ *   src/ltq_file.py:204-207).
+ */
+size_t ltq_slice_bytes(int R, int K, int kbits, int frac, int h, int sub);
+int ltq_pack_slice(const int16_t* idx, const uint8_t* gi, long long ld, int R, int K, int kbits, int frac, int h,
+                   int sub, uint8_t* out, size_t out_bytes, void* stream);
+int ltq_decode_slice(const uint8_t* data, int R, int K, int kbits, int frac, int h, int sub, const int* masks,
+                     int n_masks, const float* lut, const float* gain_tab, float* out, long long ld_out,
+                     const float* ref, long long ld_ref, unsigned long long* mismatches, void* stream);
+
+/*
  * Allocation-free tail-biting Viterbi.  No counterpart in the reference (the reference's Python wrapper allocates all
  * scratch with torch); added for callers that cannot allocate device memory while they quantize — an engine that plans
  * its device memory at start-up and forbids allocation afterwards, or a binding (cgo / JNI / N-API / ctypes) that only

@@ -34,6 +34,10 @@ SIGNATURES = {
                               ctypes.c_longlong, P, P, ctypes.c_longlong, P]),
     "ltq_ldlq_block_workspace_bytes": (SZ, [I] * 6),
     "ltq_ldlq_block": (I, [P, LL, P, LL, P, P, LL, P, LL, P, LL, P, P, LL, I, P, P, I, I, P] + [I] * 6 + [P, SZ, P]),
+    # .ltq packing and spec decode
+    "ltq_slice_bytes": (SZ, [I] * 6),
+    "ltq_pack_slice": (I, [P, P, LL] + [I] * 6 + [P, SZ, P]),
+    "ltq_decode_slice": (I, [P] + [I] * 6 + [P, I, P, P, P, LL, P, LL, P, P]),
     # allocation-free variant (scratch inside the library): same arguments without the workspace
     "ltq_viterbi_tb_noalloc_capacity": (SZ, []),
     "ltq_viterbi_tb_noalloc": (I, [P, P, I, P, P, P, P, P, P] + [I] * 5 + [P] + [I] * 10 + [P]),

@@ -1,0 +1,130 @@
+"""Concurrent quantization of many matrices on one B200.
+
+The LDLQ sweep of one matrix is a chain of K/256 dependent block launches, each of M/16 CTAs that walk their rows
+through 16 sub-blocks one after another; a single matrix therefore occupies a fraction of the 148 SMs for a time set
+by its column count.  Independent matrices (the layers of a model, the experts of an MoE) are what fills the GPU: this
+driver runs each matrix's whole quantize_matrix_liqk_v2 computation (rotation, Hessian factorisation, LDLQ, refits,
+PACK fields) on one of several CUDA streams, with no host synchronisation until every matrix has been issued.  Matrices
+are assigned longest-first to the least-loaded stream.  Results are the reference function's, bit for bit: the same
+kernels and torch operations run on every stream.
+
+The reference quantizes matrices one at a time (src/hybrid_quant.py, src/streaming_quant.py call
+quantize_matrix_liqk_v2 per matrix, optionally from LIQK_PAR host threads); this is the single-process B200 form.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Sequence, Tuple, Union
+
+import torch
+
+from . import _lib
+from .formats import TCQ_CONFIG
+from .liqk_v2 import _quantize_matrix_steps
+
+Spec = Union[str, Sequence[Tuple[int, int, str]]]
+
+
+def _specs(spec: Spec) -> List[str]:
+    return [spec] if isinstance(spec, str) else [sp for _, _, sp in spec]
+
+
+def estimated_seconds(M: int, K: int, spec: Spec) -> float:
+    """Rough B200 time of one matrix, for the longest-first assignment: the Viterbi at ~1.1 G weights/s for a four-slot
+    plain format (scaled by slots x parity classes) plus the fp32 factorisations and refit products (~K^3 and M K^2)."""
+    t = 0.0
+    for sp in _specs(spec):
+        c = TCQ_CONFIG[sp]
+        g = 1 << c["h"]
+        if c.get("n_cand"):
+            g = min(g, int(c["n_cand"]))
+        t += M * K * g * (2 if c.get("pp") else 1) / 4.0 / 1.1e9 / len(_specs(spec))
+    return t + (3.0 * K ** 3 + 8.0 * M * K * K) / 50e12
+
+
+def _record(obj, stream: torch.cuda.Stream):
+    if torch.is_tensor(obj):
+        if obj.is_cuda:
+            obj.record_stream(stream)
+    elif isinstance(obj, dict):
+        for v in obj.values():
+            _record(v, stream)
+    elif isinstance(obj, (list, tuple)):
+        for v in obj:
+            _record(v, stream)
+
+
+@torch.no_grad()
+def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], seed: int = 1337, damp: float = 0.02,
+                      n_streams: int = 8, pack: bool = True, keep_w_hat: bool = False,
+                      device: Optional[torch.device] = None, on_issued=None) -> List[Dict]:
+    """Quantize every (W [M, K], H [K, K], spec) of `jobs` as quantize_matrix_liqk_v2(W, H, spec, seed, damp) would,
+    concurrently on `n_streams` CUDA streams.  W / H may be CUDA tensors or (pinned) host tensors, which are copied to
+    the device on the matrix's stream.  Returns, per job: {"qdata", "pack" (the PACK["matrix"] fields, device tensors)
+    when pack, "W_hat" when keep_w_hat, "rel_loss" (float)}.  One host synchronisation, after the last job is issued;
+    on_issued(i), if given, is called after job i has been issued (for overlapping host work).  Raises
+    torch.linalg.LinAlgError if a damped Hessian is not positive definite."""
+    if not jobs:
+        return []
+    dev = torch.device(device) if device is not None else None
+    for W, H, _ in jobs:
+        for t in (W, H):
+            if t.is_cuda:
+                dev = dev or t.device
+    if dev is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    if dev.type != "cuda":
+        raise RuntimeError("quantize_matrices: a CUDA device is required; there is no CPU path")
+    _lib.lib()
+    main = torch.cuda.current_stream(dev)
+    streams = [torch.cuda.Stream(dev) for _ in range(max(1, n_streams))]
+    cost = [estimated_seconds(W.shape[0], W.shape[1], sp) for W, _, sp in jobs]
+    pending = sorted(range(len(jobs)), key=lambda i: -cost[i])[::-1]  # pop() takes the longest remaining job
+    out: List[Optional[Dict]] = [None] * len(jobs)
+    # one job in issue per stream; each round advances every job by one step (Hessian preparation, one 256-column
+    # block, refits), so that every stream keeps work queued while the host is blocked on a full launch queue
+    active: List[Optional[tuple]] = [None] * len(streams)
+    while pending or any(a is not None for a in active):
+        for k, s in enumerate(streams):
+            if active[k] is None and pending:
+                i = pending.pop()
+                W, H, sp = jobs[i]
+                s.wait_stream(main)
+                with torch.cuda.stream(s):
+                    Wd = W.to(dev, non_blocking=True) if not W.is_cuda else W
+                    Hd = H.to(dev, non_blocking=True) if not H.is_cuda else H
+                    if W.is_cuda:
+                        W.record_stream(s)
+                    if H.is_cuda:
+                        H.record_stream(s)
+                active[k] = (i, _quantize_matrix_steps(Wd, Hd, sp, seed, damp, None, pack))
+            if active[k] is None:
+                continue
+            i, gen = active[k]
+            with torch.cuda.stream(s):
+                try:
+                    next(gen)
+                except StopIteration as e:
+                    r = e.value
+                    if not keep_w_hat:
+                        r.pop("W_hat")
+                    out[i] = r
+                    active[k] = None
+                    if on_issued is not None:
+                        on_issued(i)
+    for s in streams:
+        main.wait_stream(s)
+    for i, r in enumerate(out):
+        _record(r, main)
+    nd = torch.stack([torch.stack([r["num"], r["den"]]) for r in out]).cpu()
+    info = torch.stack([r["chol_info"].reshape(()) for r in out]).cpu()
+    res = []
+    for i, r in enumerate(out):
+        if int(info[i]) != 0:
+            raise torch.linalg.LinAlgError(f"quantize_matrices: job {i}: the damped Hessian is not positive-definite")
+        d = {"qdata": r["qdata"], "rel_loss": float(nd[i, 0]) / float(nd[i, 1])}
+        if pack:
+            d["pack"] = r["pack"]
+        if keep_w_hat:
+            d["W_hat"] = r["W_hat"]
+        res.append(d)
+    return res

@@ -799,6 +799,9 @@ __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, un
     if (tid == 0) {
         for (int k = 1; k < G; k++)
             if (red_v[k] < bv || (red_v[k] == bv && red_i[k] < bi)) { bv = red_v[k]; bi = red_i[k]; }
+        // No metric compared below 3.4e38 (all NaN or +inf, i.e. non-finite inputs): there is no best path.  Take slot 0
+        // and the required end state (or state 0) so that the traceback stays inside the tile's survivor rows.
+        if (bi == 0x7fffffff) bi = s_end >= 0 ? s_end : 0;
         p.best[n] = bi;
         if (p.end_st) p.end_st[n] = bi % NS;
     }

@@ -38,12 +38,24 @@ def _stream(dev) -> int:
     return _lib.stream_ptr(dev)
 
 
+_SIGNS: Dict[tuple, torch.Tensor] = {}
+
+
 def make_rademacher_signs(dim: int, seed: int, device) -> torch.Tensor:
-    """Deterministic +-1 signs from a CPU generator (src/iqk_format.py:173-179)."""
-    gen = torch.Generator(device="cpu")
-    gen.manual_seed(seed)
-    bits = torch.randint(0, 2, (dim,), generator=gen, dtype=torch.int64)
-    return (bits * 2 - 1).to(dtype=torch.float32, device=device)
+    """Deterministic +-1 signs from a CPU generator (src/iqk_format.py:173-179).  Device copies are cached, so a
+    quantization in flight on a side stream never waits on a pageable host-to-device copy."""
+    dev = torch.device(device)
+    key = (dim, seed, str(dev))
+    t = _SIGNS.get(key)
+    if t is None:
+        gen = torch.Generator(device="cpu")
+        gen.manual_seed(seed)
+        bits = torch.randint(0, 2, (dim,), generator=gen, dtype=torch.int64)
+        t = (bits * 2 - 1).to(dtype=torch.float32, device=dev)
+        if dev.type == "cuda":
+            torch.cuda.current_stream(dev).synchronize()
+        _SIGNS[key] = t
+    return t
 
 
 def fwht_rows_scaled(x: torch.Tensor, scale: Optional[torch.Tensor] = None, mode: int = 0,
@@ -99,59 +111,75 @@ def compute_optimal_suh(W: torch.Tensor, H: torch.Tensor, seed: int = 1337,
     return W_rot, H_rot, suh
 
 
-class _TcqRunner:
-    """Per-format state of the sub-block Viterbi calls: tables, gains, buffers and workspace reused across calls."""
+_TABLES: Dict[tuple, tuple] = {}
 
-    def __init__(self, spec: str, M: int, device):
+
+def _format_tables(spec: str, device) -> tuple:
+    """(lut, gains, m_extra host array) of a format on a device, cached per (format, device, gain function); the
+    first use synchronises once so that later uses never wait on a host-to-device copy."""
+    dev = torch.device(device)
+    key = (spec, str(dev), make_gains)
+    t = _TABLES.get(key)
+    if t is None:
+        cfg = TCQ_CONFIG[spec]
+        lut = torch.tensor(cfg["lut"], dtype=torch.float32, device=dev)
+        gains = make_gains(cfg["h"], cfg["step"], dev).float().contiguous()
+        me = torch.tensor(list(cfg.get("m_extra", ())) + [0], dtype=torch.int32)
+        if dev.type == "cuda":
+            torch.cuda.current_stream(dev).synchronize()
+        t = (lut, gains, me)
+        _TABLES[key] = t
+    return t
+
+
+class _FormatArgs:
+    """Viterbi parameters of a format: K, sub-block length, parity mode, label masks, gain candidates, TB window."""
+
+    def __init__(self, spec: str, device):
         cfg = TCQ_CONFIG[spec]
         self.cfg = cfg
         self.dev = device
-        self.nt = M // 16
-        self.lut = torch.tensor(cfg["lut"], dtype=torch.float32, device=device)
-        self.gains = make_gains(cfg["h"], cfg["step"], device).float().contiguous()
+        self.lut, self.gains, self.me = _format_tables(spec, device)
         self.K = cfg["K"]
         self.sub = cfg.get("sub", SUBBLOCK_SIZE)
         self.pp = int(cfg.get("pp", 0))
         self.m_extra = tuple(cfg.get("m_extra", ()))
-        self.me = torch.tensor(list(self.m_extra) + [0], dtype=torch.int32)
-        self.n_cand = int(os.environ.get("TCQ_NCAND", cfg.get("n_cand", 0)))
+        self.n_cand = int(os.environ.get("TCQ_NCAND", cfg.get("n_cand", 0) or 0))
         self.tb_window = int(os.environ.get("TCQ_TB_WIN", "32"))
+
+    def me_ptr(self):
+        return ctypes.cast(self.me.data_ptr(), ctypes.c_void_p)
+
+
+class _TcqRunner(_FormatArgs):
+    """Sub-block Viterbi calls (ltq_viterbi_tb) over the M/16 tiles of one sub-block: buffers and workspace."""
+
+    def __init__(self, spec: str, M: int, device):
+        super().__init__(spec, device)
+        self.nt = M // 16
         self.x = torch.empty((self.nt, 256), dtype=torch.float32, device=device)
         self.rec = torch.empty_like(self.x)
         self.code = torch.empty((self.nt, 256), dtype=torch.int32, device=device)
-        L = _lib.lib()
-        wsb = L.ltq_viterbi_tb_workspace_bytes(self.nt, 256, self.gains.numel(), self.n_cand, self.sub, self.pp,
-                                              self.tb_window, 0)
+        wsb = _lib.lib().ltq_viterbi_tb_workspace_bytes(self.nt, 256, self.gains.numel(), self.n_cand, self.sub,
+                                                        self.pp, self.tb_window, 0)
         self.ws = torch.empty(max(int(wsb), 256), dtype=torch.uint8, device=device)
 
     def run(self, dw256: torch.Tensor):
         """Tail-biting Viterbi of self.x (tiles of the current sub-block) with per-position weights dw256 [256]."""
-        L = _lib.lib()
         c = self.cfg
-        _check(L.ltq_viterbi_tb(ptr(self.x), ptr(dw256), 0, ptr(self.lut), ptr(self.gains), None, None, ptr(self.rec),
-                                ptr(self.code), self.nt, 256, c["nu"], self.K, c["m"],
-                                ctypes.cast(self.me.data_ptr(), ctypes.c_void_p), len(self.m_extra), self.gains.numel(),
-                                self.n_cand, self.sub, 1 << (self.K - 1), 0, self.pp, 2, 0, self.tb_window,
-                                ptr(self.ws), self.ws.numel(), _stream(self.dev)), "tcq_viterbi")
+        _check(_lib.lib().ltq_viterbi_tb(
+            ptr(self.x), ptr(dw256), 0, ptr(self.lut), ptr(self.gains), None, None, ptr(self.rec), ptr(self.code),
+            self.nt, 256, c["nu"], self.K, c["m"], self.me_ptr(), len(self.m_extra), self.gains.numel(), self.n_cand,
+            self.sub, 1 << (self.K - 1), 0, self.pp, 2, 0, self.tb_window, ptr(self.ws), self.ws.numel(),
+            _stream(self.dev)), "tcq_viterbi")
 
 
-class _BlockRunner:
-    """Per-format state of the fused block kernel (ltq_ldlq_block): tables, gains, masks and workspace."""
+class _BlockRunner(_FormatArgs):
+    """Fused block kernel (ltq_ldlq_block) over the M rows of one row group: workspace."""
 
     def __init__(self, spec: str, M: int, device):
-        cfg = TCQ_CONFIG[spec]
-        self.cfg = cfg
-        self.dev = device
+        super().__init__(spec, device)
         self.M = M
-        self.lut = torch.tensor(cfg["lut"], dtype=torch.float32, device=device)
-        self.gains = make_gains(cfg["h"], cfg["step"], device).float().contiguous()
-        self.K = cfg["K"]
-        self.sub = cfg.get("sub", SUBBLOCK_SIZE)
-        self.pp = int(cfg.get("pp", 0))
-        self.m_extra = tuple(cfg.get("m_extra", ()))
-        self.me = torch.tensor(list(self.m_extra) + [0], dtype=torch.int32)
-        self.n_cand = int(os.environ.get("TCQ_NCAND", cfg.get("n_cand", 0)))
-        self.tb_window = int(os.environ.get("TCQ_TB_WIN", "32"))
         wsb = _lib.lib().ltq_ldlq_block_workspace_bytes(M, self.gains.numel(), self.n_cand, self.sub, self.pp,
                                                         self.tb_window)
         self.ws = torch.empty(max(int(wsb), 256), dtype=torch.uint8, device=device)
@@ -159,22 +187,33 @@ class _BlockRunner:
     def run(self, W_work, c0: int, d_rb_all, ibl: int, diag_w, Uc, U_blk_inv, G, idx, gi):
         """Block [c0, c0 + 256): G / idx / gi of the block's columns (W_work is read, not written)."""
         K = W_work.shape[1]
-        c = self.cfg
         _check(_lib.lib().ltq_ldlq_block(
             ptr(W_work) + 4 * c0, W_work.stride(0), ptr(d_rb_all) + 4 * ibl, d_rb_all.stride(0), ptr(diag_w) + 4 * c0,
             ptr(Uc) + 4 * (c0 * Uc.stride(0) + c0), Uc.stride(0), ptr(U_blk_inv), U_blk_inv.stride(0),
             ptr(G) + 4 * c0, G.stride(0), ptr(idx) + 2 * c0, ptr(gi) + c0, K, self.M, ptr(self.lut), ptr(self.gains),
-            self.K, c["m"], ctypes.cast(self.me.data_ptr(), ctypes.c_void_p), len(self.m_extra), self.gains.numel(),
-            self.n_cand, self.sub, self.pp, self.tb_window, ptr(self.ws), self.ws.numel(), _stream(self.dev)),
-            "ltq_ldlq_block")
+            self.K, self.cfg["m"], self.me_ptr(), len(self.m_extra), self.gains.numel(), self.n_cand, self.sub,
+            self.pp, self.tb_window, ptr(self.ws), self.ws.numel(), _stream(self.dev)), "ltq_ldlq_block")
+
+
+def _drive(gen):
+    """Run a step generator to its end and return its value."""
+    while True:
+        try:
+            next(gen)
+        except StopIteration as e:
+            return e.value
 
 
 @torch.no_grad()
-def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: torch.Tensor, diag_w: torch.Tensor,
-                            spec_name: str, n_pass: int = 2, fused: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Block16-LDLQ with TCQ tiles, row-scale formats (src/liqk_v2.py:872-1021): returns (d_full fp16 [M, K/256],
-    W_hat_rot [M, K]); with PACK set, appends the group's codes to PACK["groups"].  fused: one ltq_ldlq_block launch per
-    256-column block; otherwise a gather, a two-pass Viterbi and a feedback launch per 16-column sub-block (same bits)."""
+def _rows_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: torch.Tensor, diag_w: torch.Tensor, spec_name: str,
+               fused: bool = True) -> Tuple[torch.Tensor, torch.Tensor, dict]:
+    """Block16-LDLQ of one row group (src/liqk_v2.py:872-1021, row-scale branch :956-980) on the current stream,
+    without host synchronisation.  Returns (d_full fp16 [M, K/256], W_hat_rot [M, K], group fields)."""
+    return _drive(_rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name, fused))
+
+
+def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool = True):
+    """_rows_ldlq as a generator that yields after each 256-column block's launches (for interleaved issue)."""
     cfg = TCQ_CONFIG[spec_name]
     if not (cfg.get("row_scale") and cfg.get("tb")):
         raise ValueError(f"{spec_name}: only the tail-biting row-scale (.ltq) TCQ formats are on this path")
@@ -198,6 +237,7 @@ def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: to
     d_rb_all = torch.empty((M, nblocks), dtype=torch.float32, device=device)
     _check(L.ltq_scale_fit(ptr(W_work), W_work.stride(0), M, K, float(cfg.get("scale", 1.0)), float(e_step), int(e_bits),
                            None, ptr(d_row), ptr(e_rb), ptr(d_rb_all), st), "ltq_scale_fit")
+    group = {"spec": spec_name, "d_row": d_row, "e": e_rb, "idx": idx, "gi": gi, "G": G}
 
     Uc = U.contiguous()
     if fused:
@@ -214,9 +254,8 @@ def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: to
             if c1 < K:
                 err_blk = (W_work[:, c0:c1] - best_what_row) @ U_blk_inv
                 W_work[:, c1:] -= err_blk @ Uc[c0:c1, c1:]
-        if PACK is not None:
-            PACK["groups"].append({"spec": spec_name, "d_row": d_row, "e": e_rb, "idx": idx, "gi": gi, "G": G})
-        return d_full, W_hat_rot
+            yield
+        return d_full, W_hat_rot, group
 
     run = _TcqRunner(spec_name, M, device)
     for ibl in range(nblocks):
@@ -242,27 +281,39 @@ def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: to
         if c1 < K:
             err_blk = (w_blk_start - best_what_row) @ U_blk_inv
             W_work[:, c1:] -= err_blk @ Uc[c0:c1, c1:]
+        yield
+    return d_full, W_hat_rot, group
+
+
+@torch.no_grad()
+def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: torch.Tensor, diag_w: torch.Tensor,
+                            spec_name: str, n_pass: int = 2, fused: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Block16-LDLQ with TCQ tiles, row-scale formats (src/liqk_v2.py:872-1021): returns (d_full fp16 [M, K/256],
+    W_hat_rot [M, K]); with PACK set, appends the group's codes to PACK["groups"].  fused: one ltq_ldlq_block launch per
+    256-column block; otherwise a gather, a two-pass Viterbi and a feedback launch per 16-column sub-block (same bits)."""
+    d_full, W_hat_rot, group = _rows_ldlq(W_rot, U, U_blks_inv, diag_w, spec_name, fused)
     if PACK is not None:
-        PACK["groups"].append({"spec": spec_name, "d_row": d_row, "e": e_rb, "idx": idx, "gi": gi, "G": G})
+        PACK["groups"].append(group)
     return d_full, W_hat_rot
 
 
 @torch.no_grad()
-def quantize_matrix_liqk_v2(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
-                            row_weights: Optional[torch.Tensor] = None, cd_sweeps: int = 2, out_rot: bool = False):
-    """src/liqk_v2.py:1029-1198 for the TCQ formats: returns (qdata, W_hat [M, K] fp32, rel_loss); with PACK set,
-    PACK["matrix"] holds the .ltq fields (row_slices, idx, gi, G, d_row fp16, e int8, suh fp16)."""
-    _lib.require_cuda(W, H)
-    if out_rot:
-        s_out = make_rademacher_signs(W.shape[0], seed=seed + 7919, device=W.device)
-        rw = None
-        if row_weights is not None:
-            rw = row_weights.float().view(-1, QK_K).mean(dim=1, keepdim=True).expand(-1, QK_K).reshape(-1)
-        q_res, w_hat_r, rel = quantize_matrix_liqk_v2(_fwht_rows(W.float() * s_out.unsqueeze(1)), H, spec_or_row_specs,
-                                                      seed=seed, damp=damp, row_weights=rw, cd_sweeps=cd_sweeps)
-        q_res["s_out"] = s_out.to(torch.int8)
-        return q_res, _fwht_rows(w_hat_r) * s_out.unsqueeze(1), rel
+def _quantize_matrix_core(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
+                          row_weights: Optional[torch.Tensor] = None, want_pack: bool = False,
+                          rows_fn=None) -> dict:
+    """_quantize_matrix_steps run to its end (see there)."""
+    return _drive(_quantize_matrix_steps(W, H, spec_or_row_specs, seed, damp, row_weights, want_pack, rows_fn))
 
+
+def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
+                           row_weights: Optional[torch.Tensor] = None, want_pack: bool = False, rows_fn=None):
+    """The computation of quantize_matrix_liqk_v2 (src/liqk_v2.py:1029-1198) for the TCQ formats, on the current
+    stream and without host synchronisation (with row_weights=None): the reference's data-dependent host branches
+    become device-side selections of the same tensors (torch.where), its raising Cholesky / solve their *_ex forms.
+    Returns device tensors: qdata, W_hat, num / den of the relative loss, chol_info, and with want_pack the .ltq fields.
+    rows_fn: the row-group quantizer called for each format's rows (default: the block-stepped _rows_ldlq).  A
+    generator: it yields after the Hessian preparation and after each 256-column block, so that a scheduler can
+    interleave the launches of several matrices on several streams; its return value is the result dict."""
     W_f32 = W.float()
     H_f32 = H.float()
     M, K = W_f32.shape
@@ -278,7 +329,7 @@ def quantize_matrix_liqk_v2(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs,
     H_reg = H_rot.float().clone()
     diag_mean = H_reg.diagonal().mean().clamp(min=1e-8)
     H_reg.diagonal().add_(damp * diag_mean)
-    L_flip = torch.linalg.cholesky(H_reg.flip(0, 1))
+    L_flip, chol_info = torch.linalg.cholesky_ex(H_reg.flip(0, 1))
     del H_rot, H_reg
     U = torch.linalg.solve_triangular(L_flip, torch.eye(K, dtype=L_flip.dtype, device=L_flip.device), upper=False)
     U = U.flip(0, 1)
@@ -287,6 +338,7 @@ def quantize_matrix_liqk_v2(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs,
     eye256 = torch.eye(QK_K, dtype=torch.float32, device=W.device).unsqueeze(0).expand(nblocks, -1, -1)
     U_blks = torch.stack([U[b * QK_K:(b + 1) * QK_K, b * QK_K:(b + 1) * QK_K] for b in range(nblocks)], dim=0)
     U_blks_inv = torch.linalg.solve_triangular(U_blks, eye256, upper=True)
+    yield
 
     row_slices = [(0, M, spec_or_row_specs)] if isinstance(spec_or_row_specs, str) else spec_or_row_specs
     by_spec: Dict[str, List[Tuple[int, int]]] = {}
@@ -295,21 +347,35 @@ def quantize_matrix_liqk_v2(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs,
 
     W_hat_rot = torch.empty_like(W_rot)
     d_full = torch.empty((M, nblocks), dtype=torch.float16, device=W.device)
-    if PACK is not None:
-        PACK["groups"] = []
+    pm = None
+    if want_pack:
         pm = {"idx": torch.empty((M, K), dtype=torch.int16, device=W.device),
               "gi": torch.empty((M, K), dtype=torch.uint8, device=W.device),
               "G": torch.empty((M, K), dtype=torch.float32, device=W.device), "d_row": torch.empty(M, device=W.device),
               "e": torch.empty((M, nblocks), dtype=torch.int8, device=W.device)}
     for sp, ranges in by_spec.items():
+        if len(ranges) == 1 and ranges[0] == (0, M):
+            rows_idx = None
+            if rows_fn is None:
+                d_sub, Wh_sub, g = yield from _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, sp)
+            else:
+                d_sub, Wh_sub, g = rows_fn(W_rot, U, U_blks_inv, diag_w, sp)
+            W_hat_rot, d_full = Wh_sub, d_sub
+            if pm is not None:
+                for k in ("idx", "gi", "G", "d_row", "e"):
+                    pm[k] = g[k].to(pm[k].dtype)
+            continue
         rows_idx = torch.cat([torch.arange(r0, r1, device=W.device) for r0, r1 in ranges], dim=0)
-        d_sub, Wh_sub = _quantize_rows_tcq_ldlq(W_rot[rows_idx], U, U_blks_inv, diag_w, sp)
+        if rows_fn is None:
+            d_sub, Wh_sub, g = yield from _rows_ldlq_steps(W_rot[rows_idx], U, U_blks_inv, diag_w, sp)
+        else:
+            d_sub, Wh_sub, g = rows_fn(W_rot[rows_idx], U, U_blks_inv, diag_w, sp)
         W_hat_rot[rows_idx] = Wh_sub
         d_full[rows_idx] = d_sub
-        if PACK is not None:
-            g = PACK["groups"].pop()
+        if pm is not None:
             for k in ("idx", "gi", "G", "d_row", "e"):
                 pm[k][rows_idx] = g[k].to(pm[k].dtype)
+    del U, U_blks_inv, W_rot
 
     U_base = fwht_inplace(W_hat_rot.clone(), block_size=QK_K)
     W_hat_eff = U_base * suh.unsqueeze(0)
@@ -331,32 +397,72 @@ def quantize_matrix_liqk_v2(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs,
     A_in = (U_w.T @ U_scaled) * H_f32
     b_in = (U_w * HW).sum(dim=0)
     A_in.diagonal().add_(1e-3 * A_in.diagonal().mean().clamp(min=1e-12))
-    try:
-        suh_cand = torch.linalg.solve(A_in, b_in).to(torch.float16).to(torch.float32)
-        valid_s = torch.isfinite(suh_cand) & (suh_cand.abs() > 0.05) & (suh_cand.abs() < 10.0)
-        suh_cand = torch.where(valid_s, suh_cand, suh)
-        W_hat_cand = U_scaled * suh_cand.unsqueeze(0)
-        HQ_cand = W_hat_cand @ H_f32
-        diff_base = W_f32 - W_hat_eff
-        diff_cand = W_f32 - W_hat_cand
-        loss_base = float((((HW - HQ) * diff_base).sum(dim=1) * rw).sum().item())
-        loss_cand = float((((HW - HQ_cand) * diff_cand).sum(dim=1) * rw).sum().item())
-        if loss_cand < loss_base:
-            W_hat_eff, d_full, suh, HQ, c_pack = W_hat_cand, d_new, suh_cand, HQ_cand, c_eff.squeeze(1)
-    except RuntimeError:
-        pass
-    if PACK is not None:
+    # the reference solves, and keeps the refit when the solve succeeds and lowers the loss (src/liqk_v2.py:1161-1180)
+    sol, solve_info = torch.linalg.solve_ex(A_in, b_in)
+    suh_cand = sol.to(torch.float16).to(torch.float32)
+    valid_s = torch.isfinite(suh_cand) & (suh_cand.abs() > 0.05) & (suh_cand.abs() < 10.0)
+    suh_cand = torch.where(valid_s, suh_cand, suh)
+    W_hat_cand = U_scaled * suh_cand.unsqueeze(0)
+    HQ_cand = W_hat_cand @ H_f32
+    diff_base = W_f32 - W_hat_eff
+    diff_cand = W_f32 - W_hat_cand
+    loss_base = (((HW - HQ) * diff_base).sum(dim=1) * rw).sum()
+    loss_cand = (((HW - HQ_cand) * diff_cand).sum(dim=1) * rw).sum()
+    take = (solve_info == 0) & (loss_cand < loss_base)
+    W_hat_eff = torch.where(take, W_hat_cand, W_hat_eff)
+    d_full = torch.where(take, d_new, d_full)
+    suh = torch.where(take, suh_cand, suh)
+    HQ = torch.where(take, HQ_cand, HQ)
+    c_pack = torch.where(take, c_eff.squeeze(1), c_pack)
+    del W_hat_cand, HQ_cand, diff_base, diff_cand, U_scaled, U_w, A_in
+    pack = None
+    if pm is not None:
         d_row_p = (pm["d_row"] * c_pack).to(torch.float16)
         suh_p = suh.to(torch.float16)
         scale = d_row_p.float().unsqueeze(1) * torch.exp2(0.25 * pm["e"].float())
         Wq_rot = (scale.unsqueeze(2) * pm["G"].view(M, nblocks, QK_K)).view(M, K)
         W_hat_eff = fwht_inplace(Wq_rot, block_size=QK_K) * suh_p.float().unsqueeze(0)
         HQ = W_hat_eff @ H_f32
-        PACK["matrix"] = {"row_slices": row_slices, "idx": pm["idx"], "gi": pm["gi"], "G": pm["G"], "d_row": d_row_p,
-                          "e": pm["e"], "suh": suh_p}
+        pack = {"row_slices": row_slices, "idx": pm["idx"], "gi": pm["gi"], "G": pm["G"], "d_row": d_row_p,
+                "e": pm["e"], "suh": suh_p}
     diff = W_f32 - W_hat_eff
-    num_loss = float(((HW - HQ) * diff).sum().item())
-    den_loss = float((HW * W_f32).sum().clamp(min=1e-12).item())
-    rel_loss = num_loss / den_loss
-    qdata_out = {"d": d_full, "suh": suh.to(torch.float16), "row_slices": row_slices}
-    return qdata_out, W_hat_eff, rel_loss
+    num = ((HW - HQ) * diff).sum()
+    den = (HW * W_f32).sum().clamp(min=1e-12)
+    qdata = {"d": d_full, "suh": suh.to(torch.float16), "row_slices": row_slices}
+    return {"qdata": qdata, "W_hat": W_hat_eff, "num": num, "den": den, "chol_info": chol_info, "pack": pack}
+
+
+@torch.no_grad()
+def quantize_matrix_liqk_v2(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
+                            row_weights: Optional[torch.Tensor] = None, cd_sweeps: int = 2, out_rot: bool = False):
+    """src/liqk_v2.py:1029-1198 for the TCQ formats: returns (qdata, W_hat [M, K] fp32, rel_loss); with PACK set,
+    PACK["matrix"] holds the .ltq fields (row_slices, idx, gi, G, d_row fp16, e int8, suh fp16).  Raises like
+    torch.linalg.cholesky when the damped Hessian is not positive definite."""
+    _lib.require_cuda(W, H)
+    if out_rot:
+        s_out = make_rademacher_signs(W.shape[0], seed=seed + 7919, device=W.device)
+        rw = None
+        if row_weights is not None:
+            rw = row_weights.float().view(-1, QK_K).mean(dim=1, keepdim=True).expand(-1, QK_K).reshape(-1)
+        q_res, w_hat_r, rel = quantize_matrix_liqk_v2(_fwht_rows(W.float() * s_out.unsqueeze(1)), H, spec_or_row_specs,
+                                                      seed=seed, damp=damp, row_weights=rw, cd_sweeps=cd_sweeps)
+        q_res["s_out"] = s_out.to(torch.int8)
+        return q_res, _fwht_rows(w_hat_r) * s_out.unsqueeze(1), rel
+
+    want_pack = PACK is not None
+    if want_pack:
+        PACK["groups"] = []
+
+    def rows_fn(W_rot, U, U_blks_inv, diag_w, sp):  # the row groups also pass through PACK["groups"], as in the reference
+        d_sub, Wh_sub = _quantize_rows_tcq_ldlq(W_rot, U, U_blks_inv, diag_w, sp)
+        return d_sub, Wh_sub, (PACK["groups"].pop() if want_pack else {})
+
+    r = _quantize_matrix_core(W, H, spec_or_row_specs, seed, damp, row_weights, want_pack,
+                              rows_fn=rows_fn if want_pack else None)
+    if int(r["chol_info"].item()) != 0:
+        raise torch.linalg.LinAlgError("linalg.cholesky: the damped Hessian is not positive-definite "
+                                       f"(leading minor of order {int(r['chol_info'].item())})")
+    if want_pack:
+        PACK["matrix"] = r["pack"]
+    rel_loss = float(r["num"].item()) / float(r["den"].item())
+    return r["qdata"], r["W_hat"], rel_loss

@@ -161,3 +161,25 @@ def test_ref_kernel_fixtures():
                 assert np.array_equal(out[1], arrs["end"]), name
             n += 1
     assert n > 0
+
+
+def _ltq_fmt(name, gains):
+    from ltq_research_b200.formats import TCQ_CONFIG
+    c = TCQ_CONFIG[name]
+    return O.LtqFormat(name, c["K"], int(c.get("pp", 0)), (c["m"],) + tuple(c.get("m_extra", ())), c["h"],
+                       float(c["step"]), c.get("sub", 16), np.asarray(c["lut"], np.float32), np.asarray(gains, np.float32))
+
+
+def test_pack_slices_all_formats_match_reference():
+    """The oracle's pack_slice / decode_slice == the reference's (src/ltq_file.py:79-148) for every .ltq tile format
+    of TCQ_CONFIG (tests/golden/pack_slices.npz, made by tests/golden/make_golden_pack.py)."""
+    z = np.load(GOLDEN / "pack_slices.npz")
+    meta = json.loads(bytes(z["meta"]).decode())
+    assert len(meta) == 35  # every TCQ_CONFIG format but the three EQ ones, which have no .ltq encoding
+    for m in meta:
+        n = m["name"]
+        fmt = _ltq_fmt(n, z[f"{n}/gains"])
+        raw = O.pack_slice(z[f"{n}/idx"].astype(np.int64), z[f"{n}/gi"].astype(np.int64), fmt)
+        assert np.array_equal(np.frombuffer(raw, np.uint8), z[f"{n}/bytes"]), n
+        dec = O.decode_slice(raw, m["R"], m["K"], fmt)
+        assert np.array_equal(dec.view(np.uint32), z[f"{n}/vals"].view(np.uint32)), n
