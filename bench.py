@@ -1,23 +1,27 @@
 """Benchmark of the LTQ TCQ quantizer hot path on B200 (one JSON line on rank 0).
 
-Workload ("Gaussian rig"): one fp32 4096 x 4096 matrix of N(0, 1) values (seed 0, one matrix
-per rank: weak scaling), tiled 16 x 16 as src/ltq_file.py:69-72 does (65,536 tiles of 256), each tile divided by its
-fp16 rms (scale multiplier 1.0, src/universal_bench.py:124), quantized by the joint TCQ Viterbi with the config-1
-format (K = 2, 10-bit trellis memory, mask 359, 4 subsets, h = 2 -> 4 gains per 16 weights, table
-results/universal_gaussian.json "tcq_K2_h2"), tail-biting, full-tile first pass.  A step = one quantization of that
-matrix.  Metric: Mweights/s quantized (whole job, all ranks).
+Workload ("Llama-3.2-3B-shaped layer set"): a step is one decoder layer of seven matrices,
+q 3072x3072, k / v 1024x3072, o 3072x3072, gate / up 8192x3072, down 3072x8192 (100.7 M weights), quantized as the
+reference's quantize_matrix_liqk_v2 does (src/liqk_v2.py:1029-1198): FWHT-256 rotation with the column scale suh,
+damped (0.02 x TCQ_DAMP_MULT 10 = 0.2) Cholesky factor U of the rotated Hessian, per-(row, block) scale fit, LDLQ over
+256-column blocks with the two-pass tail-biting TCQ Viterbi (tb_window 32) per 16-column sub-block, c_row / suh refits,
+then packed into .ltq tiles and verified on the device (src/ltq_file.py:79-148, 187-213).  Even layers use TCQ3X
+(K = 3, 8 subsets, 4 gains per 16 weights), odd layers TCQ25X (K = 3 - 0.5, D2).  Synthetic seeded inputs with the
+config's distributions: bf16 Student-t(5) x 0.02 weights with 0.5 % of input columns x 20; H = X^T X / 4096 of 4096
+N(0, 1) activation rows with log-normal(0, 1) per-channel scales, one H per matrix.  Every rank quantizes its own layers
+(weak scaling, no collective on the data path).  Metric: Mweights/s quantized (whole job).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 --impl reference times the reference algorithm on the host cores: the CPU restatement of the reference Viterbi
-(oracle/, the only CPU implementation that can run on the GPU box), all host threads, bounded samples.
+(oracle/, the only CPU implementation that can run on the GPU box) on tiles of this workload's format and tail-biting
+schedule, all host threads, bounded samples.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -32,27 +36,42 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-M_ROWS = M_COLS = 4096
-TILE = 256
 METRIC = "Mweights/s quantized"
-WORKLOAD = "gaussian_rig_4096x4096_tcq_K2_h2_tailbiting"
-ACS_PER_WEIGHT = 2 * 1024 * 4   # passes x states x gain slots (tb_window = 0: two full passes)
-ALU_SLOTS_PER_ACS = 2           # one path-metric add + half a compare + half a select (issue-slot accounting)
-L2_BYTES = 126 * 2 ** 20
+WORKLOAD = "llama3.2-3b_layers_tcq3x_tcq25x_fwht_ldlq_damp0.2_tbwin32_pack"
+LAYER = [("q_proj", 3072, 3072), ("k_proj", 1024, 3072), ("v_proj", 1024, 3072), ("o_proj", 3072, 3072),
+         ("gate_proj", 8192, 3072), ("up_proj", 8192, 3072), ("down_proj", 3072, 8192)]
+FORMATS = ("TCQ3X", "TCQ25X")
+WEIGHTS_PER_LAYER = sum(m * k for _, m, k in LAYER)
+TB_WINDOW = 32
+ALU_SLOTS_PER_ACS = 2  # one path-metric add + half a compare + half a select (issue-slot accounting)
 
 
-def rig_format():
-    d = json.loads((ROOT / "ltq_research_b200" / "data" / "tcq_formats.json").read_text())["formats"]["_config1_tcq_K2_h2"]
-    return d
+def layer_spec(layer: int) -> str:
+    return FORMATS[layer % 2]
 
 
-def make_tiles(seed: int, device) -> tuple[torch.Tensor, torch.Tensor]:
-    """Seeded N(0,1) matrix -> tiles [65536, 256] divided by their fp16 rms, and the rms."""
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    W = torch.randn(M_ROWS, M_COLS, generator=g)
-    tiles = W.reshape(M_ROWS // 16, 16, M_COLS // 16, 16).permute(0, 2, 1, 3).reshape(-1, TILE).contiguous()
-    d = tiles.square().mean(dim=1, keepdim=True).sqrt().half().float()
-    return (tiles / d).to(device), d.to(device)
+def make_matrix(M: int, K: int, seed: int, device) -> tuple:
+    """bf16 Student-t(5) * 0.02 weights [M, K] with 0.5 % of the input columns x 20; H = X^T X / 4096 with
+    X = N(0, 1) [4096, K] * exp(N(0, 1)) per column."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    z = torch.randn(M, K, device=device, generator=g)
+    chi2 = torch.zeros(M, K, device=device)
+    for _ in range(5):
+        chi2.add_(torch.randn(M, K, device=device, generator=g).square_())
+    W = z.div_(chi2.div_(5.0).sqrt_()).mul_(0.02)
+    del chi2
+    cols = torch.randperm(K, device=device, generator=g)[: max(1, round(0.005 * K))]
+    W[:, cols] *= 20.0
+    W = W.to(torch.bfloat16)
+    X = torch.randn(4096, K, device=device, generator=g) * torch.exp(torch.randn(1, K, device=device, generator=g))
+    H = (X.T @ X) / 4096.0
+    return W, H
+
+
+def layer_jobs(layer: int, rank: int, device) -> list:
+    spec = layer_spec(layer)
+    return [(*make_matrix(M, K, 1_000_003 * rank + 1009 * layer + j, device), spec)
+            for j, (_, M, K) in enumerate(LAYER)]
 
 
 class ClockSampler:
@@ -110,66 +129,144 @@ def measured_peaks() -> dict:
     return json.loads(p.read_text()) if p.exists() else {}
 
 
-def cpu_baseline_sample(seconds: float = 15.0) -> dict:
-    """The CPU restatement of the reference Viterbi (oracle/) on this host's cores, config-1 tiles, bounded sample."""
+def alu_peak_gacs() -> tuple:
+    sm_mhz = float(measured_peaks().get("sm_max_mhz", 1965.0))
+    return 148 * 128 * sm_mhz * 1e6 / ALU_SLOTS_PER_ACS / 1e9, sm_mhz
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU: the oracle's restatement of the reference Viterbi on this workload's tiles (TCQ3X, tail-biting, window 32)
+# ------------------------------------------------------------------------------------------------
+
+def _cpu_format():
+    from ltq_research_b200.formats import TCQ_CONFIG
+    c = TCQ_CONFIG["TCQ3X"]
+    from ltq_research_b200.tcq_proto import make_gains
+    return c, make_gains(c["h"], c["step"], "cpu").numpy().astype(np.float32)
+
+
+def _cpu_tiles(n: int, seed: int = 0) -> tuple:
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((n, 256)).astype(np.float32)
+    w = (0.5 + rng.random(256)).astype(np.float32)
+    return x, w
+
+
+def _cpu_viterbi(x, w, c, gains, threads):
     from oracle import oracle as O
-    fmt = rig_format()
+    return O.viterbi(x, np.asarray(c["lut"], np.float32), c["K"], 10, c["m"], gains, sub=16, wts=w,
+                     m_extra=tuple(c["m_extra"]), tail_biting=True, tb_window=TB_WINDOW, return_code=True,
+                     n_threads=threads)
+
+
+def cpu_baseline_sample(seconds: float = 15.0) -> dict:
+    c, gains = _cpu_format()
     threads = len(os.sched_getaffinity(0))
-    tiles, _ = make_tiles(0, "cpu")
-    x = tiles.numpy()
+    step = max(threads, 8) * 4
+    x, w = _cpu_tiles(step * 16)
     done, t0, i = 0, time.perf_counter(), 0
-    step = max(threads, 8) * 2
-    while time.perf_counter() - t0 < seconds and i + step <= x.shape[0]:
-        O.viterbi(x[i:i + step], np.asarray(fmt["lut"], np.float32), 2, 10, 359,
-                  np.asarray(fmt["gains_cpu"], np.float32), sub=16, tail_biting=True, n_threads=threads)
-        done += step * TILE
-        i += step
+    while time.perf_counter() - t0 < seconds:
+        j = i % 16
+        _cpu_viterbi(x[j * step:(j + 1) * step], w, c, gains, threads)
+        done += step * 256
+        i += 1
     el = time.perf_counter() - t0
     return {"value": done / el / 1e6, "unit": METRIC, "cores": threads, "kind": "port",
-            "sample": f"{done // TILE} config-1 tiles (tail-biting, 2 passes) in {el:.1f} s with the C restatement of "
-                      f"the reference Viterbi (oracle/tcq_oracle.c), {threads} threads"}
+            "sample": f"{done // 256} TCQ3X tiles of 256 (two-pass tail-biting Viterbi, window 32) in {el:.1f} s with "
+                      f"the C restatement of the reference Viterbi (oracle/tcq_oracle.c), {threads} threads; the "
+                      f"Viterbi only (the LDLQ / refit linear algebra of the GPU step is not timed on the CPU)"}
 
 
 def run_reference(args, rank: int, world: int):
     """--impl reference: the reference algorithm on the host cores (the oracle port), rank 0 only."""
     if rank != 0:
         return
-    from oracle import oracle as O
-    fmt = rig_format()
+    c, gains = _cpu_format()
     threads = len(os.sched_getaffinity(0))
-    tiles, _ = make_tiles(0, "cpu")
-    x = tiles.numpy()
-    n = max(threads * 4, 64)  # tiles per step: a bounded sample of the config-1 matrix
-    kw = dict(sub=16, tail_biting=True, n_threads=threads)
-    lut, g = np.asarray(fmt["lut"], np.float32), np.asarray(fmt["gains_cpu"], np.float32)
+    n = max(threads * 8, 64)  # tiles per step: a bounded sample of one layer's sub-block tiles
+    x, w = _cpu_tiles(n * (args.steps + args.warmup + 1), seed=1)
     for k in range(args.warmup):
-        O.viterbi(x[:n], lut, 2, 10, 359, g, **kw)
+        _cpu_viterbi(x[k * n:(k + 1) * n], w, c, gains, threads)
     t0 = time.perf_counter()
     for k in range(args.steps):
-        s = (k * n) % (x.shape[0] - n)
-        O.viterbi(x[s:s + n], lut, 2, 10, 359, g, **kw)
+        s = (args.warmup + k) * n
+        _cpu_viterbi(x[s:s + n], w, c, gains, threads)
     el = time.perf_counter() - t0
-    v = args.steps * n * TILE / el / 1e6
+    v = args.steps * n * 256 / el / 1e6
+    sample = (f"{n} TCQ3X tiles of 256 per step (two-pass tail-biting Viterbi, window 32), C restatement of the "
+              f"reference Viterbi (oracle/tcq_oracle.c), {threads} threads; Viterbi only")
     line = {"metric": METRIC, "value": v, "unit": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": WORKLOAD, "tiles_per_step": n, "parallelism": "host threads"},
-            "cpu_baseline": {"value": v, "unit": METRIC, "cores": threads, "kind": "port",
-                             "sample": f"{n} config-1 tiles per step, tail-biting, C restatement of the reference "
-                                       f"Viterbi (oracle/tcq_oracle.c), {threads} threads"},
+            "cpu_baseline": {"value": v, "unit": METRIC, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": METRIC, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------
+# GPU
+# ------------------------------------------------------------------------------------------------
+
+def union_ms(iv: list) -> float:
+    tot, end = 0.0, -1e30
+    for a, b in sorted(iv):
+        if b <= end:
+            continue
+        tot += b - max(a, end)
+        end = b
+    return tot
+
+
+def isolated_block_roofline(dev, spec: str, rows: int = 27648, timed: bool = True) -> dict:
+    """One fused block launch over `rows` rows (a layer's worth of tile groups) timed alone: the block kernel at full
+    occupancy, without the concurrent factorisation / GEMM kernels of the real step."""
+    import ltq_research_b200.liqk_v2 as L
+    g = torch.Generator(device=dev).manual_seed(7)
+    W = torch.randn(rows, 256, device=dev, generator=g)
+    A = torch.randn(256, 256, device=dev, generator=g) / 16
+    U = torch.triu(A) + 4 * torch.eye(256, device=dev)
+    Ui = torch.linalg.solve_triangular(U, torch.eye(256, device=dev), upper=True).contiguous()
+    d_rb = torch.ones(rows, 1, device=dev)
+    dw = (1.0 / torch.diagonal(U) ** 2).contiguous()
+    G = torch.empty(rows, 256, device=dev)
+    idx = torch.empty(rows, 256, dtype=torch.int16, device=dev)
+    gi = torch.empty(rows, 256, dtype=torch.uint8, device=dev)
+    br = L._BlockRunner(spec, rows, dev)
+    for _ in range(2):
+        br.run(W, 0, d_rb, 0, dw, U, Ui, G, idx, gi)
+    if not timed:
+        br.run(W, 0, d_rb, 0, dw, U, Ui, G, idx, gi)
+        torch.cuda.synchronize()
+        return {}
+    ms = []
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        br.run(W, 0, d_rb, 0, dw, U, Ui, G, idx, gi)
+        b.record()
+        torch.cuda.synchronize()
+        ms.append(a.elapsed_time(b))
+    acs = br.acs_per_block()
+    return {"format": spec, "rows": rows, "ms": statistics.median(ms),
+            "achieved": acs / (statistics.median(ms) * 1e-3) / 1e9}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", action="store_true", help="one quantization of --tiles tiles, no timing (ncu runs)")
-    ap.add_argument("--tiles", type=int, default=0, help="with --profile: tiles of the config-1 matrix to quantize")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="quantize one matrix of --rows x 3072 (TCQ3X) untimed, for ncu captures of its kernels")
+    ap.add_argument("--rows", type=int, default=1024)
+    ap.add_argument("--profile-block", default=None, metavar="FORMAT",
+                    help="one fused block launch of FORMAT over --rows rows untimed (after two warm-up launches), for "
+                         "ncu captures of ldlq_block_kernel")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -184,113 +281,120 @@ def main():
     if world > 1:
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    from ltq_research_b200.tcq_proto import viterbi_ub_cuda
-    fmt = rig_format()
-    small = torch.tensor(fmt["lut"], device=dev)
-    gains = torch.tensor(fmt["gains_cpu"], device=dev)
-    x, d = make_tiles(rank, dev)
-    kw = dict(K=2, nu=10, m=359, sub=16, tail_biting=True, return_code=True)
-    if args.profile:
-        xs = x[: args.tiles] if args.tiles else x
-        rec, gi, idx = viterbi_ub_cuda(xs, small, gains=gains, **kw)
-        torch.cuda.synchronize()
-        assert torch.equal(rec, gains[gi.long()] * small[idx.long()])
-        print(f"profile run: {xs.shape[0]} tiles", flush=True)
+    from ltq_research_b200 import _lib
+    import ltq_research_b200.liqk_v2 as Lq
+    from ltq_research_b200.batch import quantize_matrices
+    from ltq_research_b200.formats import load_formats
+    fmts = load_formats(list(FORMATS), dev)
+
+    if args.profile_block:
+        r = isolated_block_roofline(dev, args.profile_block, rows=args.rows, timed=False)
+        print(f"profile run: fused block {args.profile_block} over {args.rows} rows", flush=True)
         return
-    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
-
-    def step(xx):
-        return viterbi_ub_cuda(xx, small, gains=gains, **kw)
+    if args.profile:
+        W, H = make_matrix(args.rows, 3072, 5, dev)
+        r = quantize_matrices([(W, H, "TCQ3X")], ltq_formats=fmts)
+        torch.cuda.synchronize()
+        print(f"profile run: {args.rows} x 3072 TCQ3X, rel_loss {r[0]['rel_loss']:.5f}", flush=True)
+        return
 
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        step(x)
+    # inputs of the warm-up and timed layers, resident in HBM (each layer's H and W, ~0.7 GB, far above the 126 MB L2).
+    # The warm-up quantizes as many layers as the timed region (at least --warmup), so that the timed region starts
+    # with the memory pools of all streams grown to the size it needs.
+    args.warmup = max(args.warmup, args.steps)
+    warm = [j for l in range(args.warmup) for j in layer_jobs(10_000 + l, rank, dev)]
+    timed = [j for l in range(args.steps) for j in layer_jobs(l, rank, dev)]
+    quantize_matrices(warm, n_streams=args.streams, ltq_formats=fmts, pack=False)
     barrier()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+
+    Lq.BLOCK_EVENTS = []
+    k0 = _lib.kernels_launched()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
         t_wall = time.perf_counter()
-        for k in range(args.steps):
-            flush.fill_(float(k))  # L2 flush between timed steps (outside the step's events)
-            starts[k].record()
-            rec, gi, idx = step(x)
-            ends[k].record()
+        e_start.record()
+        res = quantize_matrices(timed, n_streams=args.streams, ltq_formats=fmts, pack=False)
+        e_end.record()
         barrier()
         t_wall = time.perf_counter() - t_wall
-    dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    # one Viterbi pass timed alone (forward ACS + traceback kernels), for the ACS roofline
-    pass_ms = []
-    from ltq_research_b200.tcq_proto import viterbi_ub_cuda as vu
-    for k in range(3):
-        flush.fill_(float(k))
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        vu(x, small, 2, 10, 359, gains, sub=16, return_end_state=True)
-        b.record()
-        torch.cuda.synchronize()
-        pass_ms.append(a.elapsed_time(b))
-    # end to end through the public API: pinned host tiles in, reconstruction and codes back to the host
-    xh = x.cpu().pin_memory()
-    rec_h = torch.empty(x.shape, dtype=torch.float32).pin_memory()
-    code_h = torch.empty(x.shape, dtype=torch.int32).pin_memory()
-    e2e_ms = []
-    for k in range(max(3, args.steps // 2)):
-        flush.fill_(float(k))
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        xd = xh.to(dev, non_blocking=True)
-        r, gi, idx = step(xd)
-        rec_h.copy_(r, non_blocking=True)
-        code_h.copy_((gi << 16) | idx, non_blocking=True)
-        b.record()
-        torch.cuda.synchronize()
-        e2e_ms.append(a.elapsed_time(b))
-    # correctness guard on the timed output: recompute one tile sample through the same path
-    assert torch.equal(rec, gains[gi.long()] * small[idx.long()])
+    launches = _lib.kernels_launched() - k0
+    ev, Lq.BLOCK_EVENTS = Lq.BLOCK_EVENTS, None
+    dev_ms = e_start.elapsed_time(e_end)
+    iv = [(e_start.elapsed_time(a), e_start.elapsed_time(b)) for a, b, _, _ in ev]
+    block_ms = union_ms(iv)
+    block_acs = sum(c for _, _, c, _ in ev)
+    block_weights = sum(w for _, _, _, w in ev)
+    rel = [r["rel_loss"] for r in res]
+    packed_bytes = sum(int(r["ltq"]["data"].numel()) for r in res)
 
-    t = torch.tensor([dev_ms, statistics.median(pass_ms), statistics.median(e2e_ms)], device=dev)
+    # end to end through the public API: pinned host inputs in, the packed .ltq tensors back in pinned host memory
+    e2e_ms, h2d, d2h = None, 0, 0
+    if not args.no_e2e:
+        host = [(W.cpu().pin_memory(), H.cpu().pin_memory(), sp) for W, H, sp in timed]
+        h2d = sum(W.numel() * W.element_size() + H.numel() * H.element_size() for W, H, _ in host)
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        res_h = quantize_matrices(host, n_streams=args.streams, ltq_formats=fmts, pack=False, to_host=True)
+        b.record()
+        barrier()
+        e2e_ms = a.elapsed_time(b)
+        d2h = sum(sum(r["ltq"][k].numel() * r["ltq"][k].element_size() for k in ("data", "d_row", "e", "suh"))
+                  for r in res_h)
+        # the host run's packed bytes are the device run's
+        for r0, r1 in zip(res, res_h):
+            assert torch.equal(r0["ltq"]["data"].cpu(), r1["ltq"]["data"]), "e2e output differs from the timed run"
+        del host, res_h
+
+    t = torch.tensor([dev_ms, e2e_ms or 0.0], device=dev)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dev_ms, pass_med, e2e_med = t.tolist()
-    weights_per_rank = M_ROWS * M_COLS
-    total = weights_per_rank * world
+    dev_ms, e2e_max = t.tolist()
+    total = WEIGHTS_PER_LAYER * args.steps * world
     ms_step = dev_ms / args.steps
-    value = total / (ms_step * 1e-3) / 1e6
-    e2e_value = total / (e2e_med * 1e-3) / 1e6
+    value = total / (dev_ms * 1e-3) / 1e6
     clocks = clk.summary()
+    iso = isolated_block_roofline(dev, "TCQ3X") if rank == 0 else None
     if rank == 0:
-        peaks = measured_peaks()
-        sm_mhz = float(peaks.get("sm_max_mhz", 1965.0))
-        alu_peak = 148 * 128 * sm_mhz * 1e6 / ALU_SLOTS_PER_ACS / 1e9  # GACS/s at full issue of every SMSP
-        acs_per_pass = weights_per_rank * ACS_PER_WEIGHT / 2
-        achieved = acs_per_pass / (pass_med * 1e-3) / 1e9
-        prof = ROOT / "profiles" / "vit_fwd_config1.json"
-        traffic = json.loads(prof.read_text()).get("dram_bytes_per_pass") if prof.exists() else None
+        peak, sm_mhz = alu_peak_gacs()
+        achieved = block_acs / (block_ms * 1e-3) / 1e9
+        prof = ROOT / "profiles" / "ldlq_block_config2.json"
+        traffic = None
+        if prof.exists():
+            bpw = json.loads(prof.read_text()).get("dram_bytes_per_weight")
+            if bpw:
+                traffic = bpw * block_weights / len(ev)  # per average launch: weights x DRAM bytes per weight
         cpu = None if args.no_cpu_baseline else cpu_baseline_sample()
         line = {
             "metric": METRIC, "value": value, "unit": METRIC, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "matrix": [M_ROWS, M_COLS], "tiles_per_rank": weights_per_rank // TILE,
-                       "format": "K=2 nu=10 m=359 nl=4 h=2 sub=16 tail-biting tb_window=0",
-                       "parallelism": f"dp{world} (one matrix per rank)", "l2": "flushed between timed steps",
-                       "wall_s": t_wall},
-            "roofline": {"bound": "alu", "kernel": "viterbi pass (vit_fwd_kernel + vit_tb_kernel)",
-                         "achieved": achieved, "peak": alu_peak, "unit": "GACS/s", "frac": achieved / alu_peak,
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-2 distributions)",
+            "config": {"workload": WORKLOAD, "step": "one Llama-3.2-3B decoder layer, 7 matrices, 100.7 M weights",
+                       "formats": "TCQ3X even layers / TCQ25X odd layers", "damp": 0.2, "tb_window": TB_WINDOW,
+                       "streams": args.streams, "parallelism": f"dp{world} (own layers per rank)",
+                       "l2": "inputs larger than L2 (0.7 GB per layer)", "wall_s": t_wall,
+                       "rel_loss_mean": float(np.mean(rel)), "ltq_bytes": packed_bytes},
+            "roofline": {"bound": "alu", "kernel": "ldlq_block_kernel (fused LDLQ block: Viterbi ACS)",
+                         "achieved": achieved, "peak": peak, "unit": "GACS/s", "frac": achieved / peak,
                          "traffic": traffic,
+                         "basis": f"sum of the launches' add-compare-selects / union of their CUDA-event intervals "
+                                  f"({block_ms:.1f} ms of {dev_ms:.1f} ms) on the launching streams",
                          "peak_basis": f"148 SMs x 128 issue slots/clk x {sm_mhz:.0f} MHz (MEASURED_PEAKS sm_max_mhz) "
-                                       f"/ {ALU_SLOTS_PER_ACS} slots per ACS"},
+                                       f"/ {ALU_SLOTS_PER_ACS} slots per ACS",
+                         "isolated": dict(iso, frac=iso["achieved"] / peak)},
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": METRIC, "h2d_bytes_per_step": int(xh.numel() * 4),
-                    "d2h_bytes_per_step": int(rec_h.numel() * 4 + code_h.numel() * 4)},
-            "gpu_launches": 4 * args.steps,
+            "e2e": None if e2e_ms is None else {
+                "value": total / (e2e_max * 1e-3) / 1e6, "unit": METRIC,
+                "h2d_bytes_per_step": int(h2d // args.steps), "d2h_bytes_per_step": int(d2h // args.steps)},
+            "gpu_launches": int(launches),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -48,8 +48,50 @@ class LtqLibraryError(RuntimeError):
     pass
 
 
-def lib() -> ctypes.CDLL:
-    """The loaded library; raises LtqLibraryError when it has not been built."""
+# kernels launched by one successful call (a constant, or a function of the call's arguments)
+KERNELS_PER_CALL = {
+    "tcq_viterbi": 2,
+    "ltq_viterbi_tb": lambda a: 2 * int(a[22]),
+    "ltq_viterbi_tb_noalloc": lambda a: 2 * int(a[22]),
+    "ltq_fwht256": 1, "ltq_scale_fit": 1, "ltq_ldlq_gather": 1, "ltq_ldlq_feedback": 1, "ltq_ldlq_block": 2,
+    "ltq_pack_slice": 1, "ltq_decode_slice": 1,
+}
+
+
+class _CountingLib:
+    """The ctypes library with a count of the kernels its calls launched (``kernels``), per process."""
+
+    def __init__(self, cdll: ctypes.CDLL):
+        self._cdll = cdll
+        self.kernels = 0
+        self._lock = threading.Lock()
+
+    def __getattr__(self, name):
+        fn = getattr(self._cdll, name)
+        k = KERNELS_PER_CALL.get(name)
+        if k is None:
+            return fn
+
+        def call(*a):
+            rc = fn(*a)
+            if rc == 0:
+                n = k(a) if callable(k) else k
+                with self._lock:
+                    self.kernels += n
+            return rc
+        call.__name__ = name
+        self.__dict__[name] = call
+        return call
+
+
+def kernels_launched() -> int:
+    """Kernels launched so far by this process through the library (successful calls only)."""
+    return lib().kernels
+
+
+def lib() -> "_CountingLib":
+    """The loaded library (ctypes functions, plus a launch count); raises LtqLibraryError when it has not been
+    built."""
     global _LIB
     if _LIB is None:
         with _LOCK:
@@ -61,7 +103,7 @@ def lib() -> ctypes.CDLL:
                     fn = getattr(L, name)
                     fn.restype = res
                     fn.argtypes = args
-                _LIB = L
+                _LIB = _CountingLib(L)
     return _LIB
 
 

@@ -56,13 +56,20 @@ def _record(obj, stream: torch.cuda.Stream):
 @torch.no_grad()
 def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], seed: int = 1337, damp: float = 0.02,
                       n_streams: int = 8, pack: bool = True, keep_w_hat: bool = False,
-                      device: Optional[torch.device] = None, on_issued=None) -> List[Dict]:
+                      device: Optional[torch.device] = None, on_issued=None, ltq_formats: Optional[Dict] = None,
+                      to_host: bool = False, gemm: str = "bf16x6") -> List[Dict]:
     """Quantize every (W [M, K], H [K, K], spec) of `jobs` as quantize_matrix_liqk_v2(W, H, spec, seed, damp) would,
     concurrently on `n_streams` CUDA streams.  W / H may be CUDA tensors or (pinned) host tensors, which are copied to
     the device on the matrix's stream.  Returns, per job: {"qdata", "pack" (the PACK["matrix"] fields, device tensors)
     when pack, "W_hat" when keep_w_hat, "rel_loss" (float)}.  One host synchronisation, after the last job is issued;
-    on_issued(i), if given, is called after job i has been issued (for overlapping host work).  Raises
-    torch.linalg.LinAlgError if a damped Hessian is not positive definite."""
+    on_issued(i), if given, is called after job i has been issued (for overlapping host work).
+    ltq_formats ({name: LtqFormat}, e.g. formats.load_formats(menu, device)): each matrix is also packed into its .ltq
+    data tensor on the device and verified there (ltq_file.pack_matrix_device), on the matrix's stream; the result
+    gains "ltq": {"data" (uint8), "slices" ([r0, r1, format, offset] rows, format = position in ltq_formats),
+    "d_row" fp16, "e" int8, "suh" fp16}, as pinned host tensors when to_host.  Raises torch.linalg.LinAlgError if a
+    damped Hessian is not positive definite, RuntimeError if a packed matrix does not decode to its tile values.
+    gemm: the mode of the LDLQ inter-block update and refit products (liqk_v2.GEMM_MODES): "bf16x6" (default) runs
+    them as fp32-accurate split products on the tensor cores; "fp32" reproduces quantize_matrix_liqk_v2 bit for bit."""
     if not jobs:
         return []
     dev = torch.device(device) if device is not None else None
@@ -96,7 +103,8 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
                         W.record_stream(s)
                     if H.is_cuda:
                         H.record_stream(s)
-                active[k] = (i, _quantize_matrix_steps(Wd, Hd, sp, seed, damp, None, pack))
+                active[k] = (i, _quantize_matrix_steps(Wd, Hd, sp, seed, damp, None,
+                                                       pack or ltq_formats is not None, None, gemm))
             if active[k] is None:
                 continue
             i, gen = active[k]
@@ -107,6 +115,10 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
                     r = e.value
                     if not keep_w_hat:
                         r.pop("W_hat")
+                    if ltq_formats is not None:
+                        r["ltq"] = _pack_job(r["pack"], ltq_formats, to_host)
+                        if not pack:
+                            r["pack"] = None
                     out[i] = r
                     active[k] = None
                     if on_issued is not None:
@@ -117,14 +129,36 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
         _record(r, main)
     nd = torch.stack([torch.stack([r["num"], r["den"]]) for r in out]).cpu()
     info = torch.stack([r["chol_info"].reshape(()) for r in out]).cpu()
+    bad = (torch.stack([r["ltq"]["bad"].reshape(()) for r in out]).cpu() if ltq_formats is not None
+           else torch.zeros(len(out), dtype=torch.int64))
     res = []
     for i, r in enumerate(out):
         if int(info[i]) != 0:
             raise torch.linalg.LinAlgError(f"quantize_matrices: job {i}: the damped Hessian is not positive-definite")
+        if int(bad[i]) != 0:
+            raise RuntimeError(f"quantize_matrices: job {i}: the packed tiles disagree with the quantizer in "
+                               f"{int(bad[i])} weights")
         d = {"qdata": r["qdata"], "rel_loss": float(nd[i, 0]) / float(nd[i, 1])}
         if pack:
             d["pack"] = r["pack"]
         if keep_w_hat:
             d["W_hat"] = r["W_hat"]
+        if ltq_formats is not None:
+            d["ltq"] = {k: v for k, v in r["ltq"].items() if k != "bad"}
         res.append(d)
     return res
+
+
+def _pack_job(pm: dict, formats: Dict, to_host: bool) -> dict:
+    """.ltq data of one matrix on the current stream: packed + verified slices, scales; optionally copied to pinned
+    host memory (asynchronously, on the same stream)."""
+    from .ltq_file import pack_matrix_device
+    data, rows, bad = pack_matrix_device(pm, formats, verify=True)
+    out = {"data": data, "slices": [[r0, r1, fi, o] for r0, r1, fi, o in rows], "d_row": pm["d_row"].to(torch.float16),
+           "e": pm["e"].to(torch.int8), "suh": pm["suh"].to(torch.float16), "bad": bad}
+    if to_host:
+        for k in ("data", "d_row", "e", "suh"):
+            h = torch.empty(out[k].shape, dtype=out[k].dtype, pin_memory=True)
+            h.copy_(out[k], non_blocking=True)
+            out[k] = h
+    return out

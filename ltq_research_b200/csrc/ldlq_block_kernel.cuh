@@ -10,7 +10,7 @@
 //               (the tail-biting schedule of src/tcq_proto.py:584-609)
 //   4. feedback G[:, s0 + c] = rec, idx / gi from the codes;  e = w[:, s0:s1] - d_rb * rec;
 //               err = e @ Uinv[s0:s1, s0:s1];  w[:, s1:256] -= err @ U[s0:s1, s1:256]   (:964-971)
-// The forward passes are vit_fwd_tile (G warps, one per gain slot), the tracebacks vit_tb_tile (warp 0); the feedback
+// The forward passes are vit_fwd_tile (G warps, one per gain slot), the tracebacks tb_coop (whole CTA); the feedback
 // uses the same sequential fma chains as the stand-alone ltq_ldlq_feedback kernel, so both paths give identical bits.
 // The block's running copy of w (16 rows x 256 per CTA) lives in the workspace; W_work itself is only read, because
 // the inter-block update after the block (:972-979) needs the block's starting values.
@@ -39,8 +39,199 @@ struct LdlqParams {
     float* xbuf;              // [N][256] Viterbi input tile
     float* recbuf;            // [N][256] reconstruction (gain * table value)
     int* codebuf;             // [N][256] codes (gain index << 16 | label * U + u)
-    int fb_off;               // shared-memory offset of the feedback scratch and of the traceback warp region
+    int fb_off;               // shared-memory offset of the feedback scratch and of the traceback region
 };
+
+// ------------------------------------------------------------------------------------------------
+// Cooperative traceback of tile n by the whole CTA (the forward pass has just ended; its metric region is free).
+// One thread (thread 0) walks the survivor path back, one sub-block (`chunk`) at a time, from words staged in shared
+// memory; while it walks chunk c, the CTA's other warps stage chunk c - 1 — the words of every gain slot, because the
+// slot of chunk c - 1 is only known once the walk reaches the start of chunk c — and the gain-merge winners of that
+// boundary, into the other half of a double buffer.  The walk records per step only the code bit (bit 0 of the
+// state), the parity class (D2 / D4 / EQ) and, per chunk, the gain slot; afterwards every thread rebuilds the states
+//     s_t = ((s_0 << t) | sum_{q < t} c_{t-q} << q) & 1023
+// and reconstructs its samples.  Same decisions, tie-breaks, states, values and codes as vit_tb_tile (the stand-alone
+// traceback kernel), which the tests check bit for bit.
+// Every thread waits for all of its copies (cp.async.wait_all) before every barrier, so no copy is in flight across a
+// barrier.  Shared layout (from `base`): 2 x [G x (sub / 4) x W4 x 32 + 128] words, code bits (T / 32 words), slot per
+// chunk (32 bytes), parity class per step (T bytes), 4 ints.
+// ------------------------------------------------------------------------------------------------
+// 16-byte asynchronous global -> shared copy (completion: cp_async_wait_all by the issuing thread, then a barrier)
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
+{
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+__host__ __device__ inline int tb_coop_words(const VitParams& p)
+{
+    return p.G * (p.sub / 4) * p.W4 * 32 + 128;
+}
+
+__host__ __device__ inline int tb_coop_bytes(const VitParams& p)
+{
+    return 4 * (2 * tb_coop_words(p) + MAXT / 32) + 32 + MAXT + 16;
+}
+
+template <int MD>
+__device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigned char* base, const float* s_tab,
+                                        const float* s_gain, const float* xrow)
+{
+    constexpr bool PP = MD == 1, EQ = MD == 3;
+    const int T = p.T, G = p.G, sub = p.sub, W4 = p.W4, NGRP = sub / 4, nch = T / sub, U = p.U;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int bufw = tb_coop_words(p), per_slot = NGRP * W4 * 32;
+    uint32_t* buf = reinterpret_cast<uint32_t*>(base);
+    uint32_t* cbits = buf + 2 * bufw;
+    uint8_t* sg = reinterpret_cast<uint8_t*>(cbits + MAXT / 32);
+    uint8_t* spar = sg + 32;
+    int* flag = reinterpret_cast<int*>(spar + MAXT);  // [0] state, [1] slot, [2] stopped, [3] state at t = 0
+
+    // stage chunk c (all slots' words — per_slot consecutive words per slot in the survivor stream — and the merge
+    // winners of boundary c) into buffer b with 16-byte asynchronous copies by threads t0, t0 + ts, ...
+    const int v4 = per_slot / 4;
+    auto stage = [&](int c, int b, int t0, int ts) {
+        uint32_t* d = buf + b * bufw;
+        const int nv = G * v4 + ((G > 1 && c > 0) ? NS / 32 : 0);
+        for (int i = t0; i < nv; i += ts) {
+            if (i < G * v4) {
+                const int g = i / v4, r = i - g * v4;
+                cp_async16(d + g * per_slot + 4 * r,
+                           p.svA + ((size_t)n * G + g) * (size_t)p.capA + (size_t)c * per_slot + 4 * r);
+            } else {
+                const int k = i - G * v4;
+                cp_async16(d + G * per_slot + 4 * k, p.gsw + ((size_t)n * p.nsl + c) * (NS / 8) + 4 * k);
+            }
+        }
+    };
+    if (tid == 0) {
+        const int bi = p.best[n];
+        flag[0] = bi % NS;
+        flag[1] = bi / NS;
+        flag[2] = 0;
+    }
+    // the last chunk by every thread; then, while thread 0 walks chunk c, the staging threads (the warps that do not
+    // walk, or lanes 1..31 when there is one warp) copy chunk c - 1 into the other buffer
+    const bool stager = G > 1 ? tid >= 32 : tid > 0;
+    stage(nch - 1, (nch - 1) & 1, tid, nthr);
+    cp_async_wait_all();
+    __syncthreads();
+    int pcur = 0, cstar = 0;  // thread 0: parity class of the current pair / quad (carried across steps)
+    for (int c = nch - 1; c >= 0; c--) {
+        const int b = c & 1, lo = c * sub;
+        if (stager && c > 0) stage(c - 1, b ^ 1, G > 1 ? tid - 32 : tid - 1, G > 1 ? nthr - 32 : nthr - 1);
+        if (tid == 0) {
+            int st = flag[0];
+            const int gs = flag[1];
+            sg[c] = (uint8_t)gs;
+            const uint32_t* B = buf + b * bufw + gs * per_slot;
+            uint32_t acc = 0;
+            bool stop = false, done = false;
+            for (int gl = NGRP - 1; gl >= 0 && !done; gl--) {
+                // the four steps of a group read the same lane column (bits 4..8 of the state at its last step): load
+                // its W4 words once, then walk the four steps in registers
+                constexpr int W4C = MD == 0 ? 2 : (MD == 1 ? 5 : 9);
+                const uint32_t* Wg = B + gl * W4C * 32 + ((st >> 4) & 31);
+                uint32_t w[W4C];
+#pragma unroll
+                for (int k = 0; k < W4C; k++) w[k] = Wg[32 * k];
+                cfor<3, -1, -1>([&](auto JJ) {
+                    constexpr int j = decltype(JJ)::value;
+                    if (done) return;
+                    const int t = lo + 4 * gl + j;
+                    const int b9 = st >> 1;
+                    const int bi4 = bfly_of(j, b9);
+                    if (PP && (j & 1)) {
+                        pcur = (w[j == 1 ? 2 : 4] >> ((bi4 << 1) | (st & 1))) & 1;
+                        spar[t] = spar[t - 1] = (uint8_t)pcur;
+                    }
+                    if (p.mid_st && t == p.mid_t - 1) {
+                        p.mid_st[n] = st;
+                        stop = done = true;
+                        return;
+                    }
+                    acc |= (uint32_t)(st & 1) << (t - lo);
+                    if (t == 0) {
+                        flag[3] = st;
+                        done = true;
+                        return;
+                    }
+                    int h;
+                    if constexpr (MD == 0) {
+                        h = (w[j >> 1] >> ((j & 1) ? bi4 : 16 + bi4)) & 1;
+                    } else if constexpr (PP) {
+                        if constexpr (j & 1) h = (w[j == 1 ? 1 : 3] >> (pcur ? bi4 : 16 + bi4)) & 1;
+                        else h = (w[0] >> ((j == 0) ? 16 + bi4 : bi4)) & 1;
+                    } else {
+                        const int ro = (bi4 << 1) | (st & 1);
+                        if constexpr (j == 3) {
+                            cstar = (w[7] >> ro) & 1;
+                            const int bb = (w[8] >> ro) & 1;
+                            h = ((cstar ? w[6] : w[5]) >> (bb ? bi4 : 16 + bi4)) & 1;
+                            if (EQ) {
+                                spar[t] = spar[t - 1] = spar[t - 2] = spar[t - 3] = (uint8_t)cstar;
+                            } else {
+                                spar[t] = (uint8_t)(bb ^ cstar);
+                                spar[t - 1] = (uint8_t)bb;
+                            }
+                        } else if constexpr (j == 2) {
+                            h = (w[4] >> (cstar ? bi4 : 16 + bi4)) & 1;
+                        } else if constexpr (j == 1) {
+                            const int bb = ((cstar ? w[3] : w[2]) >> ro) & 1;
+                            h = (w[1] >> (bb ? bi4 : 16 + bi4)) & 1;
+                            if (!EQ) {
+                                spar[t] = (uint8_t)(bb ^ cstar);
+                                spar[t - 1] = (uint8_t)bb;
+                            }
+                        } else {
+                            h = (w[0] >> bi4) & 1;
+                        }
+                    }
+                    st = (h << 9) | b9;
+                });
+            }
+            if (sub == 32) cbits[c] = acc;
+            else reinterpret_cast<uint16_t*>(cbits)[c] = (uint16_t)acc;
+            flag[0] = st;
+            if (stop) flag[2] = 1;
+            else if (G > 1 && c > 0)  // the walk ended at the chunk's first step: the slot of the previous chunk
+                flag[1] = (int)((buf[b * bufw + G * per_slot + (st >> 3)] >> (4 * (st & 7))) & 15u);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        if (flag[2]) return;  // first tail-biting pass: only the middle state was needed
+    }
+
+    // reconstruction: every thread, from the code bits and the state at t = 0
+    const unsigned st0 = (unsigned)flag[3];
+    float* rn = p.rec + (size_t)n * p.ld;
+    for (int t = tid; t < T; t += nthr) {
+        unsigned s = t < 10 ? (st0 << t) & 1023u : 0u;
+#pragma unroll
+        for (int q = 0; q < 10; q++) {
+            const int tq = t - q;
+            if (tq >= 1) s |= ((cbits[tq >> 5] >> (tq & 31)) & 1u) << q;
+        }
+        const int gg = sg[t / sub];
+        const int lb = label_rt((int)s, p);
+        const int gi = p.cand ? (int)p.gcand[((size_t)n * p.nsl + t / sub) * G + gg] : gg;
+        const float gt = s_gain[gi];
+        const float* tt = s_tab + lb * U;
+        const int tp = (t + p.rot) % p.ld;
+        const float xt = xrow[tp];
+        float bestd = BIG, val = 0.f;
+        int bu = 0;
+        for (int u = MD ? spar[t] : 0; u < U; u += MD ? 2 : 1) {
+            const float v = __fmul_rn(gt, tt[u]);
+            const float d = __fmaf_rn(-gt, tt[u], xt);
+            const float dd = __fmul_rn(d, d);
+            if (dd < bestd) { bestd = dd; val = v; bu = u; }
+        }
+        rn[tp] = val;
+        if (p.code) p.code[(size_t)n * p.ld + tp] = (gi << 16) | (lb * U + bu);
+    }
+}
 
 // shared memory of the fused kernel: the larger forward layout; the traceback region and the feedback scratch reuse
 // the forward pass's metric region (dead once a forward pass has ended)
@@ -53,6 +244,8 @@ __host__ __device__ inline int ldlq_smem(const VitParams& a, const VitParams& b,
     const TbSmem TB = tb_smem(b.T, b.sub, b.nl, b.U, b.U_hi, b.W4, b.NB, 1);
     int need = off + (TA.per_warp > TB.per_warp ? TA.per_warp : TB.per_warp);
     if (need < off + 2 * 256 * 4) need = off + 2 * 256 * 4;
+    const int cb = tb_coop_bytes(a) > tb_coop_bytes(b) ? tb_coop_bytes(a) : tb_coop_bytes(b);
+    if (need < off + cb) need = off + cb;
     int total = A.total > B.total ? A.total : B.total;
     if (need > total) total = need;
     if (fb_off) *fb_off = off;
@@ -60,21 +253,19 @@ __host__ __device__ inline int ldlq_smem(const VitParams& a, const VitParams& b,
 }
 
 template <class MP, int MD>
-__device__ __forceinline__ void ldlq_tb(const VitParams& p, int n, int lane, unsigned char* smem, int fb_off,
-                                        const float* xr)
+__device__ __forceinline__ void ldlq_tb(const VitParams& p, int n, unsigned char* smem, int fb_off, const float* xr)
 {
     constexpr int NP = MD ? 2 : 1;
     const FwdSmem L = fwd_smem(p.T, p.G, p.Gfull, p.sub, p.nl, NP, p.U, p.U_hi);
-    vit_tb_tile<MD>(p, n, lane, reinterpret_cast<const float*>(smem + L.tab),
-                    reinterpret_cast<const float*>(smem + L.tabhi), reinterpret_cast<const float*>(smem + L.gain),
-                    reinterpret_cast<const float*>(smem + L.gainhi), smem + fb_off, xr);
+    tb_coop<MD>(p, n, smem + fb_off, reinterpret_cast<const float*>(smem + L.tab),
+                reinterpret_cast<const float*>(smem + L.gain), xr);
 }
 
 template <class MP, int MD>
 __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) ldlq_block_kernel(const LdlqParams q)
 {
     extern __shared__ __align__(16) unsigned char smem[];
-    const int n = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int n = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x;
     const long long row0 = 16LL * n;
     float* wsub = q.wsub + row0 * 256;
     float* xr = q.xbuf + (size_t)n * 256;
@@ -98,13 +289,17 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) ldlq_block_kernel(const 
         }
         __syncthreads();
         const float* wr = q.dwrows + (size_t)ib * 256;
+        // the traceback stages the survivor words and merge winners with L2 copies (cp.async.cg): each thread's
+        // stores of the forward pass must reach L2 before the barrier that starts the traceback
         vit_fwd_tile<MP, MD, false>(q.p1, n, smem, xr, wr);
+        __threadfence();
         __syncthreads();
-        if (warp == 0) ldlq_tb<MP, MD>(q.p1, n, lane, smem, q.fb_off, xr);
+        ldlq_tb<MP, MD>(q.p1, n, smem, q.fb_off, xr);
         __syncthreads();
         vit_fwd_tile<MP, MD, false>(q.p2, n, smem, xr, wr);
+        __threadfence();
         __syncthreads();
-        if (warp == 0) ldlq_tb<MP, MD>(q.p2, n, lane, smem, q.fb_off, xr);
+        ldlq_tb<MP, MD>(q.p2, n, smem, q.fb_off, xr);
         __syncthreads();
         for (int i = tid; i < 256; i += nthr) {
             const int r = i >> 4, c = i & 15;

@@ -41,6 +41,47 @@ def _stream(dev) -> int:
 _SIGNS: Dict[tuple, torch.Tensor] = {}
 
 
+# ------------------------------------------------------------------------------------------------
+# fp32 products of the LDLQ update and the refits.  "fp32": torch's fp32 matmul (the reference's operation, bit for
+# bit).  "bf16x6": each fp32 operand is split as x = x0 + x1 + x2 in bf16 (x0 = bf16(x), x1 = bf16(x - x0), ...,
+# 24 significand bits together) and the six leading products a_i b_j (i + j <= 2) run as ONE bf16 tensor-core GEMM over
+# the K-concatenated parts with fp32 accumulation; the dropped terms are ~2^-24 relative, i.e. fp32-level accuracy,
+# with the arithmetic on the tensor pipes instead of the FP32 SIMT pipes the Viterbi kernels use.
+# ------------------------------------------------------------------------------------------------
+GEMM_MODES = ("fp32", "bf16x6")
+
+
+def _split3(x: torch.Tensor) -> tuple:
+    x0 = x.to(torch.bfloat16)
+    r = x - x0.float()
+    x1 = r.to(torch.bfloat16)
+    x2 = (r - x1.float()).to(torch.bfloat16)
+    return x0, x1, x2
+
+
+def _acat(p: tuple) -> torch.Tensor:
+    """Left operand [M, 6K]: parts in the order pairing with _bcat's rows (a0 b0, a0 b1, a1 b0, a0 b2, a1 b1, a2 b0)."""
+    return torch.cat([p[0], p[0], p[1], p[0], p[1], p[2]], dim=1)
+
+
+def _bcat(p: tuple) -> torch.Tensor:
+    """Right operand [6K, N]."""
+    return torch.cat([p[0], p[1], p[0], p[2], p[1], p[0]], dim=0)
+
+
+def _mm6(acat: torch.Tensor, bcat: torch.Tensor) -> torch.Tensor:
+    return torch.mm(acat, bcat, out_dtype=torch.float32)
+
+
+def _mm(a: torch.Tensor, b: torch.Tensor, gemm: str) -> torch.Tensor:
+    """a @ b for fp32 [M, K] x [K, N] in the given mode."""
+    if gemm == "fp32":
+        return a @ b
+    if gemm != "bf16x6":
+        raise ValueError(f"gemm mode {gemm!r}: expected one of {GEMM_MODES}")
+    return _mm6(_acat(_split3(a)), _bcat(_split3(b)))
+
+
 def make_rademacher_signs(dim: int, seed: int, device) -> torch.Tensor:
     """Deterministic +-1 signs from a CPU generator (src/iqk_format.py:173-179).  Device copies are cached, so a
     quantization in flight on a side stream never waits on a pageable host-to-device copy."""
@@ -174,6 +215,12 @@ class _TcqRunner(_FormatArgs):
             _stream(self.dev)), "tcq_viterbi")
 
 
+# When a list, every fused block launch appends (start event, end event, add-compare-selects, weights), the events
+# recorded on the launch's stream:
+# the live roofline of the block kernel in bench.py.
+BLOCK_EVENTS: Optional[list] = None
+
+
 class _BlockRunner(_FormatArgs):
     """Fused block kernel (ltq_ldlq_block) over the M rows of one row group: workspace."""
 
@@ -187,12 +234,28 @@ class _BlockRunner(_FormatArgs):
     def run(self, W_work, c0: int, d_rb_all, ibl: int, diag_w, Uc, U_blk_inv, G, idx, gi):
         """Block [c0, c0 + 256): G / idx / gi of the block's columns (W_work is read, not written)."""
         K = W_work.shape[1]
+        ev = BLOCK_EVENTS
+        if ev is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
         _check(_lib.lib().ltq_ldlq_block(
             ptr(W_work) + 4 * c0, W_work.stride(0), ptr(d_rb_all) + 4 * ibl, d_rb_all.stride(0), ptr(diag_w) + 4 * c0,
             ptr(Uc) + 4 * (c0 * Uc.stride(0) + c0), Uc.stride(0), ptr(U_blk_inv), U_blk_inv.stride(0),
             ptr(G) + 4 * c0, G.stride(0), ptr(idx) + 2 * c0, ptr(gi) + c0, K, self.M, ptr(self.lut), ptr(self.gains),
             self.K, self.cfg["m"], self.me_ptr(), len(self.m_extra), self.gains.numel(), self.n_cand, self.sub,
             self.pp, self.tb_window, ptr(self.ws), self.ws.numel(), _stream(self.dev)), "ltq_ldlq_block")
+        if ev is not None:
+            e1.record()
+            ev.append((e0, e1, self.acs_per_block(), self.M * 256))
+
+    def acs_per_block(self) -> int:
+        """Add-compare-selects of one block launch: M x 256 weights x passes (1 + 2 W / 256 for the windowed first
+        pass) x 1024 states x gain slots x parity classes."""
+        g = self.gains.numel()
+        if 0 < self.n_cand < g:
+            g = self.n_cand
+        passes = 1.0 + (2.0 * self.tb_window / 256.0 if self.tb_window else 1.0)
+        return int(self.M * 256 * passes * 1024 * g * (2 if self.pp else 1))
 
 
 def _drive(gen):
@@ -206,14 +269,17 @@ def _drive(gen):
 
 @torch.no_grad()
 def _rows_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: torch.Tensor, diag_w: torch.Tensor, spec_name: str,
-               fused: bool = True) -> Tuple[torch.Tensor, torch.Tensor, dict]:
+               fused: bool = True, gemm: str = "fp32") -> Tuple[torch.Tensor, torch.Tensor, dict]:
     """Block16-LDLQ of one row group (src/liqk_v2.py:872-1021, row-scale branch :956-980) on the current stream,
-    without host synchronisation.  Returns (d_full fp16 [M, K/256], W_hat_rot [M, K], group fields)."""
-    return _drive(_rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name, fused))
+    without host synchronisation.  Returns (d_full fp16 [M, K/256], W_hat_rot [M, K], group fields).  gemm: the mode of
+    the inter-block update products (see GEMM_MODES)."""
+    return _drive(_rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name, fused, gemm))
 
 
-def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool = True):
-    """_rows_ldlq as a generator that yields after each 256-column block's launches (for interleaved issue)."""
+def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool = True, gemm: str = "fp32",
+                     U_parts: Optional[tuple] = None):
+    """_rows_ldlq as a generator that yields after each 256-column block's launches (for interleaved issue).
+    U_parts: the bf16 split of U when the caller already has it (bf16x6 mode)."""
     cfg = TCQ_CONFIG[spec_name]
     if not (cfg.get("row_scale") and cfg.get("tb")):
         raise ValueError(f"{spec_name}: only the tail-biting row-scale (.ltq) TCQ formats are on this path")
@@ -240,6 +306,17 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
     group = {"spec": spec_name, "d_row": d_row, "e": e_rb, "idx": idx, "gi": gi, "G": G}
 
     Uc = U.contiguous()
+    if gemm == "bf16x6" and U_parts is None and nblocks > 1:
+        U_parts = _split3(Uc)
+
+    def inter_block(err_in, c0, c1, U_blk_inv):  # W_work[:, c1:] -= ((w_blk - what) @ U_blk_inv) @ U[c0:c1, c1:]
+        if gemm == "fp32":
+            err_blk = err_in @ U_blk_inv
+            W_work[:, c1:] -= err_blk @ Uc[c0:c1, c1:]
+        else:
+            err_blk = _mm(err_in, U_blk_inv, gemm)
+            W_work[:, c1:] -= _mm6(_acat(_split3(err_blk)), _bcat(tuple(p[c0:c1, c1:] for p in U_parts)))
+
     if fused:
         brun = _BlockRunner(spec_name, M, device)
         dwc = diag_w.float().contiguous()
@@ -252,8 +329,7 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
             W_hat_rot[:, c0:c1] = best_what_row
             d_full[:, ibl] = d_rb.to(torch.float16)
             if c1 < K:
-                err_blk = (W_work[:, c0:c1] - best_what_row) @ U_blk_inv
-                W_work[:, c1:] -= err_blk @ Uc[c0:c1, c1:]
+                inter_block(W_work[:, c0:c1] - best_what_row, c0, c1, U_blk_inv)
             yield
         return d_full, W_hat_rot, group
 
@@ -279,8 +355,7 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
         W_hat_rot[:, c0:c1] = best_what_row
         d_full[:, ibl] = d_rb.to(torch.float16)
         if c1 < K:
-            err_blk = (w_blk_start - best_what_row) @ U_blk_inv
-            W_work[:, c1:] -= err_blk @ Uc[c0:c1, c1:]
+            inter_block(w_blk_start - best_what_row, c0, c1, U_blk_inv)
         yield
     return d_full, W_hat_rot, group
 
@@ -300,17 +375,20 @@ def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: to
 @torch.no_grad()
 def _quantize_matrix_core(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
                           row_weights: Optional[torch.Tensor] = None, want_pack: bool = False,
-                          rows_fn=None) -> dict:
+                          rows_fn=None, gemm: str = "fp32") -> dict:
     """_quantize_matrix_steps run to its end (see there)."""
-    return _drive(_quantize_matrix_steps(W, H, spec_or_row_specs, seed, damp, row_weights, want_pack, rows_fn))
+    return _drive(_quantize_matrix_steps(W, H, spec_or_row_specs, seed, damp, row_weights, want_pack, rows_fn, gemm))
 
 
 def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
-                           row_weights: Optional[torch.Tensor] = None, want_pack: bool = False, rows_fn=None):
+                           row_weights: Optional[torch.Tensor] = None, want_pack: bool = False, rows_fn=None,
+                           gemm: str = "fp32"):
     """The computation of quantize_matrix_liqk_v2 (src/liqk_v2.py:1029-1198) for the TCQ formats, on the current
     stream and without host synchronisation (with row_weights=None): the reference's data-dependent host branches
     become device-side selections of the same tensors (torch.where), its raising Cholesky / solve their *_ex forms.
     Returns device tensors: qdata, W_hat, num / den of the relative loss, chol_info, and with want_pack the .ltq fields.
+    gemm: the mode of the LDLQ inter-block update and refit products ("fp32": the reference's torch operations bit for
+    bit; "bf16x6": fp32-accurate split products on the tensor cores, see GEMM_MODES).
     rows_fn: the row-group quantizer called for each format's rows (default: the block-stepped _rows_ldlq).  A
     generator: it yields after the Hessian preparation and after each 256-column block, so that a scheduler can
     interleave the launches of several matrices on several streams; its return value is the result dict."""
@@ -338,6 +416,7 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     eye256 = torch.eye(QK_K, dtype=torch.float32, device=W.device).unsqueeze(0).expand(nblocks, -1, -1)
     U_blks = torch.stack([U[b * QK_K:(b + 1) * QK_K, b * QK_K:(b + 1) * QK_K] for b in range(nblocks)], dim=0)
     U_blks_inv = torch.linalg.solve_triangular(U_blks, eye256, upper=True)
+    U_parts = _split3(U.contiguous()) if gemm == "bf16x6" and nblocks > 1 else None
     yield
 
     row_slices = [(0, M, spec_or_row_specs)] if isinstance(spec_or_row_specs, str) else spec_or_row_specs
@@ -357,7 +436,7 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
         if len(ranges) == 1 and ranges[0] == (0, M):
             rows_idx = None
             if rows_fn is None:
-                d_sub, Wh_sub, g = yield from _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, sp)
+                d_sub, Wh_sub, g = yield from _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, sp, True, gemm, U_parts)
             else:
                 d_sub, Wh_sub, g = rows_fn(W_rot, U, U_blks_inv, diag_w, sp)
             W_hat_rot, d_full = Wh_sub, d_sub
@@ -367,7 +446,8 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
             continue
         rows_idx = torch.cat([torch.arange(r0, r1, device=W.device) for r0, r1 in ranges], dim=0)
         if rows_fn is None:
-            d_sub, Wh_sub, g = yield from _rows_ldlq_steps(W_rot[rows_idx], U, U_blks_inv, diag_w, sp)
+            d_sub, Wh_sub, g = yield from _rows_ldlq_steps(W_rot[rows_idx], U, U_blks_inv, diag_w, sp, True, gemm,
+                                                           U_parts)
         else:
             d_sub, Wh_sub, g = rows_fn(W_rot[rows_idx], U, U_blks_inv, diag_w, sp)
         W_hat_rot[rows_idx] = Wh_sub
@@ -375,13 +455,21 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
         if pm is not None:
             for k in ("idx", "gi", "G", "d_row", "e"):
                 pm[k][rows_idx] = g[k].to(pm[k].dtype)
-    del U, U_blks_inv, W_rot
+    del U, U_blks_inv, W_rot, U_parts
 
+    if gemm == "fp32":
+        def times_h(A):
+            return A @ H_f32
+    else:
+        Hb = _bcat(_split3(H_f32))  # the split of H, shared by every product with H
+
+        def times_h(A):
+            return _mm6(_acat(_split3(A)), Hb)
     U_base = fwht_inplace(W_hat_rot.clone(), block_size=QK_K)
     W_hat_eff = U_base * suh.unsqueeze(0)
     c_pack = torch.ones((M,), dtype=torch.float32, device=W.device)
-    HW = W_f32 @ H_f32
-    HQ = W_hat_eff @ H_f32
+    HW = times_h(W_f32)
+    HQ = times_h(W_hat_eff)
     c_row = (W_hat_eff * HW).sum(dim=1) / (W_hat_eff * HQ).sum(dim=1).clamp(min=1e-12)
     c_row = torch.where(torch.isfinite(c_row) & (c_row > 0.5) & (c_row < 2.0), c_row, torch.ones_like(c_row))
     d_new = (d_full.float() * c_row.unsqueeze(1)).to(torch.float16)
@@ -394,7 +482,7 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     else:
         rw = torch.ones((M,), dtype=torch.float32, device=W.device)
         U_w = U_scaled
-    A_in = (U_w.T @ U_scaled) * H_f32
+    A_in = (U_w.T @ U_scaled if gemm == "fp32" else _mm(U_w.T, U_scaled, gemm)) * H_f32
     b_in = (U_w * HW).sum(dim=0)
     A_in.diagonal().add_(1e-3 * A_in.diagonal().mean().clamp(min=1e-12))
     # the reference solves, and keeps the refit when the solve succeeds and lowers the loss (src/liqk_v2.py:1161-1180)
@@ -403,7 +491,7 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     valid_s = torch.isfinite(suh_cand) & (suh_cand.abs() > 0.05) & (suh_cand.abs() < 10.0)
     suh_cand = torch.where(valid_s, suh_cand, suh)
     W_hat_cand = U_scaled * suh_cand.unsqueeze(0)
-    HQ_cand = W_hat_cand @ H_f32
+    HQ_cand = times_h(W_hat_cand)
     diff_base = W_f32 - W_hat_eff
     diff_cand = W_f32 - W_hat_cand
     loss_base = (((HW - HQ) * diff_base).sum(dim=1) * rw).sum()
@@ -422,9 +510,10 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
         scale = d_row_p.float().unsqueeze(1) * torch.exp2(0.25 * pm["e"].float())
         Wq_rot = (scale.unsqueeze(2) * pm["G"].view(M, nblocks, QK_K)).view(M, K)
         W_hat_eff = fwht_inplace(Wq_rot, block_size=QK_K) * suh_p.float().unsqueeze(0)
-        HQ = W_hat_eff @ H_f32
+        HQ = times_h(W_hat_eff)
         pack = {"row_slices": row_slices, "idx": pm["idx"], "gi": pm["gi"], "G": pm["G"], "d_row": d_row_p,
                 "e": pm["e"], "suh": suh_p}
+    del times_h
     diff = W_f32 - W_hat_eff
     num = ((HW - HQ) * diff).sum()
     den = (HW * W_f32).sum().clamp(min=1e-12)

@@ -240,3 +240,30 @@ def test_ldlq_fused_block_equals_per_subblock(spec, cuda_dev, monkeypatch):
     gains = L.make_gains(cfg["h"], cfg["step"], cuda_dev)
     idx, gi, G = outs[0][2], outs[0][3], outs[0][4]
     assert torch.equal(G, gains[gi.long()] * lut[idx.long()])
+
+
+@pytest.mark.parametrize("spec", ["TCQ3X", "TCQ25X", "TCQ275X2"])
+def test_fused_block_deterministic_full_waves(spec, cuda_dev):
+    """Two full waves of the fused block kernel (2 x 148 x 7 tile groups) give identical bits on repeated launches: the
+    survivor words the forward writes and the traceback stages through L2 must never be read stale."""
+    import ltq_research_b200.liqk_v2 as L
+    rows = 2 * 148 * 7 * 16
+    g = torch.Generator(device=cuda_dev).manual_seed(3)
+    W = torch.randn(rows, 256, device=cuda_dev, generator=g)
+    A = torch.randn(256, 256, device=cuda_dev, generator=g) / 16
+    U = torch.triu(A) + 4 * torch.eye(256, device=cuda_dev)
+    Ui = torch.linalg.solve_triangular(U, torch.eye(256, device=cuda_dev), upper=True).contiguous()
+    d_rb = torch.rand(rows, 1, device=cuda_dev, generator=g) + 0.5
+    dw = (1.0 / torch.diagonal(U) ** 2).contiguous()
+    br = L._BlockRunner(spec, rows, cuda_dev)
+    outs = []
+    for _ in range(3):
+        G = torch.empty(rows, 256, device=cuda_dev)
+        idx = torch.empty(rows, 256, dtype=torch.int16, device=cuda_dev)
+        gi = torch.empty(rows, 256, dtype=torch.uint8, device=cuda_dev)
+        br.run(W, 0, d_rb, 0, dw, U, Ui, G, idx, gi)
+        outs.append((G, idx, gi))
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        for a, b in zip(outs[0], o):
+            assert torch.equal(a, b), spec
