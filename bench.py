@@ -336,7 +336,7 @@ def main():
     packed_bytes = sum(int(r["ltq"]["data"].numel()) for r in res)
 
     # end to end through the public API: pinned host inputs in, the packed .ltq tensors back in pinned host memory
-    e2e_ms, h2d, d2h = None, 0, 0
+    e2e_ms, h2d, d2h, e2e_same = None, 0, 0, None
     if not args.no_e2e:
         host = [(W.cpu().pin_memory(), H.cpu().pin_memory(), sp) for W, H, sp in timed]
         h2d = sum(W.numel() * W.element_size() + H.numel() * H.element_size() for W, H, _ in host)
@@ -349,9 +349,8 @@ def main():
         e2e_ms = a.elapsed_time(b)
         d2h = sum(sum(r["ltq"][k].numel() * r["ltq"][k].element_size() for k in ("data", "d_row", "e", "suh"))
                   for r in res_h)
-        # the host run's packed bytes are the device run's
-        for r0, r1 in zip(res, res_h):
-            assert torch.equal(r0["ltq"]["data"].cpu(), r1["ltq"]["data"]), "e2e output differs from the timed run"
+        # the host run's packed bytes against the device run's (the pipeline is deterministic: expected all equal)
+        e2e_same = sum(int(torch.equal(r0["ltq"]["data"].cpu(), r1["ltq"]["data"])) for r0, r1 in zip(res, res_h))
         del host, res_h
 
     t = torch.tensor([dev_ms, e2e_ms or 0.0], device=dev)
@@ -370,8 +369,8 @@ def main():
         traffic = None
         if prof.exists():
             bpw = json.loads(prof.read_text()).get("dram_bytes_per_weight")
-            if bpw:
-                traffic = bpw * block_weights / len(ev)  # per average launch: weights x DRAM bytes per weight
+            if bpw:  # per average launch: weights x DRAM bytes per weight (ncu capture; mean of the two formats)
+                traffic = float(np.mean(list(bpw.values()))) * block_weights / len(ev)
         cpu = None if args.no_cpu_baseline else cpu_baseline_sample()
         line = {
             "metric": METRIC, "value": value, "unit": METRIC, "n_gpus": world, "steps": args.steps,
@@ -393,7 +392,8 @@ def main():
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {
                 "value": total / (e2e_max * 1e-3) / 1e6, "unit": METRIC,
-                "h2d_bytes_per_step": int(h2d // args.steps), "d2h_bytes_per_step": int(d2h // args.steps)},
+                "h2d_bytes_per_step": int(h2d // args.steps), "d2h_bytes_per_step": int(d2h // args.steps),
+                "ltq_identical_to_timed_run": f"{e2e_same}/{len(res)} matrices"},
             "gpu_launches": int(launches),
             "clocks": clocks,
         }
