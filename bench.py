@@ -343,12 +343,24 @@ def main():
         barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        res_h = quantize_matrices(host, n_streams=args.streams, ltq_formats=fmts, pack=False, to_host=True)
+        if dist is None:  # one GPU: the packed tensors come back to pinned host memory on the matrices' streams
+            res_h = quantize_matrices(host, n_streams=args.streams, ltq_formats=fmts, pack=False, to_host=True)
+            d2h = sum(sum(r["ltq"][k].numel() * r["ltq"][k].element_size() for k in ("data", "d_row", "e", "suh"))
+                      for r in res_h)
+        else:  # several GPUs: every rank's packed tensors go to rank 0 in one NCCL gather, then to its host memory
+            from ltq_research_b200.shard import gather_ltq
+            res_h = quantize_matrices(host, n_streams=args.streams, ltq_formats=fmts, pack=False)
+            got = gather_ltq({rank * len(res_h) + i: r["ltq"] for i, r in enumerate(res_h)}, dst=0)
+            if rank == 0:
+                res_h = [{"ltq": got[i]} for i in range(len(res_h))]
+                d2h = sum(sum(t.numel() * t.element_size() for k, t in d.items() if k in ("data", "d_row", "e", "suh"))
+                          for d in got.values())
+            else:
+                res_h = [{"ltq": {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in r["ltq"].items()}}
+                         for r in res_h]
         b.record()
         barrier()
         e2e_ms = a.elapsed_time(b)
-        d2h = sum(sum(r["ltq"][k].numel() * r["ltq"][k].element_size() for k in ("data", "d_row", "e", "suh"))
-                  for r in res_h)
         # the host run's packed bytes against the device run's (the pipeline is deterministic: expected all equal)
         e2e_same = sum(int(torch.equal(r0["ltq"]["data"].cpu(), r1["ltq"]["data"])) for r0, r1 in zip(res, res_h))
         del host, res_h

@@ -41,6 +41,19 @@ def estimated_seconds(M: int, K: int, spec: Spec) -> float:
     return t + (3.0 * K ** 3 + 8.0 * M * K * K) / 50e12
 
 
+_STREAMS: Dict[tuple, List[torch.cuda.Stream]] = {}
+
+
+def _streams(dev: torch.device, n: int) -> List[torch.cuda.Stream]:
+    """The driver's CUDA streams on `dev`, created once and reused by every call: the caching allocator keeps freed
+    blocks per stream, so reusing the streams lets each call reuse the memory the previous calls cached (fresh streams
+    on every call would allocate anew and grow the reserved memory call after call)."""
+    key = (str(dev), n)
+    if key not in _STREAMS:
+        _STREAMS[key] = [torch.cuda.Stream(dev) for _ in range(n)]
+    return _STREAMS[key]
+
+
 def _record(obj, stream: torch.cuda.Stream):
     if torch.is_tensor(obj):
         if obj.is_cuda:
@@ -83,7 +96,7 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
         raise RuntimeError("quantize_matrices: a CUDA device is required; there is no CPU path")
     _lib.lib()
     main = torch.cuda.current_stream(dev)
-    streams = [torch.cuda.Stream(dev) for _ in range(max(1, n_streams))]
+    streams = _streams(dev, max(1, n_streams))
     cost = [estimated_seconds(W.shape[0], W.shape[1], sp) for W, _, sp in jobs]
     pending = sorted(range(len(jobs)), key=lambda i: -cost[i])[::-1]  # pop() takes the longest remaining job
     out: List[Optional[Dict]] = [None] * len(jobs)

@@ -93,16 +93,12 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
     const int v4 = per_slot / 4;
     auto stage = [&](int c, int b, int t0, int ts) {
         uint32_t* d = buf + b * bufw;
-        const int nv = G * v4 + ((G > 1 && c > 0) ? NS / 32 : 0);
-        for (int i = t0; i < nv; i += ts) {
-            if (i < G * v4) {
-                const int g = i / v4, r = i - g * v4;
-                cp_async16(d + g * per_slot + 4 * r,
-                           p.svA + ((size_t)n * G + g) * (size_t)p.capA + (size_t)c * per_slot + 4 * r);
-            } else {
-                const int k = i - G * v4;
-                cp_async16(d + G * per_slot + 4 * k, p.gsw + ((size_t)n * p.nsl + c) * (NS / 8) + 4 * k);
-            }
+        const uint32_t* src = p.svA + (size_t)n * G * (size_t)p.capA + (size_t)c * per_slot;
+        for (int g = 0; g < G; g++, d += per_slot, src += p.capA)
+            for (int r = t0; r < v4; r += ts) cp_async16(d + 4 * r, src + 4 * r);
+        if (G > 1 && c > 0) {  // d now points at the merge-winner words of the buffer
+            const uint32_t* gsrc = p.gsw + ((size_t)n * p.nsl + c) * (NS / 8);
+            for (int k = t0; k < NS / 32; k += ts) cp_async16(d + 4 * k, gsrc + 4 * k);
         }
     };
     if (tid == 0) {

@@ -547,29 +547,58 @@ static __device__ __forceinline__ void merge_any(int G, const float* s_dp, float
 }
 
 // branch-error table of one sub-block for one gain slot (src/cuda/tcq_viterbi.cu:202-213): for each step, label and
-// parity class, w * min_u (x - g tab[u])^2, written in the NV label variants err'[P][v] = err[v ^ (P << 1)]
-template <int NL, int NP, bool MD>
-static __device__ __noinline__ void build_err(float* myerr, const float* s_x, const float* s_w, const float* s_tab,
-                                              const float* s_tabhi, float gain, float gainhi, int t0, int sub, int U,
-                                              int U_hi, int mix, int lane)
+// parity class, w * min_u (x - g tab[u])^2, written in the NV label variants err'[P][v] = err[v ^ (P << 1)].
+// UC > 0: the table width U as a compile-time constant (the minimum over u unrolled, same operations in the same
+// order); UC = 0: any U and the half-integer tables (mix > 0).
+template <int NL, int NP, bool MD, int UC>
+static __device__ __noinline__ void build_err_u(float* myerr, const float* s_x, const float* s_w, const float* s_tab,
+                                                const float* s_tabhi, float gain, float gainhi, int t0, int sub, int U,
+                                                int U_hi, int mix, int lane)
 {
     constexpr int NV = NL / 2, EW = NL * NP;
     __syncwarp();
     for (int it = lane; it < sub * NL * NP; it += 32) {
         const int tt = it / (NL * NP), lb = (it / NP) % NL, pc = it % NP;
         const int t = t0 + tt;
-        const bool hi = !MD && mix > 0 && ((t / mix) & 1);
         const float x = s_x[t];
         float e;
-        if (MD) e = branch_err(x, gain, s_tab + lb * U, pc, 2, U);
-        else if (hi) e = branch_err(x, gainhi, s_tabhi + lb * U_hi, 0, 1, U_hi);
-        else e = branch_err(x, gain, s_tab + lb * U, 0, 1, U);
+        if constexpr (UC > 0) {
+            const float* tl = s_tab + lb * UC + (MD ? pc : 0);
+            e = BIG;
+#pragma unroll
+            for (int u = 0; u < UC; u += MD ? 2 : 1) {
+                const float d = __fmaf_rn(-gain, tl[u], x);
+                e = fminf(e, __fmul_rn(d, d));
+            }
+        } else {
+            const bool hi = !MD && mix > 0 && ((t / mix) & 1);
+            if (MD) e = branch_err(x, gain, s_tab + lb * U, pc, 2, U);
+            else if (hi) e = branch_err(x, gainhi, s_tabhi + lb * U_hi, 0, 1, U_hi);
+            else e = branch_err(x, gain, s_tab + lb * U, 0, 1, U);
+        }
         e = __fmul_rn(e, s_w[t]);
         float* dst = myerr + (size_t)tt * NV * EW + pc;
 #pragma unroll
         for (int P = 0; P < NV; P++) dst[P * EW + (lb ^ (P << 1)) * NP] = e;
     }
     __syncwarp();
+}
+
+template <int NL, int NP, bool MD>
+static __device__ __forceinline__ void build_err(float* myerr, const float* s_x, const float* s_w, const float* s_tab,
+                                                 const float* s_tabhi, float gain, float gainhi, int t0, int sub,
+                                                 int U, int U_hi, int mix, int lane)
+{
+    if (mix == 0) {
+        switch (U) {
+            case 2: build_err_u<NL, NP, MD, 2>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
+            case 4: build_err_u<NL, NP, MD, 4>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
+            case 8: build_err_u<NL, NP, MD, 8>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
+            case 16: build_err_u<NL, NP, MD, 16>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
+            default: break;
+        }
+    }
+    build_err_u<NL, NP, MD, 0>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane);
 }
 
 // ------------------------------------------------------------------------------------------------

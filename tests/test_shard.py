@@ -1,0 +1,99 @@
+"""Sharding across ranks (ltq_research_b200.shard) on CPU: the longest-first assignment, and the end-of-run gather of
+the packed .ltq tensors over a world-size-2 gloo process group (the same collective code runs over NCCL on the GPUs);
+a rank that leaves before the gather makes the other rank's gather fail within the process-group timeout instead of
+waiting for ever."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from ltq_research_b200.batch import estimated_seconds
+from ltq_research_b200.shard import assign
+
+LAYER = [(3072, 3072), (1024, 3072), (1024, 3072), (3072, 3072), (8192, 3072), (8192, 3072), (3072, 8192)]
+
+
+def _shapes(n_layers=4):
+    return [(M, K, "TCQ3X" if l % 2 == 0 else "TCQ25X") for l in range(n_layers) for M, K in LAYER]
+
+
+def test_assign_is_complete_deterministic_and_balanced():
+    shapes = _shapes()
+    for world in (1, 2, 3, 8):
+        a = assign(shapes, world)
+        assert a == assign(shapes, world)
+        assert sorted(i for lst in a for i in lst) == list(range(len(shapes)))
+        cost = [estimated_seconds(*s) for s in shapes]
+        loads = [sum(cost[i] for i in lst) for lst in a]
+        assert max(loads) <= sum(cost) / world + max(cost) + 1e-12
+    with pytest.raises(ValueError):
+        assign(shapes, 0)
+
+
+def _fake_ltq(i):
+    g = torch.Generator().manual_seed(i)
+    M, K = 16 * (1 + i % 3), 256
+    return {"data": torch.randint(0, 256, (1000 + 64 * i,), generator=g, dtype=torch.uint8),
+            "slices": [[0, M, i % 2, 0]],
+            "d_row": torch.randn(M, generator=g).to(torch.float16),
+            "e": torch.randint(-16, 16, (M, K // 256), generator=g, dtype=torch.int8),
+            "suh": torch.randn(K, generator=g).to(torch.float16)}
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, mode, q):
+    import datetime
+    import torch.distributed as dist
+    from ltq_research_b200.shard import gather_ltq
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    mine = assign(_shapes(2), world)[rank]
+    if mode == "leave" and rank == 1:
+        os._exit(0)  # leaves between steps, with no collective in flight
+    try:
+        out = gather_ltq({i: _fake_ltq(i) for i in mine}, dst=0)
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", type(e).__name__))
+        return
+    if rank == 0:
+        ok = sorted(out) == list(range(len(_shapes(2))))
+        for i, d in out.items():
+            w = _fake_ltq(i)
+            ok = ok and d["slices"] == w["slices"] and all(torch.equal(d[k], w[k]) for k in ("data", "d_row", "e", "suh"))
+        q.put((rank, "ok" if ok else "mismatch", None))
+    else:
+        q.put((rank, "ok" if out is None else "unexpected", None))
+    dist.destroy_process_group()
+
+
+def _run(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    n = 2 if mode == "ok" else 1
+    res = sorted(q.get(timeout=120) for _ in range(n))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return res
+
+
+def test_gather_ltq_world2_gloo():
+    assert _run("ok") == [(0, "ok", None), (1, "ok", None)]
+
+
+def test_gather_ltq_peer_leaves_gloo():
+    res = _run("leave")
+    assert res[0][0] == 0 and res[0][1] == "error", res
