@@ -258,7 +258,7 @@ __device__ __forceinline__ void ldlq_tb(const VitParams& p, int n, unsigned char
 }
 
 template <class MP, int MD>
-__global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) ldlq_block_kernel(const LdlqParams q)
+__global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) ldlq_block_kernel(const __grid_constant__ LdlqParams q)
 {
     extern __shared__ __align__(16) unsigned char smem[];
     const int n = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x;
@@ -287,16 +287,16 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) ldlq_block_kernel(const 
         const float* wr = q.dwrows + (size_t)ib * 256;
         // the traceback stages the survivor words and merge winners with L2 copies (cp.async.cg): each thread's
         // stores of the forward pass must reach L2 before the barrier that starts the traceback
-        vit_fwd_tile<MP, MD, false>(q.p1, n, smem, xr, wr);
-        __threadfence();
-        __syncthreads();
-        ldlq_tb<MP, MD>(q.p1, n, smem, q.fb_off, xr);
-        __syncthreads();
-        vit_fwd_tile<MP, MD, false>(q.p2, n, smem, xr, wr);
-        __threadfence();
-        __syncthreads();
-        ldlq_tb<MP, MD>(q.p2, n, smem, q.fb_off, xr);
-        __syncthreads();
+        // both passes run the same code (one copy of the forward and traceback bodies in the instruction cache)
+#pragma unroll 1
+        for (int ps = 0; ps < 2; ps++) {
+            const VitParams& pp = ps ? q.p2 : q.p1;
+            vit_fwd_tile<MP, MD, false>(pp, n, smem, xr, wr);
+            __threadfence();
+            __syncthreads();
+            ldlq_tb<MP, MD>(pp, n, smem, q.fb_off, xr);
+            __syncthreads();
+        }
         for (int i = tid; i < 256; i += nthr) {
             const int r = i >> 4, c = i & 15;
             const long long row = row0 + r;
