@@ -86,7 +86,7 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
     uint32_t* cbits = buf + 2 * bufw;
     uint8_t* sg = reinterpret_cast<uint8_t*>(cbits + MAXT / 32);
     uint8_t* spar = sg + 32;
-    int* flag = reinterpret_cast<int*>(spar + MAXT);  // [0] state, [1] slot, [2] stopped, [3] state at t = 0
+    int* flag = reinterpret_cast<int*>(spar + MAXT);  // [0] state, [1] slot, [3] state at t = 0
 
     // stage chunk c (all slots' words — per_slot consecutive words per slot in the survivor stream — and the merge
     // winners of boundary c) into buffer b with 16-byte asynchronous copies by threads t0, t0 + ts, ...
@@ -105,7 +105,6 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
         const int bi = p.best[n];
         flag[0] = bi % NS;
         flag[1] = bi / NS;
-        flag[2] = 0;
     }
     // the last chunk by every thread; then, while thread 0 walks chunk c, the staging threads (the warps that do not
     // walk, or lanes 1..31 when there is one warp) copy chunk c - 1 into the other buffer
@@ -114,6 +113,7 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
     cp_async_wait_all();
     __syncthreads();
     int pcur = 0, cstar = 0;  // thread 0: parity class of the current pair / quad (carried across steps)
+    bool stopped = false;     // thread 0: the walk reached the first-pass middle
     for (int c = nch - 1; c >= 0; c--) {
         const int b = c & 1, lo = c * sub;
         if (stager && c > 0) stage(c - 1, b ^ 1, G > 1 ? tid - 32 : tid - 1, G > 1 ? nthr - 32 : nthr - 1);
@@ -190,13 +190,14 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
             if (sub == 32) cbits[c] = acc;
             else reinterpret_cast<uint16_t*>(cbits)[c] = (uint16_t)acc;
             flag[0] = st;
-            if (stop) flag[2] = 1;
-            else if (G > 1 && c > 0)  // the walk ended at the chunk's first step: the slot of the previous chunk
+            stopped = stop;
+            if (!stop && G > 1 && c > 0)  // the walk ended at the chunk's first step: the slot of the previous chunk
                 flag[1] = (int)((buf[b * bufw + G * per_slot + (st >> 3)] >> (4 * (st & 7))) & 15u);
         }
         cp_async_wait_all();
-        __syncthreads();
-        if (flag[2]) return;  // first tail-biting pass: only the middle state was needed
+        // the stop travels with the barrier (bar.red.or): a flag in shared memory read after the barrier could already
+        // be overwritten by thread 0's walk of the next chunk, which no barrier separates from the read
+        if (__syncthreads_or(stopped)) return;  // first tail-biting pass: only the middle state was needed
     }
 
     // reconstruction: every thread, from the code bits and the state at t = 0

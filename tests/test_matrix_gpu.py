@@ -244,8 +244,11 @@ def test_ldlq_fused_block_equals_per_subblock(spec, cuda_dev, monkeypatch):
 
 @pytest.mark.parametrize("spec", ["TCQ3X", "TCQ25X", "TCQ275X2"])
 def test_fused_block_deterministic_full_waves(spec, cuda_dev):
-    """Two full waves of the fused block kernel (2 x 148 x 7 tile groups) give identical bits on repeated launches: the
-    survivor words the forward writes and the traceback stages through L2 must never be read stale."""
+    """Two full waves of the fused block kernel (2 x 148 x 7 tile groups) give identical bits on repeated launches, with
+    GEMMs on another stream competing for the SMs on every other launch: the survivor words the forward writes and the
+    traceback stages through L2 must never be read stale, and no warp may leave the traceback a barrier early (a stop
+    flag read after a barrier that the walking thread can overwrite before the next one did that, about once in
+    10^4 - 10^5 tile groups under load)."""
     import ltq_research_b200.liqk_v2 as L
     rows = 2 * 148 * 7 * 16
     g = torch.Generator(device=cuda_dev).manual_seed(3)
@@ -256,14 +259,22 @@ def test_fused_block_deterministic_full_waves(spec, cuda_dev):
     d_rb = torch.rand(rows, 1, device=cuda_dev, generator=g) + 0.5
     dw = (1.0 / torch.diagonal(U) ** 2).contiguous()
     br = L._BlockRunner(spec, rows, cuda_dev)
+    bg = torch.cuda.Stream(device=cuda_dev)
+    Ab = torch.randn(4096, 4096, device=cuda_dev, generator=g)
     outs = []
-    for _ in range(3):
+    for rep in range(8):
+        if rep % 2:
+            bg.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(bg):
+                for _ in range(3):
+                    Cb = Ab @ Ab
         G = torch.empty(rows, 256, device=cuda_dev)
         idx = torch.empty(rows, 256, dtype=torch.int16, device=cuda_dev)
         gi = torch.empty(rows, 256, dtype=torch.uint8, device=cuda_dev)
         br.run(W, 0, d_rb, 0, dw, U, Ui, G, idx, gi)
         outs.append((G, idx, gi))
     torch.cuda.synchronize()
+    del Cb
     for o in outs[1:]:
         for a, b in zip(outs[0], o):
             assert torch.equal(a, b), spec
