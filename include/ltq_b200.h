@@ -102,6 +102,32 @@ int ltq_ldlq_feedback(float* w, long long ld, int M, int s0, const float* d_rb, 
  * slots in the search (n_cand <= 4 or Gfull <= 4).
  */
 size_t ltq_ldlq_block_workspace_bytes(int M, int Gfull, int n_cand, int sub, int pp, int tb_window);
+/*
+ * The inter-block update after a block (src/liqk_v2.py:972-979),
+ *     W_work[:, c1:] -= ((w_blk - d_rb * G) @ Uinv_blk) @ U[c0:c1, c1:],
+ * as one fp32-accurate tensor-core GEMM acat @ bcat_b of bf16 operands (the three-way split x = x0 + x1 + x2,
+ * x0 = bf16(x), x1 = bf16(x - x0), x2 = bf16(x - x0 - x1), and the six products a0 b0 + a0 b1 + a1 b0 + a0 b2 + a1 b1 + a2 b0):
+ * ltq_ldlq_bcat, once per matrix: for every block b < K/256 - 1 (c0 = 256 b, c1 = c0 + 256) the [1536, K - c1] matrix
+ *   [u0; u1; u0; u2; u1; u0] of U[c0:c1, c1:K], contiguous, at element offset 1536 * sum_{b' < b} (K - 256 (b' + 1));
+ *   ltq_ldlq_bcat_elems(K) elements in all (bf16 bits).  U 16-byte aligned, ldU a multiple of 4.
+ * ltq_ldlq_inter, per block after ltq_ldlq_block: what = d * G and d_h = fp16(d) (d = max(d_rb, 1e-8)) — the
+ *   reference's own operations; with acat (else NULL, e.g. for the last block): err = (w_blk - what) @ Uinv (fp32
+ *   sequential fma chains, Uinv upper triangular) as acat [M, 1536] = [e0 e0 e1 e0 e1 e2] (bf16 bits, row stride 1536).
+ *   d_h may be NULL.  M % 16 == 0.
+ */
+/*
+ * ltq_bf16x6_split: one operand of that six-product form for a general fp32 product (the refits' products with H,
+ *   src/liqk_v2.py:1136-1170): order 0 the left slots [x0 x0 x1 x0 x1 x2], order 1 the right slots
+ *   [x0 x1 x0 x2 x1 x0]; side 0 concatenates them along the columns (out [rows, 6 cols]), side 1 along the rows
+ *   (out [6 rows, cols]); row strides ld / ld_out.  cols, ld, ld_out multiples of 4; x 16-byte, out 8-byte aligned.
+ */
+int ltq_bf16x6_split(const float* x, long long ld, int rows, int cols, int order, int side, uint16_t* out,
+                     long long ld_out, void* stream);
+size_t ltq_ldlq_bcat_elems(int K);
+int ltq_ldlq_bcat(const float* U, long long ldU, int K, uint16_t* bcat, void* stream);
+int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* G, long long ldG,
+                   const float* Uinv, long long ldUi, int M, float* what, long long ld_what, uint16_t* d_h,
+                   long long ld_dh, uint16_t* acat, void* stream);
 int ltq_ldlq_block(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* dw,
                    const float* U, long long ldU, const float* Uinv, long long ldUi, float* G, long long ldG,
                    int16_t* idx, uint8_t* gi, long long ldP, int M, const float* tab, const float* gains, int K, int m,

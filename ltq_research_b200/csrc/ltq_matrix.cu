@@ -3,7 +3,9 @@
 //                         used by compute_optimal_suh src/liqk_v2.py:409-441 and _fwht_rows :1024-1026);
 //   * ltq_scale_fit     — per-(row, 256-block) scale: fp16 d_row and 5-bit exponent (src/liqk_v2.py:938-946);
 //   * ltq_ldlq_gather   — the Viterbi input tiles of one 16-column sub-block (src/liqk_v2.py:913-916, :960-963);
-//   * ltq_ldlq_feedback — the intra-block LDLQ error feedback after a sub-block (src/liqk_v2.py:964-971).
+//   * ltq_ldlq_feedback — the intra-block LDLQ error feedback after a sub-block (src/liqk_v2.py:964-971);
+//   * ltq_ldlq_bcat / ltq_ldlq_inter — the operands of the inter-block update after a 256-column block
+//                         (src/liqk_v2.py:972-979) in the six-product bf16 form of an fp32 GEMM on the tensor cores.
 // All are memory-bound SIMT kernels: one warp per row or per (row, block), coalesced 16-byte accesses.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -189,6 +191,121 @@ __global__ void __launch_bounds__(256) ldlq_feedback_kernel(float* __restrict__ 
     }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Six-product bf16 form of an fp32 product: x = x0 + x1 + x2 with x0 = bf16(x), x1 = bf16(x - x0), x2 = bf16(x - x0 - x1)
+// (each difference exact in fp32), and a @ b ~ a0 b0 + a0 b1 + a1 b0 + a0 b2 + a1 b1 + a2 b0, i.e. the product of the
+// K-concatenations [a0 a0 a1 a0 a1 a2] and [b0; b1; b0; b2; b1; b0] with fp32 accumulation.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void split3_bf16(float x, uint16_t& p0, uint16_t& p1, uint16_t& p2)
+{
+    const __nv_bfloat16 h0 = __float2bfloat16_rn(x);
+    const float r = __fsub_rn(x, __bfloat162float(h0));
+    const __nv_bfloat16 h1 = __float2bfloat16_rn(r);
+    const __nv_bfloat16 h2 = __float2bfloat16_rn(__fsub_rn(r, __bfloat162float(h1)));
+    p0 = __bfloat16_as_ushort(h0);
+    p1 = __bfloat16_as_ushort(h1);
+    p2 = __bfloat16_as_ushort(h2);
+}
+
+// right operands of every block's update: block b's [1536, N_b] (N_b = K - 256 (b + 1)) matrix
+// [u0; u1; u0; u2; u1; u0] of U[256 b : 256 b + 256, 256 (b + 1) : K]; one thread per 4 columns of one source row
+__global__ void __launch_bounds__(256) ldlq_bcat_kernel(const float* __restrict__ U, long long ldU, int K,
+                                                        uint16_t* __restrict__ out)
+{
+    const int b = blockIdx.y >> 8, i = blockIdx.y & 255;
+    const int c0 = 256 * b, c1 = c0 + 256, nb = K - c1;
+    const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (j >= nb) return;
+    const long long off = 1536LL * ((long long)b * K - 128LL * b * (b + 1));
+    const float4 v = *reinterpret_cast<const float4*>(U + (long long)(c0 + i) * ldU + c1 + j);
+    const float x[4] = {v.x, v.y, v.z, v.w};
+    uint16_t p[3][4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) split3_bf16(x[k], p[0][k], p[1][k], p[2][k]);
+    constexpr int part_of_slot[6] = {0, 1, 0, 2, 1, 0};
+#pragma unroll
+    for (int sl = 0; sl < 6; sl++) {
+        const int q = part_of_slot[sl];
+        const uint2 w = make_uint2((uint32_t)p[q][0] | ((uint32_t)p[q][1] << 16), (uint32_t)p[q][2] | ((uint32_t)p[q][3] << 16));
+        *reinterpret_cast<uint2*>(out + off + (long long)(256 * sl + i) * nb + j) = w;
+    }
+}
+
+// after block [c0, c0 + 256): W_hat = d * G, d_h = fp16(d), e = w - W_hat (the reference's operations, same bits), and
+// for the update err = e @ Uinv (Uinv upper triangular: err[k] = sum_{i <= k} e[i] Uinv[i][k], i ascending, fma) split
+// into acat [M, 1536] = [e0 e0 e1 e0 e1 e2].  One CTA per 16 rows, thread k = column k.
+__global__ void __launch_bounds__(256) ldlq_inter_kernel(const float* __restrict__ w, long long ld_w,
+                                                         const float* __restrict__ d_rb, long long ld_d,
+                                                         const float* __restrict__ G, long long ldG,
+                                                         const float* __restrict__ Uinv, long long ldUi,
+                                                         float* __restrict__ what, long long ld_what,
+                                                         uint16_t* __restrict__ d_h, long long ld_dh,
+                                                         uint16_t* __restrict__ acat)
+{
+    __shared__ __align__(16) float se[256 * 20];  // e[r][i] at se[20 i + r] (rows of one column contiguous)
+    const int k = threadIdx.x;
+    const long long r0 = 16LL * blockIdx.x;
+#pragma unroll 4
+    for (int r = 0; r < 16; r++) {
+        const long long row = r0 + r;
+        const float d = fmaxf(d_rb[row * ld_d], 1e-8f);
+        const float wh = __fmul_rn(d, G[row * ldG + k]);
+        what[row * ld_what + k] = wh;
+        se[20 * k + r] = __fsub_rn(w[row * ld_w + k], wh);
+        if (k == 0 && d_h) d_h[row * ld_dh] = __half_as_ushort(__float2half_rn(d));
+    }
+    if (!acat) return;
+    __syncthreads();
+    float acc[16];
+#pragma unroll
+    for (int r = 0; r < 16; r++) acc[r] = 0.f;
+    for (int i = 0; i <= k; i++) {
+        const float u = Uinv[(long long)i * ldUi + k];
+        const float4* e4 = reinterpret_cast<const float4*>(se + 20 * i);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float4 e = e4[q];
+            acc[4 * q] = __fmaf_rn(e.x, u, acc[4 * q]);
+            acc[4 * q + 1] = __fmaf_rn(e.y, u, acc[4 * q + 1]);
+            acc[4 * q + 2] = __fmaf_rn(e.z, u, acc[4 * q + 2]);
+            acc[4 * q + 3] = __fmaf_rn(e.w, u, acc[4 * q + 3]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+        uint16_t p0, p1, p2;
+        split3_bf16(acc[r], p0, p1, p2);
+        uint16_t* a = acat + (r0 + r) * 1536 + k;
+        a[0] = p0; a[256] = p0; a[512] = p1; a[768] = p0; a[1024] = p1; a[1280] = p2;
+    }
+}
+
+// one operand of the six-product form of x (rows x cols, row stride ld): order 0 puts the parts [x0 x0 x1 x0 x1 x2] in
+// the six slots (left operand), order 1 [x0 x1 x0 x2 x1 x0] (right operand); side 0 concatenates the slots along the
+// columns (out[r][s cols + c]), side 1 along the rows (out[s rows + r][c]).  One thread per 4 columns of one row.
+__global__ void __launch_bounds__(256) bf16x6_split_kernel(const float* __restrict__ x, long long ld, int rows, int cols,
+                                                           int order, int side, uint16_t* __restrict__ out,
+                                                           long long ld_out)
+{
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int c4 = cols >> 2;
+    if (t >= (long long)rows * c4) return;
+    const int r = (int)(t / c4), c = 4 * (int)(t - (long long)r * c4);
+    const float4 v = *reinterpret_cast<const float4*>(x + (long long)r * ld + c);
+    const float xv[4] = {v.x, v.y, v.z, v.w};
+    uint16_t p[3][4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) split3_bf16(xv[k], p[0][k], p[1][k], p[2][k]);
+    constexpr int left[6] = {0, 0, 1, 0, 1, 2}, right[6] = {0, 1, 0, 2, 1, 0};
+#pragma unroll
+    for (int sl = 0; sl < 6; sl++) {
+        const int q = order ? right[sl] : left[sl];
+        const uint2 w = make_uint2((uint32_t)p[q][0] | ((uint32_t)p[q][1] << 16), (uint32_t)p[q][2] | ((uint32_t)p[q][3] << 16));
+        const long long o = side ? ((long long)sl * rows + r) * ld_out + c : (long long)r * ld_out + (long long)sl * cols + c;
+        *reinterpret_cast<uint2*>(out + o) = w;
+    }
+}
+
 }  // namespace
 
 extern "C" int ltq_fwht256(const void* in, int in_bf16, long long ld_in, float* out, long long ld_out, const float* scale,
@@ -237,5 +354,47 @@ extern "C" int ltq_ldlq_feedback(float* w, long long ld, int M, int s0, const fl
     if (M == 0) return 0;
     ldlq_feedback_kernel<<<(M + 7) / 8, 256, 0, (cudaStream_t)stream>>>(w, ld, M, s0, d_rb, rec, code, U, ldU, Uinv, ldUi,
                                                                        G, ldG, idx, gi, ldP);
+    return (int)cudaGetLastError();
+}
+
+extern "C" size_t ltq_ldlq_bcat_elems(int K)
+{
+    if (K < 256 || K % 256) return 0;
+    const long long nb = K / 256 - 1;  // blocks with an update
+    return (size_t)(1536LL * (nb * K - 128LL * nb * (nb + 1)));
+}
+
+extern "C" int ltq_ldlq_bcat(const float* U, long long ldU, int K, uint16_t* bcat, void* stream)
+{
+    if (K < 256 || K % 256 || ldU < K || ((uintptr_t)U & 15) || (ldU & 3) || ((uintptr_t)bcat & 7)) return -1;
+    const int nb = K / 256 - 1;
+    if (nb == 0) return 0;
+    const dim3 grid((unsigned)((K - 256) / 4 + 255) / 256, (unsigned)(nb * 256));
+    ldlq_bcat_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(U, ldU, K, bcat);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* G,
+                              long long ldG, const float* Uinv, long long ldUi, int M, float* what, long long ld_what,
+                              uint16_t* d_h, long long ld_dh, uint16_t* acat, void* stream)
+{
+    if (M < 0 || M % 16 || !w_blk || !d_rb || !G || !what || (acat && !Uinv)) return -1;
+    if (M == 0) return 0;
+    ldlq_inter_kernel<<<M / 16, 256, 0, (cudaStream_t)stream>>>(w_blk, ld_w, d_rb, ld_d, G, ldG, Uinv, ldUi, what,
+                                                               ld_what, d_h, ld_dh, acat);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_bf16x6_split(const float* x, long long ld, int rows, int cols, int order, int side, uint16_t* out,
+                                long long ld_out, void* stream)
+{
+    if (rows < 0 || cols < 0 || cols % 4 || ld % 4 || ld < cols || ld_out % 4 || ((uintptr_t)x & 15) ||
+        ((uintptr_t)out & 7) || (order != 0 && order != 1) || (side != 0 && side != 1) ||
+        ld_out < (side ? cols : 6LL * cols))
+        return -1;
+    const long long n = (long long)rows * (cols / 4);
+    if (n == 0) return 0;
+    bf16x6_split_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, ld, rows, cols, order, side,
+                                                                                       out, ld_out);
     return (int)cudaGetLastError();
 }

@@ -73,13 +73,45 @@ def _mm6(acat: torch.Tensor, bcat: torch.Tensor) -> torch.Tensor:
     return torch.mm(acat, bcat, out_dtype=torch.float32)
 
 
+def _op6(x: torch.Tensor, order: int, side: int) -> Optional[torch.Tensor]:
+    """The six-slot bf16 operand of an fp32 matrix with unit column stride in one kernel (ltq_bf16x6_split): order 0
+    the left slots (as _acat), 1 the right slots (as _bcat); side 0 slots along the columns, 1 along the rows.  None
+    when the layout does not meet the kernel's alignment."""
+    rows, cols = x.shape
+    if (x.dtype != torch.float32 or not x.is_cuda or x.stride(1) != 1 or cols % 4 or x.stride(0) % 4
+            or x.data_ptr() % 16):
+        return None
+    out = torch.empty((rows, 6 * cols) if side == 0 else (6 * rows, cols), dtype=torch.bfloat16, device=x.device)
+    _check(_lib.lib().ltq_bf16x6_split(ptr(x), x.stride(0), rows, cols, order, side, ptr(out), out.stride(0),
+                                       _stream(x.device)), "ltq_bf16x6_split")
+    return out
+
+
+def _left6(a: torch.Tensor) -> torch.Tensor:
+    """_acat(_split3(a)), bit for bit, with one kernel where the layout allows (a or a.T with unit column stride)."""
+    o = _op6(a, 0, 0)
+    if o is None and a.stride(0) == 1:
+        o = _op6(a.T, 0, 1)
+        o = o.T if o is not None else None
+    return o if o is not None else _acat(_split3(a))
+
+
+def _right6(b: torch.Tensor) -> torch.Tensor:
+    """_bcat(_split3(b)), bit for bit, with one kernel where the layout allows."""
+    o = _op6(b, 1, 1)
+    if o is None and b.stride(0) == 1:
+        o = _op6(b.T, 1, 0)
+        o = o.T if o is not None else None
+    return o if o is not None else _bcat(_split3(b))
+
+
 def _mm(a: torch.Tensor, b: torch.Tensor, gemm: str) -> torch.Tensor:
     """a @ b for fp32 [M, K] x [K, N] in the given mode."""
     if gemm == "fp32":
         return a @ b
     if gemm != "bf16x6":
         raise ValueError(f"gemm mode {gemm!r}: expected one of {GEMM_MODES}")
-    return _mm6(_acat(_split3(a)), _bcat(_split3(b)))
+    return _mm6(_left6(a), _right6(b))
 
 
 def make_rademacher_signs(dim: int, seed: int, device) -> torch.Tensor:
@@ -306,7 +338,7 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
     group = {"spec": spec_name, "d_row": d_row, "e": e_rb, "idx": idx, "gi": gi, "G": G}
 
     Uc = U.contiguous()
-    if gemm == "bf16x6" and U_parts is None and nblocks > 1:
+    if gemm == "bf16x6" and U_parts is None and nblocks > 1 and not fused:
         U_parts = _split3(Uc)
 
     def inter_block(err_in, c0, c1, U_blk_inv):  # W_work[:, c1:] -= ((w_blk - what) @ U_blk_inv) @ U[c0:c1, c1:]
@@ -316,6 +348,34 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
         else:
             err_blk = _mm(err_in, U_blk_inv, gemm)
             W_work[:, c1:] -= _mm6(_acat(_split3(err_blk)), _bcat(tuple(p[c0:c1, c1:] for p in U_parts)))
+
+    if fused and gemm == "bf16x6":
+        # per block: the fused block kernel, the inter-block operands (W_hat, d, the split of err @ Uinv) and one
+        # tensor-core GEMM W_work[:, c1:] -= acat @ bcat_b
+        brun = _BlockRunner(spec_name, M, device)
+        dwc = diag_w.float().contiguous()
+        bcat = torch.empty(max(int(L.ltq_ldlq_bcat_elems(K)), 1), dtype=torch.bfloat16, device=device)
+        _check(L.ltq_ldlq_bcat(ptr(Uc), Uc.stride(0), K, ptr(bcat), st), "ltq_ldlq_bcat")
+        acat = torch.empty((M, 6 * QK_K), dtype=torch.bfloat16, device=device)
+        U_blks_inv = U_blks_inv.contiguous()  # row-major blocks (a batched triangular solve may return column-major)
+        off = 0
+        for ibl in range(nblocks):
+            c0, c1 = ibl * QK_K, (ibl + 1) * QK_K
+            U_blk_inv = U_blks_inv[ibl]
+            brun.run(W_work, c0, d_rb_all, ibl, dwc, Uc, U_blk_inv, G, idx, gi)
+            last = c1 >= K
+            _check(L.ltq_ldlq_inter(ptr(W_work) + 4 * c0, W_work.stride(0), ptr(d_rb_all) + 4 * ibl, d_rb_all.stride(0),
+                                    ptr(G) + 4 * c0, G.stride(0), ptr(U_blk_inv), U_blk_inv.stride(0), M,
+                                    ptr(W_hat_rot) + 4 * c0, W_hat_rot.stride(0), ptr(d_full) + 2 * ibl,
+                                    d_full.stride(0), None if last else ptr(acat), st), "ltq_ldlq_inter")
+            if not last:
+                nb = K - c1
+                Wv = W_work[:, c1:]
+                torch.addmm(Wv, acat, bcat[off:off + 6 * QK_K * nb].view(6 * QK_K, nb), out_dtype=torch.float32,
+                            beta=1, alpha=-1, out=Wv)
+                off += 6 * QK_K * nb
+            yield
+        return d_full, W_hat_rot, group
 
     if fused:
         brun = _BlockRunner(spec_name, M, device)
@@ -416,7 +476,7 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     eye256 = torch.eye(QK_K, dtype=torch.float32, device=W.device).unsqueeze(0).expand(nblocks, -1, -1)
     U_blks = torch.stack([U[b * QK_K:(b + 1) * QK_K, b * QK_K:(b + 1) * QK_K] for b in range(nblocks)], dim=0)
     U_blks_inv = torch.linalg.solve_triangular(U_blks, eye256, upper=True)
-    U_parts = _split3(U.contiguous()) if gemm == "bf16x6" and nblocks > 1 else None
+    U_parts = None  # the fused path builds its own bf16 operands of U (ltq_ldlq_bcat)
     yield
 
     row_slices = [(0, M, spec_or_row_specs)] if isinstance(spec_or_row_specs, str) else spec_or_row_specs
@@ -461,10 +521,10 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
         def times_h(A):
             return A @ H_f32
     else:
-        Hb = _bcat(_split3(H_f32))  # the split of H, shared by every product with H
+        Hb = _right6(H_f32)  # the split of H, shared by every product with H
 
         def times_h(A):
-            return _mm6(_acat(_split3(A)), Hb)
+            return _mm6(_left6(A), Hb)
     U_base = fwht_inplace(W_hat_rot.clone(), block_size=QK_K)
     W_hat_eff = U_base * suh.unsqueeze(0)
     c_pack = torch.ones((M,), dtype=torch.float32, device=W.device)
@@ -485,8 +545,16 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     A_in = (U_w.T @ U_scaled if gemm == "fp32" else _mm(U_w.T, U_scaled, gemm)) * H_f32
     b_in = (U_w * HW).sum(dim=0)
     A_in.diagonal().add_(1e-3 * A_in.diagonal().mean().clamp(min=1e-12))
-    # the reference solves, and keeps the refit when the solve succeeds and lowers the loss (src/liqk_v2.py:1161-1180)
-    sol, solve_info = torch.linalg.solve_ex(A_in, b_in)
+    # the reference solves, and keeps the refit when the solve succeeds and lowers the loss (src/liqk_v2.py:1161-1180).
+    # A_in = (U_w^T U_scaled) o H + eps I is symmetric positive definite by construction (a Schur product of two Gram
+    # matrices plus a positive diagonal): the fast mode solves it by Cholesky (no pivot search, no host-blocking LU);
+    # a failed factorization skips the refit like the reference's failed solve.  The fp32 mode keeps the reference's LU.
+    if gemm == "fp32":
+        sol, solve_info = torch.linalg.solve_ex(A_in, b_in)
+    else:
+        Lc, solve_info = torch.linalg.cholesky_ex(A_in)
+        sol = torch.cholesky_solve(b_in.unsqueeze(1), Lc).squeeze(1)
+        del Lc
     suh_cand = sol.to(torch.float16).to(torch.float32)
     valid_s = torch.isfinite(suh_cand) & (suh_cand.abs() > 0.05) & (suh_cand.abs() < 10.0)
     suh_cand = torch.where(valid_s, suh_cand, suh)
