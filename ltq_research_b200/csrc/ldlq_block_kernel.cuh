@@ -319,13 +319,27 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) ldlq_block_kernel(const 
             ferr[i] = acc;
         }
         __syncthreads();
+        // w[:, s1:] -= err @ U[s0:s1, s1:]: a thread per column, the column's 16 values of U loaded once for all 16 rows;
+        // each output is the same sequential fma chain over k = 0..15 as in the stand-alone feedback kernel
         const int s1 = s0 + 16, ncol = 256 - s1;
-        for (int i = tid; i < 16 * ncol; i += nthr) {
-            const int r = i / ncol, j = i - r * ncol;
-            float acc = 0.f;
+        for (int j = tid; j < ncol; j += nthr) {
+            float u[16];
 #pragma unroll
-            for (int k = 0; k < 16; k++) acc = __fmaf_rn(ferr[r * 16 + k], q.U[(long long)(s0 + k) * q.ldU + s1 + j], acc);
-            wsub[r * 256 + s1 + j] = __fsub_rn(wsub[r * 256 + s1 + j], acc);
+            for (int k = 0; k < 16; k++) u[k] = q.U[(long long)(s0 + k) * q.ldU + s1 + j];
+#pragma unroll 2
+            for (int r = 0; r < 16; r++) {
+                const float4* e4 = reinterpret_cast<const float4*>(ferr + r * 16);
+                float acc = 0.f;
+#pragma unroll
+                for (int k4 = 0; k4 < 4; k4++) {
+                    const float4 e = e4[k4];
+                    acc = __fmaf_rn(e.x, u[4 * k4], acc);
+                    acc = __fmaf_rn(e.y, u[4 * k4 + 1], acc);
+                    acc = __fmaf_rn(e.z, u[4 * k4 + 2], acc);
+                    acc = __fmaf_rn(e.w, u[4 * k4 + 3], acc);
+                }
+                wsub[r * 256 + s1 + j] = __fsub_rn(wsub[r * 256 + s1 + j], acc);
+            }
         }
     }
 }

@@ -243,6 +243,7 @@ __global__ void __launch_bounds__(256) ldlq_inter_kernel(const float* __restrict
                                                          uint16_t* __restrict__ acat)
 {
     __shared__ __align__(16) float se[256 * 20];  // e[r][i] at se[20 i + r] (rows of one column contiguous)
+    __shared__ __align__(16) float su[16 * 256];  // 16 rows of Uinv at a time
     const int k = threadIdx.x;
     const long long r0 = 16LL * blockIdx.x;
 #pragma unroll 4
@@ -259,16 +260,27 @@ __global__ void __launch_bounds__(256) ldlq_inter_kernel(const float* __restrict
     float acc[16];
 #pragma unroll
     for (int r = 0; r < 16; r++) acc[r] = 0.f;
-    for (int i = 0; i <= k; i++) {
-        const float u = Uinv[(long long)i * ldUi + k];
-        const float4* e4 = reinterpret_cast<const float4*>(se + 20 * i);
+    // rows i0 .. i0 + 15 of Uinv staged in shared memory by the whole CTA (coalesced), then consumed by every column
+    for (int i0 = 0; i0 < 256; i0 += 16) {
+        __syncthreads();
+        for (int t = k; t < 16 * 64; t += 256) {
+            const int r = t >> 6, c = 4 * (t & 63);
+            *reinterpret_cast<float4*>(su + 256 * r + c) =
+                *reinterpret_cast<const float4*>(Uinv + (long long)(i0 + r) * ldUi + c);
+        }
+        __syncthreads();
+        const int iend = k + 1 < i0 + 16 ? k + 1 : i0 + 16;
+        for (int i = i0; i < iend; i++) {
+            const float u = su[256 * (i - i0) + k];
+            const float4* e4 = reinterpret_cast<const float4*>(se + 20 * i);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const float4 e = e4[q];
-            acc[4 * q] = __fmaf_rn(e.x, u, acc[4 * q]);
-            acc[4 * q + 1] = __fmaf_rn(e.y, u, acc[4 * q + 1]);
-            acc[4 * q + 2] = __fmaf_rn(e.z, u, acc[4 * q + 2]);
-            acc[4 * q + 3] = __fmaf_rn(e.w, u, acc[4 * q + 3]);
+            for (int q = 0; q < 4; q++) {
+                const float4 e = e4[q];
+                acc[4 * q] = __fmaf_rn(e.x, u, acc[4 * q]);
+                acc[4 * q + 1] = __fmaf_rn(e.y, u, acc[4 * q + 1]);
+                acc[4 * q + 2] = __fmaf_rn(e.z, u, acc[4 * q + 2]);
+                acc[4 * q + 3] = __fmaf_rn(e.w, u, acc[4 * q + 3]);
+            }
         }
     }
 #pragma unroll
@@ -378,7 +390,8 @@ extern "C" int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d
                               long long ldG, const float* Uinv, long long ldUi, int M, float* what, long long ld_what,
                               uint16_t* d_h, long long ld_dh, uint16_t* acat, void* stream)
 {
-    if (M < 0 || M % 16 || !w_blk || !d_rb || !G || !what || (acat && !Uinv)) return -1;
+    if (M < 0 || M % 16 || !w_blk || !d_rb || !G || !what || (acat && (!Uinv || ((uintptr_t)Uinv & 15) || ldUi % 4)))
+        return -1;
     if (M == 0) return 0;
     ldlq_inter_kernel<<<M / 16, 256, 0, (cudaStream_t)stream>>>(w_blk, ld_w, d_rb, ld_d, G, ldG, Uinv, ldUi, what,
                                                                ld_what, d_h, ld_dh, acat);

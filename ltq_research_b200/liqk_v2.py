@@ -471,11 +471,19 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     del H_rot, H_reg
     U = torch.linalg.solve_triangular(L_flip, torch.eye(K, dtype=L_flip.dtype, device=L_flip.device), upper=False)
     U = U.flip(0, 1)
-    del L_flip
     diag_w = 1.0 / (torch.diagonal(U) ** 2).clamp(min=1e-12)
-    eye256 = torch.eye(QK_K, dtype=torch.float32, device=W.device).unsqueeze(0).expand(nblocks, -1, -1)
-    U_blks = torch.stack([U[b * QK_K:(b + 1) * QK_K, b * QK_K:(b + 1) * QK_K] for b in range(nblocks)], dim=0)
-    U_blks_inv = torch.linalg.solve_triangular(U_blks, eye256, upper=True)
+    if gemm == "fp32":  # the reference's inverses of U's diagonal blocks (src/liqk_v2.py:1085-1087)
+        eye256 = torch.eye(QK_K, dtype=torch.float32, device=W.device).unsqueeze(0).expand(nblocks, -1, -1)
+        U_blks = torch.stack([U[b * QK_K:(b + 1) * QK_K, b * QK_K:(b + 1) * QK_K] for b in range(nblocks)], dim=0)
+        U_blks_inv = torch.linalg.solve_triangular(U_blks, eye256, upper=True)
+    else:
+        # U = P L^-1 P (P the reversal), so U^-1 = P L P, and the diagonal blocks of a triangular matrix's inverse are
+        # the inverses of its diagonal blocks: U_blk^-1 is the flipped diagonal block of L itself — one strided copy
+        # instead of a batched triangular solve (which also blocked the host)
+        s0, s1 = L_flip.stride()  # any layout (the factorization may return column-major)
+        U_blks_inv = L_flip.as_strided((nblocks, QK_K, QK_K), (QK_K * (s0 + s1), s0, s1),
+                                       L_flip.storage_offset()).flip(0, 1, 2).contiguous()
+    del L_flip
     U_parts = None  # the fused path builds its own bf16 operands of U (ltq_ldlq_bcat)
     yield
 

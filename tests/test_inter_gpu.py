@@ -108,3 +108,25 @@ def test_bf16x6_operands_one_kernel_equal_torch_split(cuda_dev):
     for a in (x, x.T.contiguous().T):
         assert torch.equal(_left6(a).view(torch.int16), _acat(_split3(a.contiguous())).view(torch.int16))
         assert torch.equal(_right6(a).view(torch.int16), _bcat(_split3(a.contiguous())).view(torch.int16))
+
+
+def test_block_inverses_from_the_cholesky_factor(cuda_dev):
+    """The fast mode takes U_blk^-1 from the Cholesky factor (U = P L^-1 P, so U^-1 = P L P and its diagonal blocks are
+    the flipped diagonal blocks of L) instead of solving U_blk X = I: the two agree to fp32 rounding, for L in the
+    layout the factorization returns."""
+    g = torch.Generator(device=cuda_dev).manual_seed(2)
+    K = 1024
+    nb = K // 256
+    X = torch.randn(4096, K, device=cuda_dev, dtype=torch.float64, generator=g)
+    H = (X.T @ X / 4096).float()
+    H.diagonal().add_(0.05 * H.diagonal().mean())
+    L, info = torch.linalg.cholesky_ex(H.flip(0, 1))
+    assert int(info) == 0
+    U = torch.linalg.solve_triangular(L, torch.eye(K, device=cuda_dev), upper=False).flip(0, 1)
+    Ub = torch.stack([U[b * 256:(b + 1) * 256, b * 256:(b + 1) * 256] for b in range(nb)])
+    ref = torch.linalg.solve_triangular(Ub, torch.eye(256, device=cuda_dev).expand(nb, -1, -1), upper=True)
+    s0, s1 = L.stride()
+    got = L.as_strided((nb, 256, 256), (256 * (s0 + s1), s0, s1), L.storage_offset()).flip(0, 1, 2)
+    assert ((got - ref).norm() / ref.norm()).item() < 1e-5
+    assert (torch.bmm(Ub, got) - torch.eye(256, device=cuda_dev)).abs().max().item() < 1e-4
+    assert torch.equal(torch.triu(got), got)
