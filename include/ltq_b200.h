@@ -123,6 +123,16 @@ size_t ltq_ldlq_block_workspace_bytes(int M, int Gfull, int n_cand, int sub, int
  */
 int ltq_bf16x6_split(const float* x, long long ld, int rows, int cols, int order, int side, uint16_t* out,
                      long long ld_out, void* stream);
+/* the same for `batch` matrices at x + z * xbs -> out + z * obs (z < 65536); neg splits -x. */
+int ltq_bf16x6_split_batched(const float* x, long long ld, long long xbs, int rows, int cols, int batch, int order,
+                             int side, int neg, uint16_t* out, long long ld_out, long long obs, void* stream);
+/*
+ * Hessian factorization (src/liqk_v2.py:1074-1088, U = flip(L^-1) for L = chol(flip(H_reg))), the leaves of the
+ * triangular inverse: the inverses of the nb lower-triangular 256 x 256 diagonal blocks of L (row-major, row stride ldL)
+ * into the diagonal blocks of X (row stride ldX; each block's strictly upper part written as 0), by forward
+ * substitution in fp32.  The blocks above the leaves are merged by GEMMs on the caller's side.
+ */
+int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* X, long long ldX, void* stream);
 size_t ltq_ldlq_bcat_elems(int K);
 int ltq_ldlq_bcat(const float* U, long long ldU, int K, uint16_t* bcat, void* stream);
 int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* G, long long ldG,

@@ -11,6 +11,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <atomic>
 #include "ltq_b200.h"
 
 namespace {
@@ -292,19 +293,23 @@ __global__ void __launch_bounds__(256) ldlq_inter_kernel(const float* __restrict
     }
 }
 
-// one operand of the six-product form of x (rows x cols, row stride ld): order 0 puts the parts [x0 x0 x1 x0 x1 x2] in
-// the six slots (left operand), order 1 [x0 x1 x0 x2 x1 x0] (right operand); side 0 concatenates the slots along the
-// columns (out[r][s cols + c]), side 1 along the rows (out[s rows + r][c]).  One thread per 4 columns of one row.
-__global__ void __launch_bounds__(256) bf16x6_split_kernel(const float* __restrict__ x, long long ld, int rows, int cols,
-                                                           int order, int side, uint16_t* __restrict__ out,
-                                                           long long ld_out)
+// one operand of the six-product form of x (rows x cols, row stride ld; batch element z at x + z * xbs): order 0 puts
+// the parts [x0 x0 x1 x0 x1 x2] in the six slots (left operand), order 1 [x0 x1 x0 x2 x1 x0] (right operand); side 0
+// concatenates the slots along the columns (out[r][s cols + c]), side 1 along the rows (out[s rows + r][c]); neg splits
+// -x (exact).  One thread per 4 columns of one row; blockIdx.y = batch element.
+__global__ void __launch_bounds__(256) bf16x6_split_kernel(const float* __restrict__ x, long long ld, long long xbs,
+                                                           int rows, int cols, int order, int side, int neg,
+                                                           uint16_t* __restrict__ out, long long ld_out, long long obs)
 {
     const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const int c4 = cols >> 2;
     if (t >= (long long)rows * c4) return;
+    x += (long long)blockIdx.y * xbs;
+    out += (long long)blockIdx.y * obs;
     const int r = (int)(t / c4), c = 4 * (int)(t - (long long)r * c4);
     const float4 v = *reinterpret_cast<const float4*>(x + (long long)r * ld + c);
-    const float xv[4] = {v.x, v.y, v.z, v.w};
+    const float sg = neg ? -1.f : 1.f;
+    const float xv[4] = {sg * v.x, sg * v.y, sg * v.z, sg * v.w};
     uint16_t p[3][4];
 #pragma unroll
     for (int k = 0; k < 4; k++) split3_bf16(xv[k], p[0][k], p[1][k], p[2][k]);
@@ -316,6 +321,30 @@ __global__ void __launch_bounds__(256) bf16x6_split_kernel(const float* __restri
         const long long o = side ? ((long long)sl * rows + r) * ld_out + c : (long long)r * ld_out + (long long)sl * cols + c;
         *reinterpret_cast<uint2*>(out + o) = w;
     }
+}
+
+// inverse of the 256 x 256 lower-triangular diagonal block b of L (row-major, row stride ldL) into the diagonal block of
+// X (row stride ldX; the block's upper part written as 0), by forward substitution: thread t owns column j = 128 h + t
+// (h = blockIdx.y), x_i = (delta_ij - sum_{k < i} L_ik x_k) / L_ii for i >= j, the sum in ascending k; the column lives
+// in shared memory (x_k = 0 for k < j, so every thread runs the same k range).
+__global__ void __launch_bounds__(128) trtri256_lower_kernel(const float* __restrict__ L, long long ldL,
+                                                             float* __restrict__ X, long long ldX)
+{
+    extern __shared__ float xs[];  // [256][128]
+    const int t = threadIdx.x, h = blockIdx.y, j = 128 * h + t, i0 = 128 * h;
+    const long long b = blockIdx.x;
+    const float* Lb = L + 256 * b * (ldL + 1);
+    float* Xb = X + 256 * b * (ldX + 1);
+    for (int i = i0; i < 256; i++) {
+        const float* Li = Lb + (long long)i * ldL;
+        float acc = 0.f;
+        int k = i0;
+#pragma unroll 4
+        for (; k < i; k++) acc = __fmaf_rn(__ldg(Li + k), xs[(k - i0) * 128 + t], acc);
+        const float x = i < j ? 0.f : __fdiv_rn(__fsub_rn(i == j ? 1.f : 0.f, acc), __ldg(Li + i));
+        xs[(i - i0) * 128 + t] = x;
+    }
+    for (int i = 0; i < 256; i++) Xb[(long long)i * ldX + j] = i < i0 ? 0.f : xs[(i - i0) * 128 + t];
 }
 
 }  // namespace
@@ -398,16 +427,41 @@ extern "C" int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d
     return (int)cudaGetLastError();
 }
 
+extern "C" int ltq_bf16x6_split_batched(const float* x, long long ld, long long xbs, int rows, int cols, int batch,
+                                        int order, int side, int neg, uint16_t* out, long long ld_out, long long obs,
+                                        void* stream)
+{
+    if (rows < 0 || cols < 0 || batch < 0 || batch > 65535 || cols % 4 || ld % 4 || ld < cols || xbs % 4 ||
+        ld_out % 4 || obs % 4 || ((uintptr_t)x & 15) || ((uintptr_t)out & 7) || (order != 0 && order != 1) ||
+        (side != 0 && side != 1) || ld_out < (side ? cols : 6LL * cols))
+        return -1;
+    const long long n = (long long)rows * (cols / 4);
+    if (n == 0 || batch == 0) return 0;
+    const dim3 grid((unsigned)((n + 255) / 256), (unsigned)batch);
+    bf16x6_split_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, ld, xbs, rows, cols, order, side, neg ? 1 : 0, out,
+                                                                ld_out, obs);
+    return (int)cudaGetLastError();
+}
+
 extern "C" int ltq_bf16x6_split(const float* x, long long ld, int rows, int cols, int order, int side, uint16_t* out,
                                 long long ld_out, void* stream)
 {
-    if (rows < 0 || cols < 0 || cols % 4 || ld % 4 || ld < cols || ld_out % 4 || ((uintptr_t)x & 15) ||
-        ((uintptr_t)out & 7) || (order != 0 && order != 1) || (side != 0 && side != 1) ||
-        ld_out < (side ? cols : 6LL * cols))
-        return -1;
-    const long long n = (long long)rows * (cols / 4);
-    if (n == 0) return 0;
-    bf16x6_split_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, ld, rows, cols, order, side,
-                                                                                       out, ld_out);
+    return ltq_bf16x6_split_batched(x, ld, 0, rows, cols, 1, order, side, 0, out, ld_out, 0, stream);
+}
+
+extern "C" int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* X, long long ldX, void* stream)
+{
+    if (nb < 0 || ldL < 256LL * nb || ldX < 256LL * nb || !L || !X) return -1;
+    if (nb == 0) return 0;
+    static std::atomic<int> attr_done[64];  // the shared-memory opt-in, once per device
+    constexpr int smem = 256 * 128 * 4;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
+        const cudaError_t e = cudaFuncSetAttribute(trtri256_lower_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int)e;
+        attr_done[dev].store(1, std::memory_order_release);
+    }
+    trtri256_lower_kernel<<<dim3((unsigned)nb, 2), 128, smem, (cudaStream_t)stream>>>(L, ldL, X, ldX);
     return (int)cudaGetLastError();
 }

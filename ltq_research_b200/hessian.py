@@ -1,0 +1,118 @@
+"""Hessian accumulation and factorization on the B200 (lumen-inference/ltq-research src/liqk_v2.py:207-231 and
+:1066-1088).
+
+* CovAccumulator — the reference's _CovAccumulator: H = (1/N) sum X^T X over calibration batches, the batch Gram on the
+  tensor cores (bf16 / fp16 operands, fp32 output) or as an fp32 product, the batches summed in fp64.  Same API (add,
+  get, H, n) and, for the same inputs on the same device, the same bits: the Gram is the same library product and the
+  fp64 sum adds the same exactly converted values (one fused fp32 -> fp64 add instead of a conversion and an add).
+* tri_inv_lower — X = L^-1 for the lower-triangular Cholesky factor, the K x K triangular inverse behind
+  U = flip(L^-1) (:1079-1082).  The reference solves L X = I with a general triangular solve (O(K^3) work that does
+  not use the zeros of I); here the 256 x 256 diagonal blocks are inverted by forward substitution in one kernel
+  (ltq_trtri256_lower) and adjacent inverted blocks are merged level by level, X21 = -C^-1 (L21 A^-1) for
+  L = [[A, 0], [L21, C]], with the two products of every level as one batched tensor-core GEMM each in the six-product
+  bf16 form (fp32-accurate, the error bound of an fp32 product).  log2(K / 256) levels, about seven launches each.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import ptr
+
+QK = 256
+
+
+class CovAccumulator:
+    """H = (1/N) sum over batches of X^T X (src/liqk_v2.py:207-231), accumulated on the batch's device without
+    keeping X: bf16 / fp16 batches by a half-precision tensor-core GEMM with fp32 output, fp32 batches by an fp32
+    product; batches summed in fp64."""
+
+    def __init__(self):
+        self.H: Optional[torch.Tensor] = None
+        self.n = 0
+
+    def add(self, x: torch.Tensor):
+        x_2d = x.detach().reshape(-1, x.shape[-1])
+        if x_2d.dtype in (torch.bfloat16, torch.float16):
+            gram = torch.mm(x_2d.T, x_2d, out_dtype=torch.float32)
+        else:
+            x_2d = x_2d.float()
+            gram = x_2d.T @ x_2d
+        if self.H is None:
+            self.H = torch.zeros((x_2d.shape[1],) * 2, dtype=torch.float64, device=x_2d.device)
+        self.H.add_(gram)  # fp32 -> fp64 is exact: the same sums as converting first
+        self.n += x_2d.shape[0]
+
+    def get(self) -> torch.Tensor:
+        return (self.H / max(self.n, 1)).to(torch.float32)
+
+
+def _stream(dev) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise RuntimeError(f"{what}: error {rc}")
+
+
+def _split6(x: torch.Tensor, xbs: int, rows: int, cols: int, batch: int, order: int, side: int, neg: bool,
+            ld: int) -> torch.Tensor:
+    """Batched six-slot bf16 operand (ltq_bf16x6_split_batched) of `batch` rows x cols matrices at x + z * xbs (row
+    stride ld): [batch, rows, 6 cols] (side 0) or [batch, 6 rows, cols] (side 1)."""
+    shape = (batch, rows, 6 * cols) if side == 0 else (batch, 6 * rows, cols)
+    out = torch.empty(shape, dtype=torch.bfloat16, device=x.device)
+    _check(_lib.lib().ltq_bf16x6_split_batched(
+        x.data_ptr(), ld, xbs, rows, cols, batch, order, side, int(neg), ptr(out), out.stride(1), out.stride(0),
+        _stream(x.device)), "ltq_bf16x6_split_batched")
+    return out
+
+
+def tri_inv_lower(L: torch.Tensor) -> torch.Tensor:
+    """L^-1 (row-major fp32 [K, K], upper part exactly 0) of a lower-triangular fp32 L with K a multiple of 256, any
+    layout, on the current stream, without host synchronisation."""
+    if L.dim() != 2 or L.shape[0] != L.shape[1] or L.shape[0] % QK or L.dtype != torch.float32 or not L.is_cuda:
+        raise ValueError("tri_inv_lower: a square fp32 CUDA matrix with a multiple of 256 rows is required")
+    K = L.shape[0]
+    Lr = L if L.stride(1) == 1 and L.stride(0) == K else L.contiguous()
+    X = torch.zeros_like(Lr)
+    st = _stream(L.device)
+    nb = K // QK
+    _check(_lib.lib().ltq_trtri256_lower(ptr(Lr), K, nb, ptr(X), K, st), "ltq_trtri256_lower")
+    blocks: List[Tuple[int, int]] = [(QK * i, QK) for i in range(nb)]  # inverted diagonal blocks (start, size)
+    while len(blocks) > 1:
+        pairs = [(blocks[2 * i], blocks[2 * i + 1]) for i in range(len(blocks) // 2)]
+        carry = [blocks[-1]] if len(blocks) % 2 else []
+        # all pairs but possibly the last have equal halves (every block of a level has one size, except a carried
+        # smaller last block); equal pairs sit at a constant stride along the diagonal and run as one batch
+        eq = [p for p in pairs if p[0][1] == p[1][1] == pairs[0][0][1]]
+        rest = pairs[len(eq):]
+        if eq:
+            _merge(Lr, X, eq[0][0][0], eq[0][0][1], eq[0][1][1], len(eq), 2 * eq[0][0][1])
+        for (a0, ba), (c0, bc) in rest:
+            _merge(Lr, X, a0, ba, bc, 1, 0)
+        blocks = [(a0, ba + bc) for (a0, ba), (_, bc) in pairs] + carry
+    return X
+
+
+def _merge(Lr: torch.Tensor, X: torch.Tensor, a0: int, ba: int, bc: int, batch: int, step: int):
+    """For z < batch, with s = a0 + z step: X[s+ba : s+ba+bc, s : s+ba] = -X_C (L21 X_A), X_A = X[s:s+ba, s:s+ba]
+    and X_C = X[s+ba : s+ba+bc, s+ba : s+ba+bc] the inverted diagonal blocks, L21 = L[s+ba : s+ba+bc, s : s+ba]."""
+    K = X.shape[0]
+    bs = step * (K + 1)  # batch stride along the diagonal, in elements
+    c0 = a0 + ba
+    L21 = Lr.as_strided((batch, bc, ba), (bs, K, 1), Lr.storage_offset() + c0 * K + a0)
+    XA = X.as_strided((batch, ba, ba), (bs, K, 1), X.storage_offset() + a0 * K + a0)
+    XC = X.as_strided((batch, bc, bc), (bs, K, 1), X.storage_offset() + c0 * K + c0)
+    X21 = X.as_strided((batch, bc, ba), (bs, K, 1), X.storage_offset() + c0 * K + a0)
+    # T = L21 X_A  [bc, ba]
+    left = _split6(L21, bs, bc, ba, batch, 0, 0, False, K)
+    right = _split6(XA, bs, ba, ba, batch, 1, 1, False, K)
+    T = torch.bmm(left, right, out_dtype=torch.float32)
+    del left, right
+    # X21 = (-X_C) T  [bc, ba]
+    left = _split6(XC, bs, bc, bc, batch, 0, 0, True, K)
+    right = _split6(T, T.stride(0), bc, ba, batch, 1, 1, False, T.stride(1))
+    X21.copy_(torch.bmm(left, right, out_dtype=torch.float32))

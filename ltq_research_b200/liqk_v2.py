@@ -20,6 +20,7 @@ import torch
 
 from . import _lib
 from ._lib import ptr
+from .hessian import tri_inv_lower
 from .formats import LIQK_V2_SPECS, QK_K, SUBBLOCK_SIZE, TCQ_CONFIG  # noqa: F401
 from .tcq_proto import make_gains
 
@@ -469,10 +470,13 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     H_reg.diagonal().add_(damp * diag_mean)
     L_flip, chol_info = torch.linalg.cholesky_ex(H_reg.flip(0, 1))
     del H_rot, H_reg
-    U = torch.linalg.solve_triangular(L_flip, torch.eye(K, dtype=L_flip.dtype, device=L_flip.device), upper=False)
+    if gemm == "fp32":  # the reference's triangular solve L X = I (src/liqk_v2.py:1081)
+        U = torch.linalg.solve_triangular(L_flip, torch.eye(K, dtype=L_flip.dtype, device=L_flip.device), upper=False)
+    else:  # leaf inverses + blockwise merges on the tensor cores (hessian.tri_inv_lower)
+        U = tri_inv_lower(L_flip)
     U = U.flip(0, 1)
     diag_w = 1.0 / (torch.diagonal(U) ** 2).clamp(min=1e-12)
-    if gemm == "fp32":  # the reference's inverses of U's diagonal blocks (src/liqk_v2.py:1085-1087)
+    if gemm == "fp32":  # the reference's inverses of U's diagonal blocks (src/liqk_v2.py:1086-1088)
         eye256 = torch.eye(QK_K, dtype=torch.float32, device=W.device).unsqueeze(0).expand(nblocks, -1, -1)
         U_blks = torch.stack([U[b * QK_K:(b + 1) * QK_K, b * QK_K:(b + 1) * QK_K] for b in range(nblocks)], dim=0)
         U_blks_inv = torch.linalg.solve_triangular(U_blks, eye256, upper=True)
