@@ -252,6 +252,36 @@ def isolated_block_roofline(dev, spec: str, rows: int = 27648, timed: bool = Tru
             "achieved": acs / (statistics.median(ms) * 1e-3) / 1e9}
 
 
+def write_kernel_list(args, timed, fmts):
+    """The timed layers quantized once more under torch.profiler (CUPTI activity records, device timestamps): per
+    kernel name its launches, summed device time and share of the summed time, as a markdown table.  Kernels of
+    different streams overlap, so the shares describe where device time goes, not wall-clock time."""
+    from collections import defaultdict
+    from torch.profiler import ProfilerActivity, profile
+    from ltq_research_b200.batch import quantize_matrices
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        quantize_matrices(timed, n_streams=args.streams, ltq_formats=fmts, pack=False)
+        torch.cuda.synchronize()
+    agg = defaultdict(lambda: [0, 0.0])
+    t0, t1 = float("inf"), 0.0
+    for e in prof.events():
+        if e.device_type != torch.autograd.DeviceType.CUDA or e.device_time_total <= 0:
+            continue
+        a = agg[e.name[:110]]
+        a[0] += 1
+        a[1] += e.device_time_total
+        t0, t1 = min(t0, e.time_range.start), max(t1, e.time_range.end)
+    tot = sum(v[1] for v in agg.values())
+    lines = [f"| kernel | launches | device ms | share |", "|---|---|---|---|"]
+    for name, (n, us) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:40]:
+        lines.append(f"| `{name}` | {n} | {us / 1e3:.1f} | {100 * us / tot:.1f} % |")
+    head = (f"{args.steps} layers ({len(timed)} matrices), {args.streams} streams: {sum(v[0] for v in agg.values())} "
+            f"launches, summed device time {tot / 1e3:.1f} ms over a {(t1 - t0) / 1e3:.1f} ms span\n\n")
+    with open(args.kernel_list, "w") as f:
+        f.write(head + "\n".join(lines) + "\n")
+    print(head.strip(), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -267,6 +297,12 @@ def main():
     ap.add_argument("--profile-block", default=None, metavar="FORMAT",
                     help="one fused block launch of FORMAT over --rows rows untimed (after two warm-up launches), for "
                          "ncu captures of ldlq_block_kernel")
+    ap.add_argument("--profile-viterbi", default=None, metavar="FORMAT",
+                    help="three stand-alone two-pass Viterbi calls (ltq_viterbi_tb) of FORMAT over the --rows / 16 "
+                         "tiles of one sub-block, for ncu captures of vit_fwd_kernel")
+    ap.add_argument("--kernel-list", default=None, metavar="PATH",
+                    help="after the warm-up, quantize the timed layers once under the CUDA profiler (CUPTI) and write "
+                         "the per-kernel launch list (launches, total device time, share) to PATH as markdown")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -289,6 +325,16 @@ def main():
     from ltq_research_b200.formats import load_formats
     fmts = load_formats(list(FORMATS), dev)
 
+    if args.profile_viterbi:
+        r = Lq._TcqRunner(args.profile_viterbi, args.rows, dev)
+        g = torch.Generator(device=dev).manual_seed(1)
+        r.x.copy_(torch.randn(r.x.shape, device=dev, generator=g))
+        dw = torch.rand(256, device=dev, generator=g) + 0.5
+        for _ in range(3):
+            r.run(dw)
+        torch.cuda.synchronize()
+        print(f"profile run: stand-alone Viterbi {args.profile_viterbi} over {r.nt} tiles", flush=True)
+        return
     if args.profile_block:
         r = isolated_block_roofline(dev, args.profile_block, rows=args.rows, timed=False)
         print(f"profile run: fused block {args.profile_block} over {args.rows} rows", flush=True)
@@ -313,6 +359,10 @@ def main():
     timed = [j for l in range(args.steps) for j in layer_jobs(l, rank, dev)]
     quantize_matrices(warm, n_streams=args.streams, ltq_formats=fmts, pack=False)
     barrier()
+
+    if args.kernel_list:
+        write_kernel_list(args, timed, fmts)
+        return
 
     Lq.BLOCK_EVENTS = []
     k0 = _lib.kernels_launched()

@@ -551,7 +551,7 @@ static __device__ __forceinline__ void merge_any(int G, const float* s_dp, float
 // UC > 0: the table width U as a compile-time constant (the minimum over u unrolled, same operations in the same
 // order); UC = 0: any U and the half-integer tables (mix > 0).
 template <int NL, int NP, bool MD, int UC>
-static __device__ __noinline__ void build_err_u(float* myerr, const float* s_x, const float* s_w, const float* s_tab,
+static __device__ __forceinline__ void build_err_u(float* myerr, const float* s_x, const float* s_w, const float* s_tab,
                                                 const float* s_tabhi, float gain, float gainhi, int t0, int sub, int U,
                                                 int U_hi, int mix, int lane)
 {
