@@ -145,6 +145,15 @@ int ltq_ldlq_block(const float* w_blk, long long ld_w, const float* d_rb, long l
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * DP-profile sub-block quantization through a 1-D table — the reference's own export, same signature
+ * (src/cuda/tcq_viterbi.cu:806-811, bound at src/tcq_proto.py:530-532): for each of S sub-blocks of 16 values xs with
+ * weights dh, bucket b = clamp(rint(fma(x, inv_step, half_b)), 0, nb - 1), the column c < 64 of lut [nb, 64] with the
+ * smallest sum_j fma(d e, e, .) (e = x - lut[b][c], lowest c on ties), out = lut[b_j][c].  lut 8-byte aligned.
+ */
+int lut_subs_quant(const float* xs, const float* dh, const float* lut, float* out, int S, float inv_step, float half_b,
+                   int nb, void* stream);
+
+/*
  * .ltq tile packing and spec decode (src/ltq_file.py:54-148; tile fields src/ltq_format.py:104-147).  A row slice
  * [R, K] (R, K multiples of 16) is (R/16)(K/16) tiles of 16 x 16; the packed slice is four structure-of-arrays regions
  * (codes, planes, lsb, gains), each at a multiple of 64 bytes — byte for byte what the reference's pack_slice writes.

@@ -70,7 +70,7 @@ def _record(obj, stream: torch.cuda.Stream):
 def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], seed: int = 1337, damp: float = 0.02,
                       n_streams: int = 8, pack: bool = True, keep_w_hat: bool = False,
                       device: Optional[torch.device] = None, on_issued=None, ltq_formats: Optional[Dict] = None,
-                      to_host: bool = False, gemm: str = "bf16x6") -> List[Dict]:
+                      to_host: bool = False, gemm: str = "bf16x6", order: str = "lpt") -> List[Dict]:
     """Quantize every (W [M, K], H [K, K], spec) of `jobs` as quantize_matrix_liqk_v2(W, H, spec, seed, damp) would,
     concurrently on `n_streams` CUDA streams.  W / H may be CUDA tensors or (pinned) host tensors, which are copied to
     the device on the matrix's stream.  Returns, per job: {"qdata", "pack" (the PACK["matrix"] fields, device tensors)
@@ -82,7 +82,9 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
     "d_row" fp16, "e" int8, "suh" fp16}, as pinned host tensors when to_host.  Raises torch.linalg.LinAlgError if a
     damped Hessian is not positive definite, RuntimeError if a packed matrix does not decode to its tile values.
     gemm: the mode of the LDLQ inter-block update and refit products (liqk_v2.GEMM_MODES): "bf16x6" (default) runs
-    them as fp32-accurate split products on the tensor cores; "fp32" reproduces quantize_matrix_liqk_v2 bit for bit."""
+    them as fp32-accurate split products on the tensor cores; "fp32" reproduces quantize_matrix_liqk_v2 bit for bit.
+    order: the order in which the streams take jobs — "lpt" (default) longest estimated time first, "given" as listed.
+    The results do not depend on it."""
     if not jobs:
         return []
     dev = torch.device(device) if device is not None else None
@@ -98,7 +100,12 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
     main = torch.cuda.current_stream(dev)
     streams = _streams(dev, max(1, n_streams))
     cost = [estimated_seconds(W.shape[0], W.shape[1], sp) for W, _, sp in jobs]
-    pending = sorted(range(len(jobs)), key=lambda i: -cost[i])[::-1]  # pop() takes the longest remaining job
+    if order == "lpt":
+        pending = sorted(range(len(jobs)), key=lambda i: -cost[i])[::-1]  # pop() takes the longest remaining job
+    elif order == "given":
+        pending = list(range(len(jobs)))[::-1]  # pop() takes the jobs in the order given
+    else:
+        raise ValueError(f"order {order!r}: expected 'lpt' or 'given'")
     out: List[Optional[Dict]] = [None] * len(jobs)
     # one job in issue per stream; each round advances every job by one step (Hessian preparation, one 256-column
     # block, refits), so that every stream keeps work queued while the host is blocked on a full launch queue

@@ -25,6 +25,7 @@ from .formats import LIQK_V2_SPECS, QK_K, SUBBLOCK_SIZE, TCQ_CONFIG  # noqa: F40
 from .tcq_proto import make_gains
 
 NUM_SUBBLOCKS = QK_K // SUBBLOCK_SIZE
+N_LUT_BUCKETS = 8192  # buckets of the DP profile's 1-D table (src/liqk_v2.py:71)
 # Packing mode for .ltq: if not None, the quantizer stores each matrix's tile codes, d_row, e and suh in
 # PACK["matrix"] (src/liqk_v2.py:72-74)
 PACK: Optional[dict] = None
@@ -157,6 +158,96 @@ def fwht_inplace(x: torch.Tensor, block_size: int = 256) -> torch.Tensor:
 def _fwht_rows(X: torch.Tensor) -> torch.Tensor:
     """Block FWHT-256 over rows (along the first dimension), src/liqk_v2.py:1024-1026."""
     return fwht_rows_scaled(X.T.contiguous()).T.contiguous()
+
+
+# Trained register banks of the .liqk v2 formats, per (format, device) (src/liqk_v2.py:234, :379-406).  The stored bank
+# file of the reference (data/liqk_v2_banks.safetensors) and its trainer belong to the .liqk v2 quantizer, which this
+# build does not include: banks are registered here (register_warp_register_bank) and then serve the DP profile.
+_WARP_BANK_CACHE: Dict[Tuple[str, str], Dict[str, torch.Tensor]] = {}
+
+
+def register_warp_register_bank(spec_name: str, grids_all: torch.Tensor, max_grid: float, device=None,
+                                ls_all: Optional[torch.Tensor] = None, cb_all: Optional[torch.Tensor] = None) -> dict:
+    """Register the bank of `spec_name` (grids_all [C_all, levels] of candidate grids, max_grid their range) on
+    `device` and build its 1-D table as the reference does (src/liqk_v2.py:394-396): bucket centres
+    z = linspace(-max_g, max_g, N_LUT_BUCKETS), lut_val[b, c] = the point of grid c nearest to z_b (first on ties)."""
+    dev = torch.device(device) if device is not None else grids_all.device
+    grids_all = grids_all.to(dev, torch.float32)
+    z = torch.linspace(-max_grid, max_grid, N_LUT_BUCKETS, device=dev, dtype=torch.float32)
+    q_idx = (z[:, None, None] - grids_all[None, :, :]).abs().argmin(dim=-1)
+    lut_val = torch.gather(grids_all.unsqueeze(0).expand(N_LUT_BUCKETS, -1, -1), 2,
+                           q_idx.unsqueeze(-1)).squeeze(-1).contiguous()
+    bank = {"grids_all": grids_all, "ls_all": ls_all, "cb_all": cb_all, "lut_val": lut_val, "max_grid": max_grid}
+    _WARP_BANK_CACHE[(spec_name, str(dev))] = bank
+    return bank
+
+
+def get_warp_register_bank(spec_name: str, device) -> Dict[str, torch.Tensor]:
+    """The registered bank of `spec_name` on `device` (src/liqk_v2.py:379-406); raises KeyError when none is
+    registered (the reference would load data/liqk_v2_banks.safetensors or train one)."""
+    key = (spec_name, str(torch.device(device)))
+    if key not in _WARP_BANK_CACHE:
+        raise KeyError(f"{spec_name}: no register bank on {device}; register one with register_warp_register_bank "
+                       "(the trained bank file and trainer of the .liqk v2 formats are not part of this build)")
+    return _WARP_BANK_CACHE[key]
+
+
+@torch.no_grad()
+def quantize_subs_lut_chunked(x_subs: torch.Tensor, dhs: torch.Tensor, lut_val: torch.Tensor, inv_step: float,
+                              half_b: float) -> torch.Tensor:
+    """The DP profile's torch path (src/liqk_v2.py:444-466), for tables with other than 64 columns: per sub-block the
+    column of lut_val with the smallest weighted error, buckets round(x * inv_step + half_b) (product rounded before
+    the sum), in chunks of 32768 sub-blocks."""
+    S_tot = x_subs.shape[0]
+    G_out = torch.empty((S_tot, SUBBLOCK_SIZE), dtype=torch.float32, device=x_subs.device)
+    chunk = 32768
+    for i0 in range(0, S_tot, chunk):
+        i1 = min(i0 + chunk, S_tot)
+        xs = x_subs[i0:i1]
+        dh = dhs[i0:i1]
+        b_idx = (xs * inv_step + half_b).round().long().clamp(0, N_LUT_BUCKETS - 1)
+        g_cand = lut_val[b_idx]
+        err2 = (xs.unsqueeze(-1) - g_cand).square()
+        bc = (err2 * dh).sum(dim=1).argmin(dim=-1)
+        ar = torch.arange(i1 - i0, device=x_subs.device)
+        G_out[i0:i1] = g_cand[ar, :, bc]
+    return G_out
+
+
+@torch.no_grad()
+def quantize_liqk_v2_diag_rot(W_rot: torch.Tensor, diag_h: torch.Tensor, spec_name: str) -> torch.Tensor:
+    """The DP profile's diagonal quantization in the rotated basis (src/liqk_v2.py:469-506): per 256-block scale
+    d = fp16(max|w| / max_g), then LIQK_PROFILE_ITERS (default 2) rounds of sub-block quantization through the bank's
+    1-D table (the lut_subs_quant kernel for 64-column tables unless LIQK_PROFILE_CUDA=0, else the torch path) and the
+    weighted least-squares refit of d.  Returns d * G [M, K]."""
+    _lib.require_cuda(W_rot, diag_h)
+    device = W_rot.device
+    M, K = W_rot.shape
+    nblocks = K // QK_K
+    bank = get_warp_register_bank(spec_name, device)
+    lut_val = bank["lut_val"]
+    max_g = bank["max_grid"]
+    inv_step = (N_LUT_BUCKETS - 1) / (2.0 * max_g)
+    half_b = (N_LUT_BUCKETS - 1) * 0.5
+    w_blks = W_rot.float().contiguous().view(M * nblocks, QK_K)
+    dh_blks = diag_h.float().view(1, nblocks, QK_K).expand(M, nblocks, QK_K).reshape(M * nblocks, QK_K).contiguous()
+    B_tot = M * nblocks
+    S_tot = B_tot * NUM_SUBBLOCKS
+    d_cur = (w_blks.abs().amax(dim=1) / max_g).to(torch.float16).to(torch.float32).clamp(min=1e-8)
+    dhs = dh_blks.view(S_tot, SUBBLOCK_SIZE, 1)
+    G_blk = None
+    for _ in range(int(os.environ.get("LIQK_PROFILE_ITERS", "2"))):
+        x_subs = (w_blks / d_cur.unsqueeze(1)).view(S_tot, SUBBLOCK_SIZE)
+        if lut_val.shape[1] == 64 and os.environ.get("LIQK_PROFILE_CUDA", "1") == "1":
+            from .tcq_proto import lut_subs_quant_cuda
+            G_blk = lut_subs_quant_cuda(x_subs, dh_blks.view(S_tot, SUBBLOCK_SIZE), lut_val, inv_step,
+                                        half_b).view(B_tot, QK_K)
+        else:
+            G_blk = quantize_subs_lut_chunked(x_subs, dhs, lut_val, inv_step, half_b).view(B_tot, QK_K)
+        num = (dh_blks * w_blks * G_blk).sum(dim=1)
+        den = (dh_blks * G_blk * G_blk).sum(dim=1).clamp(min=1e-12)
+        d_cur = (num / den).to(torch.float16).to(torch.float32).clamp(min=1e-8)
+    return (d_cur.unsqueeze(1) * G_blk).view(M, K)
 
 
 @torch.no_grad()

@@ -15,7 +15,7 @@ import torch
 from . import _lib
 from ._lib import ptr
 
-__all__ = ["make_gains", "viterbi_ub_cuda", "viterbi_ub", "install"]
+__all__ = ["make_gains", "viterbi_ub_cuda", "viterbi_ub", "lut_subs_quant_cuda", "install"]
 
 
 def make_gains(h: int, step: float, device="cuda") -> torch.Tensor:
@@ -129,6 +129,24 @@ def viterbi_ub(x: torch.Tensor, small: torch.Tensor, K: int, nu: int, m: int, ga
     return rec, (idx // U).long(), (idx % U).long(), gi[:, ::sub].long()
 
 
+@torch.no_grad()
+def lut_subs_quant_cuda(x_subs: torch.Tensor, dh: torch.Tensor, lut_val: torch.Tensor, inv_step: float, half_b: float):
+    """DP-profile sub-block quantization through the 1-D table (src/tcq_proto.py:538-547, kernel
+    src/cuda/tcq_viterbi.cu:768-811): x_subs, dh [S, 16] -> [S, 16], each sub-block's 16 values taken from the table
+    column with the smallest weighted error (C-ABI `lut_subs_quant`, one warp per sub-block)."""
+    assert lut_val.shape[1] == 64
+    dev = _lib.require_cuda(x_subs, dh, lut_val)
+    x = x_subs.float().contiguous()
+    d = dh.float().reshape(x.shape).contiguous()
+    lut = lut_val.float().contiguous()
+    out = torch.empty_like(x)
+    rc = _lib.lib().lut_subs_quant(ptr(x), ptr(d), ptr(lut), ptr(out), x.shape[0], inv_step, half_b, lut.shape[0],
+                                   _lib.stream_ptr(dev))
+    if rc != 0:
+        raise RuntimeError(f"lut_subs_quant: CUDA error code {rc}")
+    return out
+
+
 def install(module=None):
     """Point a reference `src.tcq_proto` module (or any module binding `viterbi_ub_cuda`) at this implementation, so the
     reference's callers run on the B200 kernels unchanged (they bind `viterbi_ub_cuda` at call time or at import)."""
@@ -137,4 +155,5 @@ def install(module=None):
                                                    if m is not None and n.endswith("tcq_proto")]
     for mod in targets:
         mod.viterbi_ub_cuda = viterbi_ub_cuda
+        mod.lut_subs_quant_cuda = lut_subs_quant_cuda
     return targets

@@ -10,6 +10,7 @@ Contents, each restated from the reference (lumen-inference/ltq-research; paths 
 * ``LtqFormat`` …        — the format reference src/ltq_format.py:21-147 (labels, tile packing and decoding).
 * ``pack_slice_regions`` / ``decode_slice_regions`` — src/ltq_file.py:54-148 (SoA regions on 64-byte boundaries).
 * ``fwht``               — src/iqk_format.py:153-170 (normalized block FWHT, same butterfly order, fp32).
+* ``lut_subs``           — src/cuda/tcq_viterbi.cu:768-804 (DP-profile sub-block quantization through the 1-D table).
 
 Parity pins live in tests/test_oracle_golden.py.
 """
@@ -51,6 +52,8 @@ def lib():
         L.ora_tcq_viterbi.argtypes = ([ctypes.c_void_p] * 15 + [ctypes.c_int] * 18 +
                                       [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int])
         L.ora_max_threads.restype = ctypes.c_int
+        L.ora_lut_subs.restype = None
+        L.ora_lut_subs.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int]
         _LIB = L
     return _LIB
 
@@ -375,3 +378,14 @@ def max_threads() -> int:
 if __name__ == "__main__":
     build()
     print(LIB_PATH, os.path.getsize(LIB_PATH), "bytes,", max_threads(), "threads")
+
+
+def lut_subs(xs, dh, lut, inv_step: float, half_b: float) -> np.ndarray:
+    """lut_subs_quant (src/cuda/tcq_viterbi.cu:768-811) on CPU: xs, dh [S, 16], lut [nb, 64] -> [S, 16]."""
+    x = _f32(xs).reshape(-1, 16)
+    d = _f32(dh).reshape(x.shape)
+    t = _f32(lut)
+    assert t.ndim == 2 and t.shape[1] == 64
+    out = np.empty_like(x)
+    lib().ora_lut_subs(_ptr(x), _ptr(d), _ptr(t), _ptr(out), x.shape[0], float(inv_step), float(half_b), t.shape[0])
+    return out

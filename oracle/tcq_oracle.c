@@ -25,6 +25,7 @@
  * :363-367, :392-420); final argmin = smallest value then smallest flat index g*S + s (:561-579, :591-594);
  * candidates strict `<`, lowest gain index (:167-177); reconstruction level strict `<`, lowest u (:674-678).
  */
+#include <limits.h>
 #include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -473,4 +474,48 @@ int ora_max_threads(void)
 #else
     return 1;
 #endif
+}
+
+/* DP-profile sub-block quantization through a 1-D table (src/cuda/tcq_viterbi.cu:768-804, lut_subs_kernel, as its nvcc
+ * build computes it): bucket b = rint(fma(x, inv_step, half_b)) converted to int like cvt.rzi.s32 (NaN -> 0, saturating)
+ * and clamped to [0, nb - 1]; err[c] = fma(d * e, e, err[c]) with e = x - lut[b][c] over j = 0..15 in order; best = the
+ * first strict minimum scanned from c = 0; out[j] = lut[b_j][best]. */
+static int ora_cvt_s32(float v)
+{
+    if (v != v) return 0;
+    if (v >= 2147483648.0f) return INT_MAX;
+    if (v <= -2147483648.0f) return INT_MIN;
+    return (int)v;
+}
+
+void ora_lut_subs(const float* xs, const float* dh, const float* lut, float* out, int S, float inv_step, float half_b,
+                  int nb)
+{
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static)
+#endif
+    for (long long i = 0; i < S; i++) {
+        float err[64];
+        int bj[16];
+        for (int c = 0; c < 64; c++) err[c] = 0.f;
+        for (int j = 0; j < 16; j++) {
+            const float x = xs[i * 16 + j], d = dh[i * 16 + j];
+            int b = ora_cvt_s32(rintf(fmaf(x, inv_step, half_b)));
+            b = b < 0 ? 0 : (b > nb - 1 ? nb - 1 : b);
+            bj[j] = b;
+            for (int c = 0; c < 64; c++) {
+                const float e = x - lut[(long long)b * 64 + c];
+                const float t = d * e;
+                err[c] = fmaf(t, e, err[c]);
+            }
+        }
+        int best = 0;
+        float be = err[0];
+        for (int c = 1; c < 64; c++)
+            if (err[c] < be) {
+                be = err[c];
+                best = c;
+            }
+        for (int j = 0; j < 16; j++) out[i * 16 + j] = lut[(long long)bj[j] * 64 + best];
+    }
 }
