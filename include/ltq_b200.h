@@ -173,6 +173,16 @@ int ltq_pack_slice(const int16_t* idx, const uint8_t* gi, long long ld, int R, i
 int ltq_decode_slice(const uint8_t* data, int R, int K, int kbits, int frac, int h, int sub, const int* masks,
                      int n_masks, const float* lut, const float* gain_tab, float* out, long long ld_out,
                      const float* ref, long long ld_ref, unsigned long long* mismatches, void* stream);
+/*
+ * Batch-1 product y = W x straight from a packed slice (the inference-side decode; the reference prototypes it in
+ * src/cuda/ltq_matvec_bench.cu:77-150): y[r] = sum_b d[r][b] sum_{k in block b} val(r, k) x_rot[k] for the slice's R
+ * rows, with val the spec-decoded tile value, d[r][b] = fp16 d_row[r] * 2^(e[r][b] / 4) (d_row as fp16 bits, e int8 with
+ * row stride ld_e) and x_rot = H256(suh * x) (ltq_fwht256 mode 2), so y = W x for W = H256(d val) * suh.  K % 256 == 0,
+ * kbits <= 6, data 64-byte and x_rot 16-byte aligned.  Deterministic (fixed summation order).
+ */
+int ltq_matvec_slice(const uint8_t* data, int R, int K, int kbits, int frac, int h, int sub, const int* masks,
+                     int n_masks, const float* lut, const float* gain_tab, const uint16_t* d_row, const int8_t* e,
+                     long long ld_e, const float* x_rot, float* y, void* stream);
 
 /*
  * Allocation-free tail-biting Viterbi.  No counterpart in the reference (the reference's Python wrapper allocates all

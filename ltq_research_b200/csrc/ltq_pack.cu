@@ -14,6 +14,7 @@
 // ltq_pack_slice_kernel / ltq_decode_slice_kernel: one warp per tile.  Lane L owns row L / 2, columns 8 (L & 1) .. + 7
 // (one 16-byte load of idx, one 8-byte load of gi); a field word is assembled from the owning lanes' bit fragments with
 // warp shuffles.  Both are HBM-bound (3 bytes read per weight for packing, tile_bytes / 256 written).
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include "ltq_b200.h"
@@ -231,6 +232,107 @@ PackArgs pack_args(int R, int K, int kbits, int frac, int h, int sub)
     return a;
 }
 
+
+// ------------------------------------------------------------------------------------------------
+// Batch-1 matrix-vector product straight from a packed slice (the inference-side step after quantization;
+// src/cuda/ltq_matvec_bench.cu:77-150 prototypes it on a row-tile layout, this runs on the .ltq file's 16 x 16 tiles):
+//   y[r] = sum_b d[r][b] * sum_{k in block b} val(r, k) * xr[k],   d[r][b] = d_row[r] * 2^(e[r][b] / 4)
+// with val the spec-decoded tile value gain[g] * lut[label * U + u] and xr the rotated input H256 (suh * x), so that
+// y = W x for the assembled W = H256(d val) * suh.  One CTA per 16-row tile group, four warps taking the 256-column
+// blocks round-robin; lane L owns row L / 2 and columns 8 (L & 1) .. + 7 of every tile (as the decode kernel).  The
+// ten code bits ending at a position are one funnel shift of the tile's 256-bit code string and a bit reversal.  Sums:
+// per lane sequential fmas over a block's 16 tiles x 8 columns, the block scale, the two half-rows, then the warps in a
+// fixed order — deterministic.
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) ltq_matvec_slice_kernel(const uint8_t* __restrict__ data,
+                                                               const float* __restrict__ lut,
+                                                               const float* __restrict__ gain_tab,
+                                                               const uint16_t* __restrict__ d_row,
+                                                               const int8_t* __restrict__ e, long long ld_e,
+                                                               const float* __restrict__ xr, float* __restrict__ y,
+                                                               const DecodeArgs d)
+{
+    __shared__ float red[4][16];
+    const PackArgs& a = d.p;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 1, hf = lane & 1;
+    const long long rg = blockIdx.x;
+    const long long row = rg * 16 + r;
+    const int nblk = a.tiles_per_row / 16;
+    const int U = 1 << (a.kbits - 1);
+    const float drow = __half2float(__ushort_as_half(d_row[row]));
+    const int w_hi = r >> 1, w_lo = (w_hi + 7) & 7;  // 32-bit code words holding this lane's positions and the 32 before
+    const int o0 = 16 * (r & 1) + 8 * hf;            // bit offset of the lane's first position in word w_hi
+    const int kg = 16 * r / a.sub;                   // sub-block of the lane's positions (16 r .. 16 r + 15)
+    float acc = 0.f;
+    for (int b = warp; b < nblk; b += 4) {
+        float part = 0.f;
+        for (int kt = 0; kt < 16; kt++) {
+            const long long t = rg * a.tiles_per_row + (long long)b * 16 + kt;
+            const uint32_t* cw = reinterpret_cast<const uint32_t*>(data + a.off[0] + t * 32);
+            const uint32_t hi = __ldg(cw + w_hi), lo = __ldg(cw + w_lo);
+            const uint16_t* pl = reinterpret_cast<const uint16_t*>(data + a.off[1]) + t * a.nw[1];
+            const uint16_t* lw = reinterpret_cast<const uint16_t*>(data + a.off[2]) + t * a.nw[2];
+            const uint16_t* gw = reinterpret_cast<const uint16_t*>(data + a.off[3]) + t * a.nw[3];
+            uint64_t planes = 0;  // bit (p - 1) * 16 + c: plane p at column c of row r (kbits <= 6)
+            for (int p = 1; p < a.kbits - 1; p++) planes |= (uint64_t)__ldg(pl + (p - 1) * 16 + r) << (16 * (p - 1));
+            int g = 0;
+            if (a.h > 0)
+                for (int i = 0; i < a.h; i++) {
+                    const int bb = kg * a.h + i;
+                    g |= ((__ldg(gw + (bb >> 4)) >> (bb & 15)) & 1) << i;
+                }
+            const float gain = a.h > 0 ? __ldg(gain_tab + g) : 1.0f;
+            const float* xt = xr + (long long)b * 256 + kt * 16 + 8 * hf;
+            const float4 xa = __ldg(reinterpret_cast<const float4*>(xt)), xb = __ldg(reinterpret_cast<const float4*>(xt + 4));
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int pos = 16 * r + 8 * hf + j;
+                // bits pos - 31 .. pos of the code string, newest in bit 31; reversed, the state s has the newest in bit 0
+                const uint32_t win = __funnelshift_rc(lo, hi, o0 + j + 1);
+                const unsigned st = __brev(win) & 0x3ffu;
+                const unsigned v = st >> 1;
+                int lab = (int)(st & 1) | ((__popc(v & d.m0) & 1) << 1);
+                if (d.nmask > 1) lab |= (__popc(v & d.m1) & 1) << 2;
+                if (d.nmask > 2) lab |= (__popc(v & d.m2) & 1) << 3;
+                int u;
+                if (a.frac == 0) {
+                    u = (__ldg(lw + (pos >> 4)) >> (pos & 15)) & 1;
+                } else if (a.frac == 1) {
+                    const int bb = pos >> 1;
+                    u = (__ldg(lw + (bb >> 4)) >> (bb & 15)) & 1;
+                } else {
+                    const int q4 = pos >> 2, i = pos & 3;
+                    if (i < 3) {
+                        const int bb = 3 * q4 + i;
+                        u = (__ldg(lw + (bb >> 4)) >> (bb & 15)) & 1;
+                    } else {
+                        u = 0;
+                        for (int k = 0; k < 3; k++) {
+                            const int bb = 3 * q4 + k;
+                            u ^= (__ldg(lw + (bb >> 4)) >> (bb & 15)) & 1;
+                        }
+                    }
+                }
+                const int c = pos & 15;
+                for (int p = 1; p < a.kbits - 1; p++) u |= (int)((planes >> (16 * (p - 1) + c)) & 1) << p;
+                const float val = __fmul_rn(gain, __ldg(lut + lab * U + u));
+                part = __fmaf_rn(val, xv[j], part);
+            }
+        }
+        const float db = __fmul_rn(drow, exp2f(0.25f * (float)e[row * ld_e + b]));
+        acc = __fmaf_rn(db, part, acc);
+    }
+    acc = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 1));
+    if (hf == 0) red[warp][r] = acc;
+    __syncthreads();
+    if (threadIdx.x < 16) {
+        float s = red[0][threadIdx.x];
+        for (int w = 1; w < 4; w++) s = __fadd_rn(s, red[w][threadIdx.x]);
+        y[rg * 16 + threadIdx.x] = s;
+    }
+}
+
 }  // namespace
 
 extern "C" size_t ltq_slice_bytes(int R, int K, int kbits, int frac, int h, int sub)
@@ -271,5 +373,25 @@ extern "C" int ltq_decode_slice(const uint8_t* data, int R, int K, int kbits, in
     ltq_decode_slice_kernel<<<(unsigned)((d.p.T + 7) / 8), 256, 0, (cudaStream_t)stream>>>(data, lut, gain_tab, out,
                                                                                           ld_out, ref, ld_ref,
                                                                                           mismatches, d);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_matvec_slice(const uint8_t* data, int R, int K, int kbits, int frac, int h, int sub, const int* masks,
+                                int n_masks, const float* lut, const float* gain_tab, const uint16_t* d_row,
+                                const int8_t* e, long long ld_e, const float* x_rot, float* y, void* stream)
+{
+    if (!fmt_ok(R, K, kbits, frac, h, sub) || K % 256 || kbits > 6 || !masks || n_masks < 1 || n_masks > 3 || !lut ||
+        (h > 0 && !gain_tab) || !d_row || !e || ld_e < K / 256 || !x_rot || !y || ((uintptr_t)data & 63) ||
+        ((uintptr_t)x_rot & 15))
+        return -1;
+    DecodeArgs d{};
+    d.p = pack_args(R, K, kbits, frac, h, sub);
+    d.m0 = (unsigned)masks[0];
+    d.m1 = n_masks > 1 ? (unsigned)masks[1] : 0u;
+    d.m2 = n_masks > 2 ? (unsigned)masks[2] : 0u;
+    d.nmask = n_masks;
+    if (R == 0) return 0;
+    ltq_matvec_slice_kernel<<<(unsigned)(R / 16), 128, 0, (cudaStream_t)stream>>>(data, lut, gain_tab, d_row, e, ld_e,
+                                                                                  x_rot, y, d);
     return (int)cudaGetLastError();
 }

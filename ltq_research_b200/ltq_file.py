@@ -157,6 +157,53 @@ def assemble(G: torch.Tensor, d_row: torch.Tensor, e: torch.Tensor, suh: torch.T
     return fwht_inplace(W, block_size=TILE) * suh.float().unsqueeze(0)
 
 
+def rotate_input(x: torch.Tensor, suh: torch.Tensor) -> torch.Tensor:
+    """x_rot = H256(suh * x) for x [..., K]: the input of the packed-matrix product (W x = (d val) x_rot for
+    W = H256(d val) * suh, the block FWHT being symmetric)."""
+    from .liqk_v2 import fwht_rows_scaled
+    K = x.shape[-1]
+    return fwht_rows_scaled(x.reshape(-1, K).float().contiguous(), suh.float().contiguous(), mode=2).reshape(x.shape)
+
+
+def matvec_slice_device(data: torch.Tensor, R: int, K: int, f: LtqFormat, d_row: torch.Tensor, e: torch.Tensor,
+                        x_rot: torch.Tensor, y: Optional[torch.Tensor] = None, lut: Optional[torch.Tensor] = None,
+                        gains: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y [R] = (d val) x_rot for one packed slice (ltq_matvec_slice): val the spec-decoded tile values, d = d_row (fp16
+    [R]) * 2^(e [R, K/256] / 4), x_rot = rotate_input(x, suh) [K] fp32."""
+    _check_fmt(f)
+    dev = data.device
+    if lut is None or gains is None:
+        lt, gt = _tables(f, dev)
+        lut = lt if lut is None else lut
+        gains = gt if gains is None else gains
+    if y is None:
+        y = torch.empty(R, dtype=torch.float32, device=dev)
+    dh = d_row.to(torch.float16).contiguous()
+    ec = e.to(torch.int8).contiguous()
+    xr = x_rot.float().contiguous()
+    masks = (ctypes.c_int * 3)(*([int(m) for m in f.masks] + [0, 0, 0])[:3])
+    rc = _lib.lib().ltq_matvec_slice(ptr(data), R, K, f.K, f.frac, f.h, f.sub, ctypes.cast(masks, ctypes.c_void_p),
+                                     len(f.masks), ptr(lut), ptr(gains), ptr(dh), ptr(ec), ec.stride(0), ptr(xr),
+                                     ptr(y), _lib.stream_ptr(dev))
+    if rc != 0:
+        raise RuntimeError(f"ltq_matvec_slice: error code {rc}")
+    return y
+
+
+def matvec(data: torch.Tensor, slices, formats: List[LtqFormat], d_row: torch.Tensor, e: torch.Tensor,
+           suh: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """y = W x [M] for a packed matrix (its .ltq data tensor on the device, 64-byte aligned, and the slice table rows
+    [r0, r1, format, offset]) without decoding it to memory: one input rotation, one kernel per row slice."""
+    K = suh.shape[0]
+    M = d_row.shape[0]
+    xr = rotate_input(x.reshape(K).to(data.device), suh.to(data.device))
+    y = torch.empty(M, dtype=torch.float32, device=data.device)
+    for r0, r1, fi, off in (slices.tolist() if torch.is_tensor(slices) else slices):
+        matvec_slice_device(data[off:], r1 - r0, K, formats[fi], d_row[r0:r1].to(data.device),
+                            e[r0:r1].to(data.device), xr, y=y[r0:r1])
+    return y
+
+
 def pack_matrix_device(m: dict, formats: Dict[str, LtqFormat], verify: bool = True):
     """All row slices of a quantized matrix (liqk_v2.PACK["matrix"] fields, device tensors) packed into one uint8 CUDA
     buffer laid out as the .ltq data tensor (each slice at a multiple of 64 bytes), and the slice table rows
@@ -276,6 +323,14 @@ class LtqFile:
         for r0, r1, fi, off in self.tensor(f"{p}.ltq.slices").tolist():
             decode_slice_device(data[off:], r1 - r0, K, self.formats[fi], out=G[r0:r1])
         return assemble(G, d_row, e, suh)
+
+    def matvec(self, p: str, x: torch.Tensor, device="cuda") -> torch.Tensor:
+        """y = W x for matrix p, computed from its packed tiles on the device (ltq_matvec_slice)."""
+        d_row, e, suh = (self.tensor(f"{p}.ltq.{k}").to(device) for k in ("d_row", "e", "suh"))
+        raw = np.frombuffer(self.raw(f"{p}.ltq.data"), dtype=np.uint8)
+        data = torch.empty(_align(max(raw.size, 1), 64), dtype=torch.uint8, device=device)
+        data[: raw.size].copy_(torch.from_numpy(raw.copy()))
+        return matvec(data, self.tensor(f"{p}.ltq.slices"), self.formats, d_row, e, suh, x)
 
 
 def main():
