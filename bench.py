@@ -252,6 +252,66 @@ def isolated_block_roofline(dev, spec: str, rows: int = 27648, timed: bool = Tru
             "achieved": acs / (statistics.median(ms) * 1e-3) / 1e9}
 
 
+def _event_ms(fn, reps: int = 5) -> float:
+    """Median device time of fn() (CUDA events on the current stream, after two untimed calls)."""
+    for _ in range(2):
+        fn()
+    ms = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms.append(a.elapsed_time(b))
+    return statistics.median(ms)
+
+
+def aux_measurements(dev, fmts) -> dict:
+    """The secondary paths on one GPU:
+    * decode GEMV: y = W x from the packed tiles of a gate-shaped 8192 x 3072 TCQ3X matrix: the kernel alone
+      (ltq_matvec_slice on the rotated input; weights / s and packed bytes / s) and the whole call (input rotation +
+      kernel through ltq_file.matvec), each as 20 back-to-back calls;
+    * rings: quantize_rings of a 2048 x 2560 bf16 table (20,480 rings, TCQ4X, rotation, three scale tries,
+      tail-biting with a full first pass): values / s and the Viterbi's ACS rate (2 passes x 1024 x 4 slots x 3 tries
+      per value);
+    * DP-profile table kernel: lut_subs_quant over 2^20 sub-blocks with an 8192 x 64 table: sub-blocks / s."""
+    from ltq_research_b200.batch import quantize_matrices
+    from ltq_research_b200.ltq_file import matvec, matvec_slice_device, rotate_input
+    from ltq_research_b200.rings import quantize_rings
+    from ltq_research_b200.tcq_proto import lut_subs_quant_cuda
+    out = {"impl": "aux", "data": "synthetic (seeded)"}
+    W, H = make_matrix(8192, 3072, 5, dev)
+    r = quantize_matrices([(W, H, "TCQ3X")], ltq_formats=fmts, pack=False)[0]["ltq"]
+    data = torch.zeros(((r["data"].numel() + 63) // 64) * 64, dtype=torch.uint8, device=dev)
+    data[: r["data"].numel()] = r["data"]
+    x = torch.randn(3072, device=dev)
+    fl = list(fmts.values())
+    xr = rotate_input(x, r["suh"])
+    (r0, r1, fi, off), = r["slices"]
+    y = torch.empty(8192, device=dev)
+    reps = 20  # back-to-back calls between the events, so that host issue time does not count
+    ms_k = _event_ms(lambda: [matvec_slice_device(data[off:], r1 - r0, 3072, fl[fi], r["d_row"], r["e"], xr, y=y)
+                              for _ in range(reps)]) / reps
+    ms = _event_ms(lambda: [matvec(data, r["slices"], fl, r["d_row"], r["e"], r["suh"], x) for _ in range(reps)]) / reps
+    out["decode_gemv"] = {"shape": [8192, 3072], "format": "TCQ3X", "kernel_ms": ms_k, "call_ms": ms,
+                          "gweights_per_s": 8192 * 3072 / ms_k / 1e6, "packed_gb_per_s": r["data"].numel() / ms_k / 1e6}
+    g = torch.Generator().manual_seed(4)
+    T = (torch.randn(2048, 2560, generator=g) * 0.03 * torch.exp(0.5 * torch.randn(2048, 1, generator=g))
+         ).to(torch.bfloat16).to(dev)
+    ms = _event_ms(lambda: quantize_rings(T, "TCQ4X", True), reps=3)
+    n = T.numel()
+    out["rings"] = {"table": [2048, 2560], "format": "TCQ4X:rot", "ms": ms, "mvalues_per_s": n / ms / 1e3,
+                    "gacs_per_s": n * 2 * 1024 * 4 * 3 / ms / 1e6}
+    S = 1 << 20
+    xs = torch.randn(S, 16, device=dev)
+    dh = torch.rand(S, 16, device=dev) + 0.1
+    lut = torch.sort(torch.randn(8192, 64, device=dev), dim=0).values
+    ms = _event_ms(lambda: lut_subs_quant_cuda(xs, dh, lut, 8191 / 8.0, 4095.5))
+    out["lut_subs"] = {"sub_blocks": S, "table": [8192, 64], "ms": ms, "msub_blocks_per_s": S / ms / 1e3}
+    return out
+
+
 def write_kernel_list(args, timed, fmts):
     """The timed layers quantized once more under torch.profiler (CUPTI activity records, device timestamps): per
     kernel name its launches, summed device time and share of the summed time, as a markdown table.  Kernels of
@@ -300,6 +360,9 @@ def main():
     ap.add_argument("--profile-viterbi", default=None, metavar="FORMAT",
                     help="three stand-alone two-pass Viterbi calls (ltq_viterbi_tb) of FORMAT over the --rows / 16 "
                          "tiles of one sub-block, for ncu captures of vit_fwd_kernel")
+    ap.add_argument("--aux", action="store_true",
+                    help="time the secondary paths instead of the layer step (one JSON line): the decode GEMV from "
+                         "packed tiles, ring quantization (config 5's path) and the DP-profile table kernel")
     ap.add_argument("--kernel-list", default=None, metavar="PATH",
                     help="after the warm-up, quantize the timed layers once under the CUDA profiler (CUPTI) and write "
                          "the per-kernel launch list (launches, total device time, share) to PATH as markdown")
@@ -325,6 +388,9 @@ def main():
     from ltq_research_b200.formats import load_formats
     fmts = load_formats(list(FORMATS), dev)
 
+    if args.aux:
+        print(json.dumps(aux_measurements(dev, fmts)), flush=True)
+        return
     if args.profile_viterbi:
         r = Lq._TcqRunner(args.profile_viterbi, args.rows, dev)
         g = torch.Generator(device=dev).manual_seed(1)

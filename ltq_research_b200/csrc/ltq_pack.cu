@@ -238,13 +238,14 @@ PackArgs pack_args(int R, int K, int kbits, int frac, int h, int sub)
 // src/cuda/ltq_matvec_bench.cu:77-150 prototypes it on a row-tile layout, this runs on the .ltq file's 16 x 16 tiles):
 //   y[r] = sum_b d[r][b] * sum_{k in block b} val(r, k) * xr[k],   d[r][b] = d_row[r] * 2^(e[r][b] / 4)
 // with val the spec-decoded tile value gain[g] * lut[label * U + u] and xr the rotated input H256 (suh * x), so that
-// y = W x for the assembled W = H256(d val) * suh.  One CTA per 16-row tile group, four warps taking the 256-column
-// blocks round-robin; lane L owns row L / 2 and columns 8 (L & 1) .. + 7 of every tile (as the decode kernel).  The
+// y = W x for the assembled W = H256(d val) * suh.  One CTA per 16-row tile group with one warp per 256-column block
+// (at most 32, round-robin beyond), 64 registers a thread so that 32 warps fit an SM; lane L owns row L / 2 and columns
+// 8 (L & 1) .. + 7 of every tile (as the decode kernel).  The
 // ten code bits ending at a position are one funnel shift of the tile's 256-bit code string and a bit reversal.  Sums:
 // per lane sequential fmas over a block's 16 tiles x 8 columns, the block scale, the two half-rows, then the warps in a
 // fixed order — deterministic.
 // ------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) ltq_matvec_slice_kernel(const uint8_t* __restrict__ data,
+__global__ void __launch_bounds__(1024, 1) ltq_matvec_slice_kernel(const uint8_t* __restrict__ data,
                                                                const float* __restrict__ lut,
                                                                const float* __restrict__ gain_tab,
                                                                const uint16_t* __restrict__ d_row,
@@ -252,7 +253,9 @@ __global__ void __launch_bounds__(128) ltq_matvec_slice_kernel(const uint8_t* __
                                                                const float* __restrict__ xr, float* __restrict__ y,
                                                                const DecodeArgs d)
 {
-    __shared__ float red[4][16];
+    __shared__ float red[32][16];
+    __shared__ float s_lut[16 * 32];  // value table (labels x U <= 16 x 32) and gains, read per position
+    __shared__ float s_gain[16];
     const PackArgs& a = d.p;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 1, hf = lane & 1;
     const long long rg = blockIdx.x;
@@ -260,12 +263,17 @@ __global__ void __launch_bounds__(128) ltq_matvec_slice_kernel(const uint8_t* __
     const int nblk = a.tiles_per_row / 16;
     const int U = 1 << (a.kbits - 1);
     const float drow = __half2float(__ushort_as_half(d_row[row]));
+    for (int i = threadIdx.x; i < (2 << d.nmask) * U; i += blockDim.x) s_lut[i] = lut[i];
+    if (a.h > 0 && threadIdx.x < (1 << a.h)) s_gain[threadIdx.x] = gain_tab[threadIdx.x];
+    __syncthreads();
     const int w_hi = r >> 1, w_lo = (w_hi + 7) & 7;  // 32-bit code words holding this lane's positions and the 32 before
     const int o0 = 16 * (r & 1) + 8 * hf;            // bit offset of the lane's first position in word w_hi
     const int kg = 16 * r / a.sub;                   // sub-block of the lane's positions (16 r .. 16 r + 15)
     float acc = 0.f;
-    for (int b = warp; b < nblk; b += 4) {
+    const int nwarps = blockDim.x >> 5;
+    for (int b = warp; b < nblk; b += nwarps) {
         float part = 0.f;
+#pragma unroll 2
         for (int kt = 0; kt < 16; kt++) {
             const long long t = rg * a.tiles_per_row + (long long)b * 16 + kt;
             const uint32_t* cw = reinterpret_cast<const uint32_t*>(data + a.off[0] + t * 32);
@@ -281,7 +289,7 @@ __global__ void __launch_bounds__(128) ltq_matvec_slice_kernel(const uint8_t* __
                     const int bb = kg * a.h + i;
                     g |= ((__ldg(gw + (bb >> 4)) >> (bb & 15)) & 1) << i;
                 }
-            const float gain = a.h > 0 ? __ldg(gain_tab + g) : 1.0f;
+            const float gain = a.h > 0 ? s_gain[g] : 1.0f;
             const float* xt = xr + (long long)b * 256 + kt * 16 + 8 * hf;
             const float4 xa = __ldg(reinterpret_cast<const float4*>(xt)), xb = __ldg(reinterpret_cast<const float4*>(xt + 4));
             const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -316,7 +324,7 @@ __global__ void __launch_bounds__(128) ltq_matvec_slice_kernel(const uint8_t* __
                 }
                 const int c = pos & 15;
                 for (int p = 1; p < a.kbits - 1; p++) u |= (int)((planes >> (16 * (p - 1) + c)) & 1) << p;
-                const float val = __fmul_rn(gain, __ldg(lut + lab * U + u));
+                const float val = __fmul_rn(gain, s_lut[lab * U + u]);
                 part = __fmaf_rn(val, xv[j], part);
             }
         }
@@ -328,7 +336,7 @@ __global__ void __launch_bounds__(128) ltq_matvec_slice_kernel(const uint8_t* __
     __syncthreads();
     if (threadIdx.x < 16) {
         float s = red[0][threadIdx.x];
-        for (int w = 1; w < 4; w++) s = __fadd_rn(s, red[w][threadIdx.x]);
+        for (int w = 1; w < nwarps; w++) s = __fadd_rn(s, red[w][threadIdx.x]);
         y[rg * 16 + threadIdx.x] = s;
     }
 }
@@ -391,7 +399,9 @@ extern "C" int ltq_matvec_slice(const uint8_t* data, int R, int K, int kbits, in
     d.m2 = n_masks > 2 ? (unsigned)masks[2] : 0u;
     d.nmask = n_masks;
     if (R == 0) return 0;
-    ltq_matvec_slice_kernel<<<(unsigned)(R / 16), 128, 0, (cudaStream_t)stream>>>(data, lut, gain_tab, d_row, e, ld_e,
-                                                                                  x_rot, y, d);
+    const int nwarps = K / 256 < 32 ? K / 256 : 32;
+    if (nwarps == 0) return -1;
+    ltq_matvec_slice_kernel<<<(unsigned)(R / 16), 32 * nwarps, 0, (cudaStream_t)stream>>>(data, lut, gain_tab, d_row, e,
+                                                                                          ld_e, x_rot, y, d);
     return (int)cudaGetLastError();
 }
