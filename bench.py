@@ -501,7 +501,8 @@ def main():
             bpw = json.loads(prof.read_text()).get("dram_bytes_per_weight")
             if bpw:  # per average launch: weights x DRAM bytes per weight (ncu capture; mean of the two formats)
                 traffic = float(np.mean(list(bpw.values()))) * block_weights / len(ev)
-        cpu = None if args.no_cpu_baseline else cpu_baseline_sample()
+        # the CPU baseline is taken at N = 1 only (on rank 0), where the host cores are not shared with other ranks
+        cpu = None if (args.no_cpu_baseline or world > 1) else cpu_baseline_sample()
         line = {
             "metric": METRIC, "value": value, "unit": METRIC, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
