@@ -44,11 +44,11 @@ def estimated_seconds(M: int, K: int, spec: Spec) -> float:
 _STREAMS: Dict[tuple, List[torch.cuda.Stream]] = {}
 
 
-def _streams(dev: torch.device, n: int) -> List[torch.cuda.Stream]:
+def _streams(dev: torch.device, n: int, role: str = "lane") -> List[torch.cuda.Stream]:
     """The driver's CUDA streams on `dev`, created once and reused by every call: the caching allocator keeps freed
     blocks per stream, so reusing the streams lets each call reuse the memory the previous calls cached (fresh streams
     on every call would allocate anew and grow the reserved memory call after call)."""
-    key = (str(dev), n)
+    key = (str(dev), n, role)
     if key not in _STREAMS:
         _STREAMS[key] = [torch.cuda.Stream(dev) for _ in range(n)]
     return _STREAMS[key]
@@ -70,7 +70,8 @@ def _record(obj, stream: torch.cuda.Stream):
 def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], seed: int = 1337, damp: float = 0.02,
                       n_streams: int = 8, pack: bool = True, keep_w_hat: bool = False,
                       device: Optional[torch.device] = None, on_issued=None, ltq_formats: Optional[Dict] = None,
-                      to_host: bool = False, gemm: str = "bf16x6", order: str = "lpt") -> List[Dict]:
+                      to_host: bool = False, gemm: str = "bf16x6", order: str = "lpt",
+                      prep_ahead: bool = False) -> List[Dict]:
     """Quantize every (W [M, K], H [K, K], spec) of `jobs` as quantize_matrix_liqk_v2(W, H, spec, seed, damp) would,
     concurrently on `n_streams` CUDA streams.  W / H may be CUDA tensors or (pinned) host tensors, which are copied to
     the device on the matrix's stream.  Returns, per job: {"qdata", "pack" (the PACK["matrix"] fields, device tensors)
@@ -84,7 +85,9 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
     gemm: the mode of the LDLQ inter-block update and refit products (liqk_v2.GEMM_MODES): "bf16x6" (default) runs
     them as fp32-accurate split products on the tensor cores; "fp32" reproduces quantize_matrix_liqk_v2 bit for bit.
     order: the order in which the streams take jobs — "lpt" (default) longest estimated time first, "given" as listed.
-    The results do not depend on it."""
+    prep_ahead: issue each stream's next job's Hessian preparation on a second stream while the current job runs
+    (measured on the bench's layer set: no gain once the device is saturated, so off by default).  The results depend
+    on neither."""
     if not jobs:
         return []
     dev = torch.device(device) if device is not None else None
@@ -107,27 +110,50 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
     else:
         raise ValueError(f"order {order!r}: expected 'lpt' or 'given'")
     out: List[Optional[Dict]] = [None] * len(jobs)
-    # one job in issue per stream; each round advances every job by one step (Hessian preparation, one 256-column
-    # block, refits), so that every stream keeps work queued while the host is blocked on a full launch queue
-    active: List[Optional[tuple]] = [None] * len(streams)
-    while pending or any(a is not None for a in active):
+    preps = _streams(dev, max(1, n_streams), "prep") if prep_ahead else streams
+
+    def start(k: int) -> tuple:
+        """Issue the next job's Hessian preparation (the generator's first step) on lane k's preparation stream."""
+        i = pending.pop()
+        W, H, sp = jobs[i]
+        p, s = preps[k], streams[k]
+        p.wait_stream(main)
+        with torch.cuda.stream(p):
+            Wd = W.to(dev, non_blocking=True) if not W.is_cuda else W
+            Hd = H.to(dev, non_blocking=True) if not H.is_cuda else H
+            for t in (W, H):
+                if t.is_cuda:
+                    t.record_stream(p)
+                    t.record_stream(s)
+            gen = _quantize_matrix_steps(Wd, Hd, sp, seed, damp, None, pack or ltq_formats is not None, None, gemm)
+            next(gen)
+            ev = torch.cuda.Event()
+            ev.record(p)
+        if p is not s:
+            # what the preparation leaves to the later steps was allocated on p and is used and freed on s: the
+            # allocator must not hand that memory to p again before s's work on it has run
+            _record(dict(gen.gi_frame.f_locals), s)
+        return i, gen, ev
+
+    # every lane: one job in its block / refit steps on the lane's stream and, with prep_ahead, the next job's
+    # preparation already issued on the lane's preparation stream (its cuSOLVER / triangular-inverse kernels are
+    # latency-bound and overlap the other jobs' blocks).  Each round advances every lane's current job by one step
+    # (one 256-column block, or the refits), so that every stream keeps work queued.
+    cur: List[Optional[tuple]] = [None] * len(streams)
+    nxt: List[Optional[tuple]] = [None] * len(streams)
+    while pending or any(c is not None for c in cur) or any(n is not None for n in nxt):
         for k, s in enumerate(streams):
-            if active[k] is None and pending:
-                i = pending.pop()
-                W, H, sp = jobs[i]
-                s.wait_stream(main)
-                with torch.cuda.stream(s):
-                    Wd = W.to(dev, non_blocking=True) if not W.is_cuda else W
-                    Hd = H.to(dev, non_blocking=True) if not H.is_cuda else H
-                    if W.is_cuda:
-                        W.record_stream(s)
-                    if H.is_cuda:
-                        H.record_stream(s)
-                active[k] = (i, _quantize_matrix_steps(Wd, Hd, sp, seed, damp, None,
-                                                       pack or ltq_formats is not None, None, gemm))
-            if active[k] is None:
+            if cur[k] is None:
+                if nxt[k] is None and pending:
+                    nxt[k] = start(k)
+                if nxt[k] is not None:
+                    i, gen, ev = nxt[k]
+                    s.wait_event(ev)
+                    cur[k] = (i, gen)
+                    nxt[k] = start(k) if (prep_ahead and pending) else None
+            if cur[k] is None:
                 continue
-            i, gen = active[k]
+            i, gen = cur[k]
             with torch.cuda.stream(s):
                 try:
                     next(gen)
@@ -140,10 +166,10 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
                         if not pack:
                             r["pack"] = None
                     out[i] = r
-                    active[k] = None
+                    cur[k] = None
                     if on_issued is not None:
                         on_issued(i)
-    for s in streams:
+    for s in streams + (preps if prep_ahead else []):
         main.wait_stream(s)
     for i, r in enumerate(out):
         _record(r, main)
