@@ -245,14 +245,16 @@ PackArgs pack_args(int R, int K, int kbits, int frac, int h, int sub)
 // per lane sequential fmas over a block's 16 tiles x 8 columns, the block scale, the two half-rows, then the warps in a
 // fixed order — deterministic.
 // ------------------------------------------------------------------------------------------------
+template <int KB, int FRAC>
 __global__ void __launch_bounds__(1024, 1) ltq_matvec_slice_kernel(const uint8_t* __restrict__ data,
-                                                               const float* __restrict__ lut,
-                                                               const float* __restrict__ gain_tab,
-                                                               const uint16_t* __restrict__ d_row,
-                                                               const int8_t* __restrict__ e, long long ld_e,
-                                                               const float* __restrict__ xr, float* __restrict__ y,
-                                                               const DecodeArgs d)
+                                                                   const float* __restrict__ lut,
+                                                                   const float* __restrict__ gain_tab,
+                                                                   const uint16_t* __restrict__ d_row,
+                                                                   const int8_t* __restrict__ e, long long ld_e,
+                                                                   const float* __restrict__ xr,
+                                                                   float* __restrict__ y, const DecodeArgs d)
 {
+    constexpr int U = 1 << (KB - 1);
     __shared__ float red[32][16];
     __shared__ float s_lut[16 * 32];  // value table (labels x U <= 16 x 32) and gains, read per position
     __shared__ float s_gain[16];
@@ -261,19 +263,23 @@ __global__ void __launch_bounds__(1024, 1) ltq_matvec_slice_kernel(const uint8_t
     const long long rg = blockIdx.x;
     const long long row = rg * 16 + r;
     const int nblk = a.tiles_per_row / 16;
-    const int U = 1 << (a.kbits - 1);
     const float drow = __half2float(__ushort_as_half(d_row[row]));
     for (int i = threadIdx.x; i < (2 << d.nmask) * U; i += blockDim.x) s_lut[i] = lut[i];
     if (a.h > 0 && threadIdx.x < (1 << a.h)) s_gain[threadIdx.x] = gain_tab[threadIdx.x];
     __syncthreads();
     const int w_hi = r >> 1, w_lo = (w_hi + 7) & 7;  // 32-bit code words holding this lane's positions and the 32 before
     const int o0 = 16 * (r & 1) + 8 * hf;            // bit offset of the lane's first position in word w_hi
-    const int kg = 16 * r / a.sub;                   // sub-block of the lane's positions (16 r .. 16 r + 15)
-    float acc = 0.f;
+    // the lane's low-bit field: FRAC 0 one bit per position (word r), D2 one per pair (word r / 2), D4 three per quad
+    // (6 bits from bit 12 r + 6 hf, possibly across two words)
+    const int lb0 = FRAC == 0 ? 16 * r + 8 * hf : (FRAC == 1 ? 8 * r + 4 * hf : 12 * r + 6 * hf);
+    const int lw0 = lb0 >> 4, lsh = lb0 & 15;
+    const int gb0 = (16 * r / a.sub) * a.h;           // the sub-block's gain-index bits
+    const int gw0 = gb0 >> 4, gsh = gb0 & 15;
+    const unsigned gmask = (1u << a.h) - 1u;
     const int nwarps = blockDim.x >> 5;
+    float acc = 0.f;
     for (int b = warp; b < nblk; b += nwarps) {
         float part = 0.f;
-#pragma unroll 2
         for (int kt = 0; kt < 16; kt++) {
             const long long t = rg * a.tiles_per_row + (long long)b * 16 + kt;
             const uint32_t* cw = reinterpret_cast<const uint32_t*>(data + a.off[0] + t * 32);
@@ -281,49 +287,40 @@ __global__ void __launch_bounds__(1024, 1) ltq_matvec_slice_kernel(const uint8_t
             const uint16_t* pl = reinterpret_cast<const uint16_t*>(data + a.off[1]) + t * a.nw[1];
             const uint16_t* lw = reinterpret_cast<const uint16_t*>(data + a.off[2]) + t * a.nw[2];
             const uint16_t* gw = reinterpret_cast<const uint16_t*>(data + a.off[3]) + t * a.nw[3];
-            uint64_t planes = 0;  // bit (p - 1) * 16 + c: plane p at column c of row r (kbits <= 6)
-            for (int p = 1; p < a.kbits - 1; p++) planes |= (uint64_t)__ldg(pl + (p - 1) * 16 + r) << (16 * (p - 1));
-            int g = 0;
-            if (a.h > 0)
-                for (int i = 0; i < a.h; i++) {
-                    const int bb = kg * a.h + i;
-                    g |= ((__ldg(gw + (bb >> 4)) >> (bb & 15)) & 1) << i;
-                }
-            const float gain = a.h > 0 ? s_gain[g] : 1.0f;
+            uint32_t pw[KB > 2 ? KB - 2 : 1];  // plane p - 1 at the lane's 8 columns
+#pragma unroll
+            for (int p = 0; p < KB - 2; p++) pw[p] = (uint32_t)__ldg(pl + p * 16 + r) >> (8 * hf);
+            uint32_t lsb = (uint32_t)__ldg(lw + lw0);
+            if (FRAC == 2 && lw0 + 1 < a.nw[2]) lsb |= (uint32_t)__ldg(lw + lw0 + 1) << 16;
+            lsb >>= lsh;
+            float gain = 1.0f;
+            if (a.h > 0) {
+                uint32_t gv = (uint32_t)__ldg(gw + gw0);
+                if (gsh + a.h > 16 && gw0 + 1 < a.nw[3]) gv |= (uint32_t)__ldg(gw + gw0 + 1) << 16;
+                gain = s_gain[(gv >> gsh) & gmask];
+            }
             const float* xt = xr + (long long)b * 256 + kt * 16 + 8 * hf;
             const float4 xa = __ldg(reinterpret_cast<const float4*>(xt)), xb = __ldg(reinterpret_cast<const float4*>(xt + 4));
             const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const int pos = 16 * r + 8 * hf + j;
                 // bits pos - 31 .. pos of the code string, newest in bit 31; reversed, the state s has the newest in bit 0
                 const uint32_t win = __funnelshift_rc(lo, hi, o0 + j + 1);
                 const unsigned st = __brev(win) & 0x3ffu;
                 const unsigned v = st >> 1;
-                int lab = (int)(st & 1) | ((__popc(v & d.m0) & 1) << 1);
-                if (d.nmask > 1) lab |= (__popc(v & d.m1) & 1) << 2;
-                if (d.nmask > 2) lab |= (__popc(v & d.m2) & 1) << 3;
+                const int lab = (int)(st & 1) | ((__popc(v & d.m0) & 1) << 1) | ((__popc(v & d.m1) & 1) << 2) |
+                                ((__popc(v & d.m2) & 1) << 3);
                 int u;
-                if (a.frac == 0) {
-                    u = (__ldg(lw + (pos >> 4)) >> (pos & 15)) & 1;
-                } else if (a.frac == 1) {
-                    const int bb = pos >> 1;
-                    u = (__ldg(lw + (bb >> 4)) >> (bb & 15)) & 1;
+                if (FRAC == 0) {
+                    u = (lsb >> j) & 1;
+                } else if (FRAC == 1) {
+                    u = (lsb >> (j >> 1)) & 1;
                 } else {
-                    const int q4 = pos >> 2, i = pos & 3;
-                    if (i < 3) {
-                        const int bb = 3 * q4 + i;
-                        u = (__ldg(lw + (bb >> 4)) >> (bb & 15)) & 1;
-                    } else {
-                        u = 0;
-                        for (int k = 0; k < 3; k++) {
-                            const int bb = 3 * q4 + k;
-                            u ^= (__ldg(lw + (bb >> 4)) >> (bb & 15)) & 1;
-                        }
-                    }
+                    const uint32_t q = lsb >> (3 * (j >> 2));
+                    u = (j & 3) < 3 ? (int)((q >> (j & 3)) & 1) : (int)((q ^ (q >> 1) ^ (q >> 2)) & 1);
                 }
-                const int c = pos & 15;
-                for (int p = 1; p < a.kbits - 1; p++) u |= (int)((planes >> (16 * (p - 1) + c)) & 1) << p;
+#pragma unroll
+                for (int p = 0; p < KB - 2; p++) u |= (int)((pw[p] >> j) & 1) << (p + 1);
                 const float val = __fmul_rn(gain, s_lut[lab * U + u]);
                 part = __fmaf_rn(val, xv[j], part);
             }
@@ -339,6 +336,20 @@ __global__ void __launch_bounds__(1024, 1) ltq_matvec_slice_kernel(const uint8_t
         for (int w = 1; w < nwarps; w++) s = __fadd_rn(s, red[w][threadIdx.x]);
         y[rg * 16 + threadIdx.x] = s;
     }
+}
+
+template <int KB>
+int launch_matvec_kb(int frac, unsigned grid, int threads, cudaStream_t st, const uint8_t* data, const float* lut,
+                     const float* gain_tab, const uint16_t* d_row, const int8_t* e, long long ld_e, const float* x_rot,
+                     float* y, const DecodeArgs& d)
+{
+    switch (frac) {
+        case 0: ltq_matvec_slice_kernel<KB, 0><<<grid, threads, 0, st>>>(data, lut, gain_tab, d_row, e, ld_e, x_rot, y, d); break;
+        case 1: ltq_matvec_slice_kernel<KB, 1><<<grid, threads, 0, st>>>(data, lut, gain_tab, d_row, e, ld_e, x_rot, y, d); break;
+        case 2: ltq_matvec_slice_kernel<KB, 2><<<grid, threads, 0, st>>>(data, lut, gain_tab, d_row, e, ld_e, x_rot, y, d); break;
+        default: return -1;
+    }
+    return 0;
 }
 
 }  // namespace
@@ -401,7 +412,17 @@ extern "C" int ltq_matvec_slice(const uint8_t* data, int R, int K, int kbits, in
     if (R == 0) return 0;
     const int nwarps = K / 256 < 32 ? K / 256 : 32;
     if (nwarps == 0) return -1;
-    ltq_matvec_slice_kernel<<<(unsigned)(R / 16), 32 * nwarps, 0, (cudaStream_t)stream>>>(data, lut, gain_tab, d_row, e,
-                                                                                          ld_e, x_rot, y, d);
+    const unsigned grid = (unsigned)(R / 16);
+    const cudaStream_t st = (cudaStream_t)stream;
+    int rc = -1;
+    switch (kbits) {
+        case 2: rc = launch_matvec_kb<2>(frac, grid, 32 * nwarps, st, data, lut, gain_tab, d_row, e, ld_e, x_rot, y, d); break;
+        case 3: rc = launch_matvec_kb<3>(frac, grid, 32 * nwarps, st, data, lut, gain_tab, d_row, e, ld_e, x_rot, y, d); break;
+        case 4: rc = launch_matvec_kb<4>(frac, grid, 32 * nwarps, st, data, lut, gain_tab, d_row, e, ld_e, x_rot, y, d); break;
+        case 5: rc = launch_matvec_kb<5>(frac, grid, 32 * nwarps, st, data, lut, gain_tab, d_row, e, ld_e, x_rot, y, d); break;
+        case 6: rc = launch_matvec_kb<6>(frac, grid, 32 * nwarps, st, data, lut, gain_tab, d_row, e, ld_e, x_rot, y, d); break;
+        default: break;
+    }
+    if (rc != 0) return rc;
     return (int)cudaGetLastError();
 }
