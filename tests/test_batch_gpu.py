@@ -95,3 +95,21 @@ def test_bf16x6_pipeline_vs_reference_run(cuda_dev, monkeypatch):
         rel_ref = meta[name]["rel_loss"]
         assert eq_ref >= 0.90 and eq_32 >= 0.97, (name, eq_ref, eq_32)
         assert abs(a["rel_loss"] - rel_ref) <= 0.05 * abs(rel_ref), (name, a["rel_loss"], rel_ref)
+
+
+@pytest.mark.parametrize("M,K,spec", [(16, 256, "TCQ3X"), (16, 768, "TCQ25X"), (48, 512, "TCQ275X2")])
+def test_fast_mode_edge_shapes(M, K, spec, cuda_dev):
+    """The fast (bf16x6) pipeline on edge shapes — one 16-row tile group, a single 256-column block (no inter-block
+    update, empty right-operand set), two blocks — against the fp32 mode: packed and verified on the device, codes
+    mostly equal, rel_loss within 5 %."""
+    from ltq_research_b200.batch import quantize_matrices
+    from ltq_research_b200.formats import load_formats
+    W, H = synth(M, K, 71 + M + K)
+    job = [(W.to(cuda_dev), H.to(cuda_dev), spec)]
+    fm = load_formats([spec], cuda_dev)
+    a = quantize_matrices(job, gemm="bf16x6", ltq_formats=fm)[0]
+    b = quantize_matrices(job, gemm="fp32", ltq_formats=fm)[0]
+    eq = ((a["pack"]["idx"] == b["pack"]["idx"]) & (a["pack"]["gi"] == b["pack"]["gi"])).float().mean().item()
+    assert eq >= 0.9, eq
+    assert abs(a["rel_loss"] - b["rel_loss"]) <= 0.05 * b["rel_loss"], (a["rel_loss"], b["rel_loss"])
+    assert a["ltq"]["data"].numel() > 0
