@@ -125,10 +125,15 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
             uint32_t acc = 0;
             bool stop = false, done = false;
             for (int gl = NGRP - 1; gl >= 0 && !done; gl--) {
-                // the four steps of a group read the same lane column (bits 4..8 of the state at its last step): load
-                // its W4 words once, then walk the four steps in registers
+                // The four steps of a group read the same lane column L (bits 4..8 of the state at its last step): its
+                // W4 words are loaded once and the walk runs in the register frame of the forward pass.  At step j the
+                // state is register r of lane L in layout j + 1; its butterfly is r >> 1 and the decision bit h picks
+                // the predecessor register (r >> 1) | h << 4 in layout j (the forward step maps (ra, ra + 16) to
+                // (2 ra, 2 ra + 1)), so a step is a shift, a bit extract and an insert; the code bit is r & 1.
                 constexpr int W4C = MD == 0 ? 2 : (MD == 1 ? 5 : 9);
-                const uint32_t* Wg = B + gl * W4C * 32 + ((st >> 4) & 31);
+                const int L = (st >> 4) & 31;
+                int r = ((st >> 9) << 4) | (st & 15);  // the state in layout 4
+                const uint32_t* Wg = B + gl * W4C * 32 + L;
                 uint32_t w[W4C];
 #pragma unroll
                 for (int k = 0; k < W4C; k++) w[k] = Wg[32 * k];
@@ -136,19 +141,22 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
                     constexpr int j = decltype(JJ)::value;
                     if (done) return;
                     const int t = lo + 4 * gl + j;
-                    const int b9 = st >> 1;
-                    const int bi4 = bfly_of(j, b9);
+                    const int bi4 = r >> 1;
+                    // the full state in layout j + 1 (only where the walk stops)
+                    auto state = [&]() { return (r & ((2 << j) - 1)) | (L << (j + 1)) | ((r >> (j + 1)) << (j + 6)); };
                     if (PP && (j & 1)) {
-                        pcur = (w[j == 1 ? 2 : 4] >> ((bi4 << 1) | (st & 1))) & 1;
+                        pcur = (w[j == 1 ? 2 : 4] >> r) & 1;
                         spar[t] = spar[t - 1] = (uint8_t)pcur;
                     }
                     if (p.mid_st && t == p.mid_t - 1) {
+                        st = state();
                         p.mid_st[n] = st;
                         stop = done = true;
                         return;
                     }
-                    acc |= (uint32_t)(st & 1) << (t - lo);
+                    acc |= (uint32_t)(r & 1) << (t - lo);
                     if (t == 0) {
+                        st = state();
                         flag[3] = st;
                         done = true;
                         return;
@@ -160,7 +168,7 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
                         if constexpr (j & 1) h = (w[j == 1 ? 1 : 3] >> (pcur ? bi4 : 16 + bi4)) & 1;
                         else h = (w[0] >> ((j == 0) ? 16 + bi4 : bi4)) & 1;
                     } else {
-                        const int ro = (bi4 << 1) | (st & 1);
+                        const int ro = r;  // the output register of the state's butterfly
                         if constexpr (j == 3) {
                             cstar = (w[7] >> ro) & 1;
                             const int bb = (w[8] >> ro) & 1;
@@ -184,8 +192,9 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
                             h = (w[0] >> bi4) & 1;
                         }
                     }
-                    st = (h << 9) | b9;
+                    r = bi4 | (h << 4);
                 });
+                if (!done) st = L | (r << 5);  // the state before the group's first step, in layout 0
             }
             if (sub == 32) cbits[c] = acc;
             else reinterpret_cast<uint16_t*>(cbits)[c] = (uint16_t)acc;
