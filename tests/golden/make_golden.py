@@ -1,7 +1,7 @@
 """Generate golden fixtures from the reference Python implementation (lumen-inference/ltq-research).
 
-Runs only where the reference tree is importable (set LTQ_REF_ROOT, default /root/reference); the GPU box and the
-product never run it.  Fixtures written next to this file:
+Runs only where the reference tree is importable (LTQ_REF_ROOT names its root); the GPU box and the product never
+run it.  Fixtures written next to this file:
 
 * torch_viterbi_ub.npz  — the reference torch Viterbi `viterbi_ub` (src/tcq_proto.py:363-419) on seeded inputs, CPU.
 * ltq_format_tiles.npz  — `pack_tile` / `decode_tile` / `states_from_codes` / `labels_from_states`
