@@ -275,7 +275,11 @@ def aux_measurements(dev, fmts) -> dict:
     * rings: quantize_rings of a 2048 x 2560 bf16 table (20,480 rings, TCQ4X, rotation, three scale tries,
       tail-biting with a full first pass): values / s and the Viterbi's ACS rate (2 passes x 1024 x 4 slots x 3 tries
       per value);
-    * DP-profile table kernel: lut_subs_quant over 2^20 sub-blocks with an 8192 x 64 table: sub-blocks / s."""
+    * DP-profile table kernel: lut_subs_quant over 2^20 sub-blocks with an 8192 x 64 table: sub-blocks / s;
+    * the HBM-bound kernels of the path on a 16384 x 4096 matrix (268 MB in fp32, above the 126 MB L2), 10 back-to-back
+      calls each, algorithmic bytes / s against MEASURED_PEAKS hbm_gbs: FWHT-256 with the column scale (fp32 in and
+      out, 8 B / weight), the row-scale fit (4 B read), the .ltq pack of TCQ3X codes (idx + gi read, 3 B, tile bytes
+      written) and the on-device verify decode (tile bytes + the fp32 reference values read)."""
     from ltq_research_b200.batch import quantize_matrices
     from ltq_research_b200.ltq_file import matvec, matvec_slice_device, rotate_input
     from ltq_research_b200.rings import quantize_rings
@@ -309,6 +313,50 @@ def aux_measurements(dev, fmts) -> dict:
     lut = torch.sort(torch.randn(8192, 64, device=dev), dim=0).values
     ms = _event_ms(lambda: lut_subs_quant_cuda(xs, dh, lut, 8191 / 8.0, 4095.5))
     out["lut_subs"] = {"sub_blocks": S, "table": [8192, 64], "ms": ms, "msub_blocks_per_s": S / ms / 1e3}
+    out["hbm_kernels"] = hbm_kernels(dev, fmts["TCQ3X"])
+    return out
+
+
+def hbm_kernels(dev, f) -> dict:
+    """Bandwidth of the path's HBM-bound kernels (see aux_measurements)."""
+    from ltq_research_b200 import _lib
+    from ltq_research_b200.liqk_v2 import fwht_rows_scaled
+    from ltq_research_b200.ltq_file import decode_slice_device, pack_slice_device
+    R, K = 16384, 4096
+    n = R * K
+    peak = float(measured_peaks().get("hbm_gbs", 0.0)) or None
+    g = torch.Generator(device=dev).manual_seed(6)
+    W = torch.randn(R, K, device=dev, generator=g)
+    s = torch.rand(K, device=dev, generator=g) + 0.5
+    Wr = torch.empty_like(W)
+    d_row = torch.empty(R, device=dev)
+    e = torch.empty((R, K // 256), dtype=torch.int8, device=dev)
+    d_rb = torch.empty((R, K // 256), device=dev)
+    idx = torch.randint(0, f.n_labels * f.U, (R, K), device=dev, generator=g, dtype=torch.int16)
+    gi = torch.randint(0, 1 << f.h, (R, K), device=dev, generator=g, dtype=torch.uint8)
+    data = pack_slice_device(idx, gi, f)
+    buf = torch.zeros(((data.numel() + 63) // 64) * 64, dtype=torch.uint8, device=dev)
+    buf[: data.numel()] = data
+    ref = decode_slice_device(buf, R, K, f)
+    bad = torch.zeros(1, dtype=torch.int64, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    L = _lib.lib()
+    tb = data.numel()
+    reps = 10
+    kernels = {
+        "fwht256": (lambda: fwht_rows_scaled(W, s, mode=1, out=Wr), 8 * n),
+        "scale_fit": (lambda: L.ltq_scale_fit(W.data_ptr(), K, R, K, 1.1, 0.25, 5, None, d_row.data_ptr(),
+                                              e.data_ptr(), d_rb.data_ptr(), st), 4 * n),
+        "pack_slice": (lambda: pack_slice_device(idx, gi, f, out=buf), 3 * n + tb),
+        "decode_verify": (lambda: decode_slice_device(buf, R, K, f, ref=ref, mismatches=bad), tb + 4 * n),
+    }
+    out = {"shape": [R, K], "format": f.name, "peak_gbs": peak}
+    for name, (fn, nbytes) in kernels.items():
+        ms = _event_ms(lambda: [fn() for _ in range(reps)]) / reps
+        gbs = nbytes / ms / 1e6
+        out[name] = {"ms": ms, "algorithmic_gb": nbytes / 1e9, "gb_per_s": gbs, "frac": gbs / peak if peak else None}
+    torch.cuda.synchronize()
+    assert int(bad) == 0, "hbm_kernels: the verify decode disagrees with its own reference"
     return out
 
 
