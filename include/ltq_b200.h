@@ -133,6 +133,16 @@ int ltq_bf16x6_split_batched(const float* x, long long ld, long long xbs, int ro
  * substitution in fp32.  The blocks above the leaves are merged by GEMMs on the caller's side.
  */
 int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* X, long long ldX, void* stream);
+/*
+ * Blocked Cholesky of the damped Hessian (src/liqk_v2.py:1078 torch.linalg.cholesky of flip(H_reg); :1163 the refit
+ * system's solve), the diagonal step: the 256 x 256 block at (c0, c0) of A (row-major fp32, row stride ld, lower
+ * triangle read, trailing updates of the earlier panels already applied) is factored in place (L, zeros above its
+ * diagonal) and its factor inverted; xt6 [1536][256] (bf16) receives the six-slot right operand of L_blk^-T for the
+ * panel product below the block, and X (optional, row stride ldx) the inverse itself at (c0, c0).  The first pivot
+ * that is not positive sets *info = c0 + j + 1 when *info is 0 (LAPACK's convention).  The panel and trailing updates
+ * are tensor-core GEMMs on the caller's side.
+ */
+int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt6, float* X, long long ldx, int* info, void* stream);
 size_t ltq_ldlq_bcat_elems(int K);
 int ltq_ldlq_bcat(const float* U, long long ldU, int K, uint16_t* bcat, void* stream);
 int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* G, long long ldG,

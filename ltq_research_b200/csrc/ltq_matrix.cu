@@ -347,6 +347,181 @@ __global__ void __launch_bounds__(128) trtri256_lower_kernel(const float* __rest
     for (int i = 0; i < 256; i++) Xb[(long long)i * ldX + j] = i < i0 ? 0.f : xs[(i - i0) * 128 + t];
 }
 
+// Cholesky of the 256 x 256 diagonal block at (c0, c0) of A (row-major, row stride ld; lower triangle read; the
+// trailing updates of the earlier panels already applied) and the inverse of its factor, the diagonal step of
+// hessian.cholesky_lower.  One CTA holds the block in registers: 528 threads each own one 8 x 8 tile (bi >= bk) of the
+// lower triangle, ordered by tile column, so that the tiles still active near the end of the sweep fill whole warps.
+//   phase 1, the factorization in LDL^T form: at pivot j the owners of tile column j/8 broadcast column j through
+//     shared memory (double-buffered, one barrier per pivot) and every tile right of it takes
+//     a_ik -= (a_ij / a_jj) a_kj — 64 fma a thread, the mask on the tile column holding j keeps columns <= j; at the
+//     end L_ik = a_ik / sqrt(d_k) goes to A and L~_ik = a_ik / d_k (unit lower) to shared memory, column-major with
+//     every column starting at its tile row (32-byte aligned: 132 KB);
+//   phase 2, Y = L~^-1 by Gauss-Jordan on the identity: at pivot j the owners of tile row j/8 broadcast row j of Y and
+//     every tile below it and left of it takes y_ik -= L~_ij y_jk (rows i > j); then X = L^-1 = D^-1/2 Y;
+//   outputs: L in A's block (zeros above the diagonal); xt6 [1536][256] (bf16) = the six-slot right operand
+//     [x0; x1; x0; x2; x1; x0] of X^T (the panel below the block is A_21 X^T; every element written); X itself in the
+//     block at (c0, c0) of Xo (row stride ldx) when Xo is given; *info = c0 + j + 1 for the first pivot that is not
+//     positive (or NaN) when *info was 0 (LAPACK's convention).
+constexpr int LT_FLOATS = 33792;  // sum over columns of 256 - 8 * (j / 8)
+__device__ __forceinline__ int lt_col(int j)
+{
+    const int jb = j >> 3, c = j & 7;
+    return 8 * (256 * jb - 4 * jb * (jb - 1)) + c * (256 - 8 * jb);
+}
+
+__global__ void __launch_bounds__(544, 1) chol256_tiled_kernel(float* __restrict__ A, long long ld, int c0,
+                                                               uint16_t* __restrict__ xt6, float* __restrict__ Xo,
+                                                               long long ldx, int* __restrict__ info)
+{
+    extern __shared__ __align__(16) float smem[];
+    float* lt = smem;                 // L~, column-major from each column's tile row
+    float* cb = smem + LT_FLOATS;     // 2 x 256 broadcast buffers
+    float* sd = cb + 512;             // the pivots d_j
+    const int tid = threadIdx.x;
+    int bk = 0, rem = tid;
+    while (bk < 32 && rem >= 32 - bk) { rem -= 32 - bk; bk++; }
+    const bool own = bk < 32;
+    const int bi = bk + rem;
+    float* Ab = A + (long long)c0 * (ld + 1);
+    float a[8][8];
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+        if (own) {
+            const float* src = Ab + (long long)(8 * bi + r) * ld + 8 * bk;
+            v0 = *reinterpret_cast<const float4*>(src);
+            v1 = *reinterpret_cast<const float4*>(src + 4);
+        }
+        a[r][0] = v0.x; a[r][1] = v0.y; a[r][2] = v0.z; a[r][3] = v0.w;
+        a[r][4] = v1.x; a[r][5] = v1.y; a[r][6] = v1.z; a[r][7] = v1.w;
+    }
+    for (int jb = 0; jb < 32; jb++) {
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const int j = 8 * jb + c;
+            float* buf = cb + (c & 1) * 256;
+            if (own && bk == jb) {
+                *reinterpret_cast<float4*>(buf + 8 * bi) = make_float4(a[0][c], a[1][c], a[2][c], a[3][c]);
+                *reinterpret_cast<float4*>(buf + 8 * bi + 4) = make_float4(a[4][c], a[5][c], a[6][c], a[7][c]);
+                if (bi == jb) {
+                    sd[j] = a[c][c];
+                    if (!(a[c][c] > 0.f)) atomicCAS(info, 0, c0 + j + 1);
+                }
+            }
+            __syncthreads();
+            if (own && bk >= jb) {
+                const float inv = __frcp_rn(buf[j]);
+                const float4 k0 = *reinterpret_cast<const float4*>(buf + 8 * bk);
+                const float4 k1 = *reinterpret_cast<const float4*>(buf + 8 * bk + 4);
+                float ck[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+                if (bk == jb) {
+#pragma unroll
+                    for (int cc = 0; cc <= c; cc++) ck[cc] = 0.f;
+                }
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    const float t = buf[8 * bi + r] * inv;
+#pragma unroll
+                    for (int cc = 0; cc < 8; cc++) a[r][cc] = __fmaf_rn(-t, ck[cc], a[r][cc]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (own) {
+#pragma unroll
+        for (int cc = 0; cc < 8; cc++) {
+            const float rd = __frcp_rn(sd[8 * bk + cc]);
+            float* col = lt + lt_col(8 * bk + cc) + 8 * (bi - bk);
+            *reinterpret_cast<float4*>(col) = make_float4(a[0][cc] * rd, a[1][cc] * rd, a[2][cc] * rd, a[3][cc] * rd);
+            *reinterpret_cast<float4*>(col + 4) = make_float4(a[4][cc] * rd, a[5][cc] * rd, a[6][cc] * rd, a[7][cc] * rd);
+        }
+#pragma unroll
+        for (int cc = 0; cc < 8; cc++) {
+            const float dk = sd[8 * bk + cc];
+            const float rs = __frsqrt_rn(dk);
+#pragma unroll
+            for (int r = 0; r < 8; r++)
+                a[r][cc] = (bi != bk || r > cc) ? a[r][cc] * rs : (r == cc ? __fsqrt_rn(dk) : 0.f);
+        }
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+            float* dst = Ab + (long long)(8 * bi + r) * ld + 8 * bk;
+            *reinterpret_cast<float4*>(dst) = make_float4(a[r][0], a[r][1], a[r][2], a[r][3]);
+            *reinterpret_cast<float4*>(dst + 4) = make_float4(a[r][4], a[r][5], a[r][6], a[r][7]);
+        }
+    }
+    // phase 2: Y = L~^-1, in the registers of the factor's tile
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+#pragma unroll
+        for (int cc = 0; cc < 8; cc++) a[r][cc] = (bi == bk && r == cc) ? 1.f : 0.f;
+    __syncthreads();
+    for (int jb = 0; jb < 32; jb++) {
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const int j = 8 * jb + c;
+            float* buf = cb + (c & 1) * 256;
+            if (own && bi == jb) {
+                *reinterpret_cast<float4*>(buf + 8 * bk) = make_float4(a[c][0], a[c][1], a[c][2], a[c][3]);
+                *reinterpret_cast<float4*>(buf + 8 * bk + 4) = make_float4(a[c][4], a[c][5], a[c][6], a[c][7]);
+            }
+            __syncthreads();
+            if (own && bk <= jb && bi >= jb) {
+                const float* col = lt + lt_col(j) + 8 * (bi - jb);
+                const float4 y0 = *reinterpret_cast<const float4*>(buf + 8 * bk);
+                const float4 y1 = *reinterpret_cast<const float4*>(buf + 8 * bk + 4);
+                const float yk[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    const float l = (bi == jb && r <= c) ? 0.f : col[r];
+#pragma unroll
+                    for (int cc = 0; cc < 8; cc++) a[r][cc] = __fmaf_rn(-l, yk[cc], a[r][cc]);
+                }
+            }
+        }
+    }
+    if (!own) return;
+    // X = D^-1/2 Y; X^T's six-slot operand: row k = 8 bk + cc, columns 8 bi .. 8 bi + 7 (and zeros at the mirror)
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+        const float rs = __frsqrt_rn(sd[8 * bi + r]);
+#pragma unroll
+        for (int cc = 0; cc < 8; cc++) a[r][cc] *= rs;
+    }
+    if (Xo) {
+        float* Xb = Xo + (long long)c0 * (ldx + 1);
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+            float* dst = Xb + (long long)(8 * bi + r) * ldx + 8 * bk;
+            *reinterpret_cast<float4*>(dst) = make_float4(a[r][0], a[r][1], a[r][2], a[r][3]);
+            *reinterpret_cast<float4*>(dst + 4) = make_float4(a[r][4], a[r][5], a[r][6], a[r][7]);
+        }
+    }
+#pragma unroll
+    for (int cc = 0; cc < 8; cc++) {
+        uint32_t w[3][4];  // the three bf16 parts of column cc's 8 values, two to a word
+#pragma unroll
+        for (int r = 0; r < 8; r += 2) {
+            uint16_t p0, p1, p2, q0, q1, q2;
+            split3_bf16(a[r][cc], p0, p1, p2);
+            split3_bf16(a[r + 1][cc], q0, q1, q2);
+            w[0][r / 2] = p0 | (uint32_t)q0 << 16;
+            w[1][r / 2] = p1 | (uint32_t)q1 << 16;
+            w[2][r / 2] = p2 | (uint32_t)q2 << 16;
+        }
+        constexpr int slot_part[6] = {0, 1, 0, 2, 1, 0};
+#pragma unroll
+        for (int sl = 0; sl < 6; sl++) {
+            const int q = slot_part[sl];
+            *reinterpret_cast<uint4*>(xt6 + (long long)(256 * sl + 8 * bk + cc) * 256 + 8 * bi) =
+                make_uint4(w[q][0], w[q][1], w[q][2], w[q][3]);
+            if (bi != bk)
+                *reinterpret_cast<uint4*>(xt6 + (long long)(256 * sl + 8 * bi + cc) * 256 + 8 * bk) = make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+
 }  // namespace
 
 extern "C" int ltq_fwht256(const void* in, int in_bf16, long long ld_in, float* out, long long ld_out, const float* scale,
@@ -463,5 +638,23 @@ extern "C" int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* 
         attr_done[dev].store(1, std::memory_order_release);
     }
     trtri256_lower_kernel<<<dim3((unsigned)nb, 2), 128, smem, (cudaStream_t)stream>>>(L, ldL, X, ldX);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt6, float* X, long long ldx, int* info,
+                                void* stream)
+{
+    if (!A || !xt6 || !info || c0 < 0 || ld < c0 + 256LL || (X && ldx < c0 + 256LL)) return -1;
+    if (c0 % 4 || ld % 4 || (X && ldx % 4) || ((uintptr_t)A & 15) || ((uintptr_t)xt6 & 15) || ((uintptr_t)X & 15)) return -1;
+    static std::atomic<int> attr_done[64];
+    constexpr int smem = (LT_FLOATS + 768) * 4;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
+        const cudaError_t e = cudaFuncSetAttribute(chol256_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int)e;
+        attr_done[dev].store(1, std::memory_order_release);
+    }
+    chol256_tiled_kernel<<<1, 544, smem, (cudaStream_t)stream>>>(A, ld, c0, xt6, X, ldx, info);
     return (int)cudaGetLastError();
 }

@@ -11,6 +11,13 @@
   (ltq_trtri256_lower) and adjacent inverted blocks are merged level by level, X21 = -C^-1 (L21 A^-1) for
   L = [[A, 0], [L21, C]], with the two products of every level as one batched tensor-core GEMM each in the six-product
   bf16 form (fp32-accurate, the error bound of an fp32 product).  log2(K / 256) levels, about seven launches each.
+* cholesky_lower — the factorization itself (the reference's torch.linalg.cholesky of flip(H_reg), :1078, and the
+  refit system's solve, :1163), right-looking in 256-column panels: the diagonal block is factored and its factor
+  inverted by one single-CTA kernel (ltq_chol256_diag, which also emits the six-slot operand of the block inverse), the
+  panel below it is L21 = A21 L11^-T and the trailing matrix A22 -= L21 L21^T, both tensor-core GEMMs in the six-product
+  bf16 form.  The trailing product covers about three quarters of the square instead of all of it (the strictly upper
+  part is never read).  With inverse=True the diagonal block inverses seed tri_inv_lower, so the factor and its inverse
+  cost one pass of leaf kernels.
 """
 from __future__ import annotations
 
@@ -70,17 +77,26 @@ def _split6(x: torch.Tensor, xbs: int, rows: int, cols: int, batch: int, order: 
     return out
 
 
-def tri_inv_lower(L: torch.Tensor) -> torch.Tensor:
+def _square_fp32_cuda(A: torch.Tensor, what: str):
+    if A.dim() != 2 or A.shape[0] != A.shape[1] or A.shape[0] % QK or A.dtype != torch.float32 or not A.is_cuda:
+        raise ValueError(f"{what}: a square fp32 CUDA matrix with a multiple of 256 rows is required")
+
+
+def tri_inv_lower(L: torch.Tensor, X: Optional[torch.Tensor] = None) -> torch.Tensor:
     """L^-1 (row-major fp32 [K, K], upper part exactly 0) of a lower-triangular fp32 L with K a multiple of 256, any
-    layout, on the current stream, without host synchronisation."""
-    if L.dim() != 2 or L.shape[0] != L.shape[1] or L.shape[0] % QK or L.dtype != torch.float32 or not L.is_cuda:
-        raise ValueError("tri_inv_lower: a square fp32 CUDA matrix with a multiple of 256 rows is required")
+    layout, on the current stream, without host synchronisation.  X: a row-major [K, K] whose 256 x 256 diagonal
+    blocks already hold the inverses of L's diagonal blocks and whose other blocks are 0 (cholesky_lower leaves it so);
+    the merges then complete it in place."""
+    _square_fp32_cuda(L, "tri_inv_lower")
     K = L.shape[0]
     Lr = L if L.stride(1) == 1 and L.stride(0) == K else L.contiguous()
-    X = torch.zeros_like(Lr)
     st = _stream(L.device)
     nb = K // QK
-    _check(_lib.lib().ltq_trtri256_lower(ptr(Lr), K, nb, ptr(X), K, st), "ltq_trtri256_lower")
+    if X is None:
+        X = torch.zeros_like(Lr)
+        _check(_lib.lib().ltq_trtri256_lower(ptr(Lr), K, nb, ptr(X), K, st), "ltq_trtri256_lower")
+    elif X.shape != Lr.shape or X.stride() != (K, 1) or X.dtype != torch.float32:
+        raise ValueError("tri_inv_lower: X must be a row-major fp32 matrix of L's shape")
     blocks: List[Tuple[int, int]] = [(QK * i, QK) for i in range(nb)]  # inverted diagonal blocks (start, size)
     while len(blocks) > 1:
         pairs = [(blocks[2 * i], blocks[2 * i + 1]) for i in range(len(blocks) // 2)]
@@ -116,3 +132,48 @@ def _merge(Lr: torch.Tensor, X: torch.Tensor, a0: int, ba: int, bc: int, batch: 
     left = _split6(XC, bs, bc, bc, batch, 0, 0, True, K)
     right = _split6(T, T.stride(0), bc, ba, batch, 1, 1, False, T.stride(1))
     X21.copy_(torch.bmm(left, right, out_dtype=torch.float32))
+
+
+def cholesky_lower(A: torch.Tensor, inverse: bool = False, overwrite: bool = False
+                   ) -> Tuple[torch.Tensor, torch.Tensor, Optional[torch.Tensor]]:
+    """(L, info, X): the lower Cholesky factor of the symmetric positive definite fp32 A (lower triangle read; K a
+    multiple of 256), row-major with exact zeros above the diagonal; info an int32 device scalar, 0 or the order of the
+    first leading minor that is not positive (torch.linalg.cholesky_ex's convention; the factor is then not usable);
+    X = L^-1 (as tri_inv_lower) with inverse=True, else None.  overwrite=True factors a contiguous A in place.  On the
+    current stream, without host synchronisation."""
+    _square_fp32_cuda(A, "cholesky_lower")
+    K = A.shape[0]
+    dev = A.device
+    if not (overwrite and A.is_contiguous()):
+        A = A.contiguous().clone() if A.is_contiguous() else A.contiguous()
+    info = torch.zeros(1, dtype=torch.int32, device=dev)
+    X = torch.zeros_like(A) if inverse else None
+    xt6 = torch.empty((6 * QK, QK), dtype=torch.bfloat16, device=dev)
+    st = _stream(dev)
+    L_ = _lib.lib()
+    nb = K // QK
+    for p in range(nb):
+        c0, c1 = QK * p, QK * (p + 1)
+        _check(L_.ltq_chol256_diag(ptr(A), K, c0, ptr(xt6), ptr(X) if X is not None else None, K, ptr(info), st),
+               "ltq_chol256_diag")
+        if c1 == K:
+            break
+        m = K - c1
+        A21 = A[c1:, c0:c1]
+        L21 = torch.mm(_split6(A21, 0, m, QK, 1, 0, 0, False, K)[0], xt6, out_dtype=torch.float32)
+        A21.copy_(L21)
+        left = _split6(L21, 0, m, QK, 1, 0, 0, False, QK)[0]     # [m, 1536], slots [x0 x0 x1 x0 x1 x2]
+        right = _split6(L21, 0, m, QK, 1, 1, 0, False, QK)[0].T  # [1536, m], slots [x0 x1 x0 x2 x1 x0] of L21^T
+        A22 = A[c1:, c1:]
+        h = QK * (m // QK // 2) if m >= 4 * QK else m
+        # A22 -= L21 L21^T on the lower triangle's cover: the leading h x h square, then the rows below it in full
+        C = A22[:h, :h]
+        torch.addmm(C, left[:h], right[:, :h], beta=1, alpha=-1, out_dtype=torch.float32, out=C)
+        if h < m:
+            C = A22[h:]
+            torch.addmm(C, left[h:], right, beta=1, alpha=-1, out_dtype=torch.float32, out=C)
+        del left, right, L21
+    A.tril_()
+    if inverse:
+        tri_inv_lower(A, X)
+    return A, info.view(()), X

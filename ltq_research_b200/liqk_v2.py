@@ -20,7 +20,7 @@ import torch
 
 from . import _lib
 from ._lib import ptr
-from .hessian import tri_inv_lower
+from .hessian import cholesky_lower
 from .formats import LIQK_V2_SPECS, QK_K, SUBBLOCK_SIZE, TCQ_CONFIG  # noqa: F401
 from .tcq_proto import make_gains
 
@@ -559,12 +559,12 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     H_reg = H_rot.float().clone()
     diag_mean = H_reg.diagonal().mean().clamp(min=1e-8)
     H_reg.diagonal().add_(damp * diag_mean)
-    L_flip, chol_info = torch.linalg.cholesky_ex(H_reg.flip(0, 1))
-    del H_rot, H_reg
-    if gemm == "fp32":  # the reference's triangular solve L X = I (src/liqk_v2.py:1081)
+    if gemm == "fp32":  # the reference's factorization and triangular solve L X = I (src/liqk_v2.py:1078-1081)
+        L_flip, chol_info = torch.linalg.cholesky_ex(H_reg.flip(0, 1))
         U = torch.linalg.solve_triangular(L_flip, torch.eye(K, dtype=L_flip.dtype, device=L_flip.device), upper=False)
-    else:  # leaf inverses + blockwise merges on the tensor cores (hessian.tri_inv_lower)
-        U = tri_inv_lower(L_flip)
+    else:  # blocked factorization whose leaf kernels also invert the diagonal blocks, then the tensor-core merges
+        L_flip, chol_info, U = cholesky_lower(H_reg.flip(0, 1), inverse=True, overwrite=True)
+    del H_rot, H_reg
     U = U.flip(0, 1)
     diag_w = 1.0 / (torch.diagonal(U) ** 2).clamp(min=1e-12)
     if gemm == "fp32":  # the reference's inverses of U's diagonal blocks (src/liqk_v2.py:1086-1088)
@@ -655,7 +655,7 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     if gemm == "fp32":
         sol, solve_info = torch.linalg.solve_ex(A_in, b_in)
     else:
-        Lc, solve_info = torch.linalg.cholesky_ex(A_in)
+        Lc, solve_info, _ = cholesky_lower(A_in, overwrite=True)
         sol = torch.cholesky_solve(b_in.unsqueeze(1), Lc).squeeze(1)
         del Lc
     suh_cand = sol.to(torch.float16).to(torch.float32)

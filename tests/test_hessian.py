@@ -89,3 +89,84 @@ def test_tri_inv_lower_column_major_input(cuda_dev):
     Lt = L.T.contiguous().T  # column-major copy
     assert Lt.stride() != L.contiguous().stride()
     assert torch.equal(tri_inv_lower(Lt), tri_inv_lower(L.contiguous()))
+
+
+def _damped_gram(K, seed, dev, damp=0.2):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    X = torch.randn(max(2 * K, 1024), K, device=dev, generator=g) * torch.exp(torch.randn(1, K, device=dev, generator=g))
+    H = X.T @ X / X.shape[0]
+    H.diagonal().add_(damp * H.diagonal().mean())
+    return H
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("K", [256, 768, 1280, 3072])
+def test_cholesky_lower_accuracy(K, cuda_dev):
+    """Blocked factorization (leaf kernel + tensor-core panel and trailing products) against the fp64 factor of the
+    same matrix: exact zeros above the diagonal; backward error |A - L L^T| / |A| and forward error of L within 4x
+    those of torch.linalg.cholesky_ex's own fp32 factor (or 16 u / 1e-5 when the library's are smaller still); info 0;
+    the inverse within tri_inv_lower's bounds; the input untouched unless overwrite is asked for."""
+    from ltq_research_b200.hessian import cholesky_lower
+    A = _damped_gram(K, K + 1, cuda_dev).flip(0, 1).contiguous()
+    A0 = A.clone()
+    L, info, X = cholesky_lower(A, inverse=True)
+    torch.cuda.synchronize()
+    assert int(info) == 0 and torch.equal(A, A0)
+    assert L.is_contiguous() and torch.equal(torch.tril(L), L) and torch.equal(torch.tril(X), X)
+    Ad, Ld = A.double(), L.double()
+    exact = torch.linalg.cholesky(Ad)
+    Lc = torch.linalg.cholesky_ex(A)[0].double()
+    back = ((Ad - Ld @ Ld.T).norm() / Ad.norm()).item()
+    back_lib = ((Ad - Lc @ Lc.T).norm() / Ad.norm()).item()
+    fwd = ((Ld - exact).norm() / exact.norm()).item()
+    fwd_lib = ((Lc - exact).norm() / exact.norm()).item()
+    print(f"K={K}: backward {back:.3g} (library {back_lib:.3g}), forward {fwd:.3g} (library {fwd_lib:.3g})")
+    assert back <= max(4 * back_lib, 16 * 2.0 ** -24), (back, back_lib)
+    assert fwd <= max(4 * fwd_lib, 1e-5), (fwd, fwd_lib)
+    I = torch.eye(K, device=cuda_dev, dtype=torch.float64)
+    Xd = X.double()
+    assert ((Ld @ Xd - I).norm() / (Ld.norm() * Xd.norm())).item() <= 4 * 2.0 ** -24
+    inv = torch.linalg.solve_triangular(exact, I, upper=False)
+    assert ((Xd - inv).norm() / inv.norm()).item() < 1e-5
+    L2, info2, X2 = cholesky_lower(A0, overwrite=True)
+    assert X2 is None and L2.data_ptr() == A0.data_ptr() and torch.equal(L2, L) and int(info2) == 0
+
+
+@pytest.mark.gpu
+def test_cholesky_lower_solve_refit_system(cuda_dev):
+    """The refit system of the fast mode: A = (U^T U) o H + 1e-3 mean(diag) I, solved through the blocked factor and
+    torch.cholesky_solve, against fp64."""
+    from ltq_research_b200.hessian import cholesky_lower
+    K = 1024
+    g = torch.Generator(device=cuda_dev).manual_seed(3)
+    U = torch.randn(512, K, device=cuda_dev, generator=g)
+    H = _damped_gram(K, 4, cuda_dev)
+    A = (U.T @ U) * H
+    A.diagonal().add_(1e-3 * A.diagonal().mean())
+    b = torch.randn(K, device=cuda_dev, generator=g)
+    L, info, _ = cholesky_lower(A)
+    x = torch.cholesky_solve(b.unsqueeze(1), L).squeeze(1)
+    want = torch.linalg.solve(A.double(), b.double())
+    assert int(info) == 0
+    assert ((x.double() - want).norm() / want.norm()).item() < 1e-4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("j", [0, 37, 255, 256, 700])
+def test_cholesky_lower_info_first_bad_minor(j, cuda_dev):
+    """A = T D T^T with T unit lower (small entries) and D = I except D_jj = -1: the leading minor of order m is
+    prod_{i < m} D_i, so the first that is not positive has order j + 1 — the blocked factorization reports exactly
+    that.  torch.linalg.cholesky_ex (cuSOLVER) agrees except at the last column of a 256-column panel, where it was
+    seen to report j + 2."""
+    from ltq_research_b200.hessian import cholesky_lower
+    K = 768
+    g = torch.Generator(device=cuda_dev).manual_seed(j)
+    T = torch.tril(torch.randn(K, K, device=cuda_dev, dtype=torch.float64, generator=g) * 0.02, -1)
+    T.diagonal().fill_(1.0)
+    D = torch.ones(K, device=cuda_dev, dtype=torch.float64)
+    D[j] = -1.0
+    A = ((T * D) @ T.T).float()
+    _, info, _ = cholesky_lower(A)
+    _, info_lib = torch.linalg.cholesky_ex(A)
+    assert int(info) == j + 1
+    assert int(info_lib) == j + 1 or (j % 256 == 255 and int(info_lib) == j + 2)
