@@ -160,10 +160,10 @@ def cholesky_lower(A: torch.Tensor, inverse: bool = False, overwrite: bool = Fal
             break
         m = K - c1
         A21 = A[c1:, c0:c1]
-        L21 = torch.mm(_split6(A21, 0, m, QK, 1, 0, 0, False, K)[0], xt6, out_dtype=torch.float32)
-        A21.copy_(L21)
-        left = _split6(L21, 0, m, QK, 1, 0, 0, False, QK)[0]     # [m, 1536], slots [x0 x0 x1 x0 x1 x2]
-        right = _split6(L21, 0, m, QK, 1, 1, 0, False, QK)[0].T  # [1536, m], slots [x0 x1 x0 x2 x1 x0] of L21^T
+        # L21 = A21 L11^-T written over A21 (beta = 0: the old values are not read)
+        torch.addmm(A21, _split6(A21, 0, m, QK, 1, 0, 0, False, K)[0], xt6, beta=0, out_dtype=torch.float32, out=A21)
+        left = _split6(A21, 0, m, QK, 1, 0, 0, False, K)[0]     # [m, 1536], slots [x0 x0 x1 x0 x1 x2]
+        right = _split6(A21, 0, m, QK, 1, 1, 0, False, K)[0].T  # [1536, m], slots [x0 x1 x0 x2 x1 x0] of L21^T
         A22 = A[c1:, c1:]
         h = QK * (m // QK // 2) if m >= 4 * QK else m
         # A22 -= L21 L21^T on the lower triangle's cover: the leading h x h square, then the rows below it in full
@@ -172,7 +172,7 @@ def cholesky_lower(A: torch.Tensor, inverse: bool = False, overwrite: bool = Fal
         if h < m:
             C = A22[h:]
             torch.addmm(C, left[h:], right, beta=1, alpha=-1, out_dtype=torch.float32, out=C)
-        del left, right, L21
+        del left, right
     A.tril_()
     if inverse:
         tri_inv_lower(A, X)
