@@ -107,6 +107,22 @@ def _right6(b: torch.Tensor) -> torch.Tensor:
     return o if o is not None else _bcat(_split3(b))
 
 
+def _gram_lower6(x: torch.Tensor) -> torch.Tensor:
+    """x^T x ([K, K]) of an fp32 [M, K] in the six-product form, for a consumer that reads the lower triangle only:
+    the leading half square and the rows below it are computed (three quarters of the product), the 256-column blocks
+    above the diagonal blocks of the rest are left uninitialised."""
+    K = x.shape[1]
+    left, right = _left6(x.T), _right6(x)  # [K, 6 M], [6 M, K]
+    h = QK_K * (K // QK_K // 2) if K >= 4 * QK_K else K
+    C = torch.empty((K, K), dtype=torch.float32, device=x.device)
+    top = C[:h, :h]
+    torch.addmm(top, left[:h], right[:, :h], beta=0, out_dtype=torch.float32, out=top)
+    if h < K:
+        bottom = C[h:]
+        torch.addmm(bottom, left[h:], right, beta=0, out_dtype=torch.float32, out=bottom)
+    return C
+
+
 def _mm(a: torch.Tensor, b: torch.Tensor, gemm: str) -> torch.Tensor:
     """a @ b for fp32 [M, K] x [K, N] in the given mode."""
     if gemm == "fp32":
@@ -645,7 +661,12 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     else:
         rw = torch.ones((M,), dtype=torch.float32, device=W.device)
         U_w = U_scaled
-    A_in = (U_w.T @ U_scaled if gemm == "fp32" else _mm(U_w.T, U_scaled, gemm)) * H_f32
+    if gemm == "fp32":
+        A_in = (U_w.T @ U_scaled) * H_f32
+    elif row_weights is None:  # U_w is U_scaled: a Gram matrix, needed on its lower triangle only (Cholesky below)
+        A_in = _gram_lower6(U_scaled) * H_f32
+    else:
+        A_in = _mm(U_w.T, U_scaled, gemm) * H_f32
     b_in = (U_w * HW).sum(dim=0)
     A_in.diagonal().add_(1e-3 * A_in.diagonal().mean().clamp(min=1e-12))
     # the reference solves, and keeps the refit when the solve succeeds and lowers the loss (src/liqk_v2.py:1161-1180).
@@ -680,8 +701,17 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
         suh_p = suh.to(torch.float16)
         scale = d_row_p.float().unsqueeze(1) * torch.exp2(0.25 * pm["e"].float())
         Wq_rot = (scale.unsqueeze(2) * pm["G"].view(M, nblocks, QK_K)).view(M, K)
-        W_hat_eff = fwht_inplace(Wq_rot, block_size=QK_K) * suh_p.float().unsqueeze(0)
-        HQ = times_h(W_hat_eff)
+        W_pk = fwht_inplace(Wq_rot, block_size=QK_K) * suh_p.float().unsqueeze(0)
+        if gemm == "fp32":
+            HQ = times_h(W_pk)
+        else:
+            # the packed reconstruction differs from W_hat_eff only by the fp16 roundings of the row scale and suh:
+            # HQ takes the product of that small change, in the three-product bf16 form (the first three slots of
+            # each six-slot operand: relative error ~2^-16 of the change, far below fp32 rounding of HQ itself)
+            dl = _left6(W_pk - W_hat_eff)
+            HQ = torch.addmm(HQ, dl[:, :3 * K], Hb[:3 * K], out_dtype=torch.float32)
+            del dl
+        W_hat_eff = W_pk
         pack = {"row_slices": row_slices, "idx": pm["idx"], "gi": pm["gi"], "G": pm["G"], "d_row": d_row_p,
                 "e": pm["e"], "suh": suh_p}
     del times_h
