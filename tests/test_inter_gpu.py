@@ -130,3 +130,23 @@ def test_block_inverses_from_the_cholesky_factor(cuda_dev):
     assert ((got - ref).norm() / ref.norm()).item() < 1e-5
     assert (torch.bmm(Ub, got) - torch.eye(256, device=cuda_dev)).abs().max().item() < 1e-4
     assert torch.equal(torch.triu(got), got)
+
+
+@pytest.mark.parametrize("K", [512, 1024, 1280])
+def test_gram_lower6_lower_triangle(K, cuda_dev):
+    """_gram_lower6(x) (the refit's Gram matrix, computed on the lower triangle's cover only) against fp64 x^T x: every
+    element on or below the diagonal within the fp32 error bound of a dot product of length M, and every 256 x 256
+    diagonal block computed in full (the blockwise Cholesky reads whole diagonal blocks)."""
+    from ltq_research_b200.liqk_v2 import _gram_lower6
+    g = torch.Generator().manual_seed(K)
+    M = 640
+    x = _wide((M, K), g, cuda_dev)
+    C = _gram_lower6(x)
+    torch.cuda.synchronize()
+    xd = x.double()
+    want = xd.T @ xd
+    bound = _gamma(M) * (xd.abs().T @ xd.abs()) + 2 * U_RND * want.abs()
+    low = torch.tril(torch.ones(K, K, dtype=torch.bool, device=cuda_dev))
+    for b in range(K // 256):
+        low[256 * b:256 * (b + 1), 256 * b:256 * (b + 1)] = True
+    assert ((C.double() - want).abs() <= 2 * bound)[low].all()
