@@ -504,8 +504,13 @@ def main():
     if not args.no_e2e:
         host = [(W.cpu().pin_memory(), H.cpu().pin_memory(), sp) for W, H, sp in timed]
         h2d = sum(W.numel() * W.element_size() + H.numel() * H.element_size() for W, H, _ in host)
-        # one untimed pass through the same path first (pinned host output buffers, host-to-device staging)
-        quantize_matrices(host, n_streams=args.streams, ltq_formats=fmts, pack=False, to_host=dist is None)
+        # one untimed pass through the same path first (pinned host output buffers, host-to-device staging; with
+        # several GPUs also the gather, whose first call sets up NCCL's point-to-point connections)
+        warm_h = quantize_matrices(host, n_streams=args.streams, ltq_formats=fmts, pack=False, to_host=dist is None)
+        if dist is not None:
+            from ltq_research_b200.shard import gather_ltq
+            gather_ltq({rank * len(warm_h) + i: r["ltq"] for i, r in enumerate(warm_h)}, dst=0)
+        del warm_h
         barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
