@@ -57,11 +57,14 @@ def _pack_bytes(items: Dict[int, dict], device: torch.device) -> Tuple[torch.Ten
 
 
 def _unpack_bytes(buf: torch.Tensor, header: list) -> Dict[int, dict]:
+    """Inverse of _pack_bytes.  Byte fields (the packed tiles, most of the volume) are views into `buf`; the small
+    typed fields are copied, since their offsets in the flat buffer need not be aligned to their element size."""
     out, off = {}, 0
     for ent in header:
         d = {"slices": ent["slices"]}
         for k, dt, shape, n in ent["fields"]:
-            d[k] = buf[off:off + n].clone().view(getattr(torch, dt)).reshape(shape)
+            b = buf[off:off + n]
+            d[k] = (b if dt == "uint8" else b.clone().view(getattr(torch, dt))).reshape(shape)
             off += n
         out[ent["index"]] = d
     return out
@@ -85,9 +88,19 @@ def gather_ltq(local: Dict[int, dict], dst: int = 0, group=None) -> Optional[Dic
     if rank == dst:
         recv = [torch.empty(n_max, dtype=torch.uint8, device=dev) for _ in range(world)]
         dist.gather(send, recv, dst=dst, group=group)
+        host = []
+        for r in range(world):  # device buffers come back through pinned memory, all copies in flight at once
+            if recv[r].is_cuda:
+                h = torch.empty(meta[r][0], dtype=torch.uint8, pin_memory=True)
+                h.copy_(recv[r][: meta[r][0]], non_blocking=True)
+            else:
+                h = recv[r][: meta[r][0]]
+            host.append(h)
+        if dev.type == "cuda":
+            torch.cuda.current_stream(dev).synchronize()
         out: Dict[int, dict] = {}
         for r in range(world):
-            out.update(_unpack_bytes(recv[r][: meta[r][0]].cpu(), meta[r][1]))
+            out.update(_unpack_bytes(host[r], meta[r][1]))
         return out
     dist.gather(send, None, dst=dst, group=group)
     return None
