@@ -71,3 +71,25 @@ def test_no_cpu_fallback():
     x = torch.zeros(2, 256)
     with pytest.raises(RuntimeError, match="CUDA"):
         viterbi_ub_cuda(x, torch.zeros(8), 2, 10, 359)
+
+
+def test_matrix_entries_reject_bad_arguments():
+    """The Hessian and LDLQ helper entry points return -1 on invalid sizes, strides and alignments before any CUDA
+    call (fake, never-dereferenced addresses)."""
+    L = _lib.lib()
+    a, b = 1 << 20, 1 << 21  # 16-byte aligned stand-ins
+    # blocked-Cholesky diagonal step: null pointers, c0 or ld not a multiple of 4, ld too small, misaligned pointers
+    assert L.ltq_chol256_diag(None, 256, 0, b, None, 0, a, None) == -1
+    assert L.ltq_chol256_diag(a, 256, 0, None, None, 0, a, None) == -1
+    assert L.ltq_chol256_diag(a, 256, 0, b, None, 0, None, None) == -1
+    assert L.ltq_chol256_diag(a, 512, 2, b, None, 0, a, None) == -1
+    assert L.ltq_chol256_diag(a, 254, 0, b, None, 0, a, None) == -1
+    assert L.ltq_chol256_diag(a, 510, 256, b, None, 0, a, None) == -1
+    assert L.ltq_chol256_diag(a + 4, 256, 0, b, None, 0, a, None) == -1
+    assert L.ltq_chol256_diag(a, 256, 0, b + 2, None, 0, a, None) == -1
+    assert L.ltq_chol256_diag(a, 256, 0, b, a, 255, a, None) == -1
+    # six-slot operand split: bad order / side, unaligned input, output row stride too small
+    assert L.ltq_bf16x6_split(a, 256, 4, 256, 2, 0, b, 1536, None) == -1
+    assert L.ltq_bf16x6_split(a, 256, 4, 256, 0, 2, b, 1536, None) == -1
+    assert L.ltq_bf16x6_split(a + 4, 256, 4, 256, 0, 0, b, 1536, None) == -1
+    assert L.ltq_bf16x6_split(a, 256, 4, 256, 0, 0, b, 1532, None) == -1
