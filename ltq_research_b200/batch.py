@@ -71,7 +71,7 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
                       n_streams: int = 8, pack: bool = True, keep_w_hat: bool = False,
                       device: Optional[torch.device] = None, on_issued=None, ltq_formats: Optional[Dict] = None,
                       to_host: bool = False, gemm: str = "bf16x6", order: str = "lpt",
-                      prep_ahead: bool = False) -> List[Dict]:
+                      prep_ahead: bool = False, row_reduce=None) -> List[Dict]:
     """Quantize every (W [M, K], H [K, K], spec) of `jobs` as quantize_matrix_liqk_v2(W, H, spec, seed, damp) would,
     concurrently on `n_streams` CUDA streams.  W / H may be CUDA tensors or (pinned) host tensors, which are copied to
     the device on the matrix's stream.  Returns, per job: {"qdata", "pack" (the PACK["matrix"] fields, device tensors)
@@ -87,7 +87,11 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
     order: the order in which the streams take jobs — "lpt" (default) longest estimated time first, "given" as listed.
     prep_ahead: issue each stream's next job's Hessian preparation on a second stream while the current job runs
     (measured on the bench's layer set: no gain once the device is saturated, so off by default).  The results depend
-    on neither."""
+    on neither.
+    row_reduce: every job is this rank's row slice of a matrix whose rows are split across ranks (shard.row_ranges),
+    and row_reduce(t) sums t in place over those ranks (shard.nccl_row_reduce); see liqk_v2._quantize_matrix_steps.
+    Every rank must pass the same matrices in the same order; the jobs are then taken as given, so that all ranks
+    issue their sums in the same order whatever their slices' sizes."""
     if not jobs:
         return []
     dev = torch.device(device) if device is not None else None
@@ -103,6 +107,8 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
     main = torch.cuda.current_stream(dev)
     streams = _streams(dev, max(1, n_streams))
     cost = [estimated_seconds(W.shape[0], W.shape[1], sp) for W, _, sp in jobs]
+    if row_reduce is not None:
+        order = "given"
     if order == "lpt":
         pending = sorted(range(len(jobs)), key=lambda i: -cost[i])[::-1]  # pop() takes the longest remaining job
     elif order == "given":
@@ -125,7 +131,8 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
                 if t.is_cuda:
                     t.record_stream(p)
                     t.record_stream(s)
-            gen = _quantize_matrix_steps(Wd, Hd, sp, seed, damp, None, pack or ltq_formats is not None, None, gemm)
+            gen = _quantize_matrix_steps(Wd, Hd, sp, seed, damp, None, pack or ltq_formats is not None, None, gemm,
+                                         row_reduce)
             next(gen)
             ev = torch.cuda.Event()
             ev.record(p)

@@ -268,14 +268,23 @@ def quantize_liqk_v2_diag_rot(W_rot: torch.Tensor, diag_h: torch.Tensor, spec_na
 
 @torch.no_grad()
 def compute_optimal_suh(W: torch.Tensor, H: torch.Tensor, seed: int = 1337,
-                        row_weights: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+                        row_weights: Optional[torch.Tensor] = None,
+                        row_reduce=None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """src/liqk_v2.py:409-441: suh = fp16(sign * clamp(col_rms^0.5 * h_std^-0.25, 0.25, 4));
-    W_rot = FWHT(W / suh), H_rot = FWHT(FWHT(H * suh)^T * suh)^T."""
+    W_rot = FWHT(W / suh), H_rot = FWHT(FWHT(H * suh)^T * suh)^T.
+    row_reduce: W holds some rows of the matrix and row_reduce(t) sums t in place over the holders of all of them
+    (see _quantize_matrix_steps); the column RMS is then taken over every row."""
     device = W.device
     M, K = W.shape
     signs = make_rademacher_signs(K, seed=seed, device=device)
     Wf = W.float()
-    if row_weights is not None:
+    if row_reduce is not None:
+        if row_weights is not None:
+            raise ValueError("row-sharded quantization takes no row weights")
+        acc = torch.cat([Wf.square().sum(dim=0), torch.full((1,), float(M), device=device)])
+        row_reduce(acc)
+        col_rms = (acc[:K] / acc[K]).sqrt().clamp(min=1e-6)
+    elif row_weights is not None:
         rw = row_weights.float().clamp(min=float(row_weights.mean().item()) * 0.1)
         rw = (rw / rw.mean().clamp(min=1e-12)).clamp(0.25, 4.0)
         col_rms = ((Wf.square() * rw.unsqueeze(1)).mean(dim=0)).sqrt().clamp(min=1e-6)
@@ -543,14 +552,15 @@ def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: to
 @torch.no_grad()
 def _quantize_matrix_core(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
                           row_weights: Optional[torch.Tensor] = None, want_pack: bool = False,
-                          rows_fn=None, gemm: str = "fp32") -> dict:
+                          rows_fn=None, gemm: str = "fp32", row_reduce=None) -> dict:
     """_quantize_matrix_steps run to its end (see there)."""
-    return _drive(_quantize_matrix_steps(W, H, spec_or_row_specs, seed, damp, row_weights, want_pack, rows_fn, gemm))
+    return _drive(_quantize_matrix_steps(W, H, spec_or_row_specs, seed, damp, row_weights, want_pack, rows_fn, gemm,
+                                         row_reduce))
 
 
 def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, seed: int = 1337, damp: float = 0.02,
                            row_weights: Optional[torch.Tensor] = None, want_pack: bool = False, rows_fn=None,
-                           gemm: str = "fp32"):
+                           gemm: str = "fp32", row_reduce=None):
     """The computation of quantize_matrix_liqk_v2 (src/liqk_v2.py:1029-1198) for the TCQ formats, on the current
     stream and without host synchronisation (with row_weights=None): the reference's data-dependent host branches
     become device-side selections of the same tensors (torch.where), its raising Cholesky / solve their *_ex forms.
@@ -559,7 +569,12 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     bit; "bf16x6": fp32-accurate split products on the tensor cores, see GEMM_MODES).
     rows_fn: the row-group quantizer called for each format's rows (default: the block-stepped _rows_ldlq).  A
     generator: it yields after the Hessian preparation and after each 256-column block, so that a scheduler can
-    interleave the launches of several matrices on several streams; its return value is the result dict."""
+    interleave the launches of several matrices on several streams; its return value is the result dict.
+    row_reduce: for a matrix whose rows are split across ranks (src/liqk_v2.py's quantizer is row-local except for the
+    column statistics of suh and the refit's sums over rows), W holds this rank's rows and row_reduce(t) must sum t in
+    place over all ranks holding the matrix (e.g. torch.distributed.all_reduce on their group), called in the same
+    order on every rank: the column sums of W^2 with the row count, the refit's Gram matrix U^T U and b_in, the two
+    refit losses, and num / den.  H is the whole matrix's Hessian on every rank.  No row weights."""
     W_f32 = W.float()
     H_f32 = H.float()
     M, K = W_f32.shape
@@ -570,7 +585,7 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
             raise ValueError(f"{sp}: not a TCQ (.ltq) format; this path quantizes the TCQ formats only")
     damp *= float(os.environ.get("TCQ_DAMP_MULT", "10"))
 
-    W_rot, H_rot, suh = compute_optimal_suh(W, H_f32, seed=seed, row_weights=row_weights)
+    W_rot, H_rot, suh = compute_optimal_suh(W, H_f32, seed=seed, row_weights=row_weights, row_reduce=row_reduce)
 
     H_reg = H_rot.float().clone()
     diag_mean = H_reg.diagonal().mean().clamp(min=1e-8)
@@ -662,12 +677,16 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
         rw = torch.ones((M,), dtype=torch.float32, device=W.device)
         U_w = U_scaled
     if gemm == "fp32":
-        A_in = (U_w.T @ U_scaled) * H_f32
+        A_in = U_w.T @ U_scaled
     elif row_weights is None:  # U_w is U_scaled: a Gram matrix, needed on its lower triangle only (Cholesky below)
-        A_in = _gram_lower6(U_scaled) * H_f32
+        A_in = _gram_lower6(U_scaled)
     else:
-        A_in = _mm(U_w.T, U_scaled, gemm) * H_f32
+        A_in = _mm(U_w.T, U_scaled, gemm)
     b_in = (U_w * HW).sum(dim=0)
+    if row_reduce is not None:  # both are sums over the rows
+        row_reduce(A_in)
+        row_reduce(b_in)
+    A_in = A_in * H_f32
     A_in.diagonal().add_(1e-3 * A_in.diagonal().mean().clamp(min=1e-12))
     # the reference solves, and keeps the refit when the solve succeeds and lowers the loss (src/liqk_v2.py:1161-1180).
     # A_in = (U_w^T U_scaled) o H + eps I is symmetric positive definite by construction (a Schur product of two Gram
@@ -688,6 +707,10 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     diff_cand = W_f32 - W_hat_cand
     loss_base = (((HW - HQ) * diff_base).sum(dim=1) * rw).sum()
     loss_cand = (((HW - HQ_cand) * diff_cand).sum(dim=1) * rw).sum()
+    if row_reduce is not None:
+        losses = torch.stack([loss_base, loss_cand])
+        row_reduce(losses)
+        loss_base, loss_cand = losses[0], losses[1]
     take = (solve_info == 0) & (loss_cand < loss_base)
     W_hat_eff = torch.where(take, W_hat_cand, W_hat_eff)
     d_full = torch.where(take, d_new, d_full)
@@ -717,7 +740,12 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     del times_h
     diff = W_f32 - W_hat_eff
     num = ((HW - HQ) * diff).sum()
-    den = (HW * W_f32).sum().clamp(min=1e-12)
+    den = (HW * W_f32).sum()
+    if row_reduce is not None:
+        nd = torch.stack([num, den])
+        row_reduce(nd)
+        num, den = nd[0], nd[1]
+    den = den.clamp(min=1e-12)
     qdata = {"d": d_full, "suh": suh.to(torch.float16), "row_slices": row_slices}
     return {"qdata": qdata, "W_hat": W_hat_eff, "num": num, "den": den, "chol_info": chol_info, "pack": pack}
 

@@ -8,6 +8,13 @@ computes the same assignment without communicating.  Each rank quantizes its sha
 `gather_ltq` then brings every rank's packed tensors (data, slice table, d_row, e, suh) to one rank with
 torch.distributed — NCCL between the GPUs of a B200 node (NVLink / NVSwitch), gloo on CPU for the tests — as one
 all-gather of sizes and headers followed by one gather of a flat byte buffer per rank.
+
+Matrices can also be split by rows (many matrices of one shape, such as MoE experts, or fewer matrices than ranks):
+`row_ranges` gives every rank a contiguous range of 16-row tiles, each rank quantizes its rows of every matrix with
+batch.quantize_matrices(..., row_reduce=nccl_row_reduce(group)) — H is the whole matrix's Hessian on every rank, the
+quantizer is row-local except for sums over rows (the column statistics of suh, the refit's Gram matrix and right-hand
+side, its two losses, the final loss), which row_reduce adds up across the ranks, five all-reduces per matrix, so all
+ranks reach the same suh — and `merge_row_shards` joins the shards' packed fields into one matrix.
 """
 from __future__ import annotations
 
@@ -34,6 +41,58 @@ def assign(shapes: Sequence[Tuple[int, int, object]], world: int) -> List[List[i
     for lst in out:
         lst.sort()
     return out
+
+
+def row_ranges(M: int, world: int, multiple: int = 16) -> List[Tuple[int, int]]:
+    """Contiguous row ranges [r0, r1) of an M-row matrix for `world` ranks, for matrices sharded by rows (many experts
+    of one shape, or too few matrices per rank): every boundary a multiple of `multiple` (16, the Viterbi tile's
+    height), sizes within one multiple of each other, earlier ranks taking the larger ones.  Every rank gets rows
+    (every rank takes part in the row sums): M >= world * multiple."""
+    if world < 1 or multiple < 1 or M % multiple or M < world * multiple:
+        raise ValueError(f"row_ranges: M = {M} must be a multiple of {multiple} and at least {world} x {multiple}")
+    units = M // multiple
+    q, rem = divmod(units, world)
+    out, r0 = [], 0
+    for k in range(world):
+        n = (q + (1 if k < rem else 0)) * multiple
+        out.append((r0, r0 + n))
+        r0 += n
+    return out
+
+
+def nccl_row_reduce(group=None):
+    """The row_reduce of batch.quantize_matrices for ranks that split matrices by rows: an in-place sum over `group`
+    (NCCL between the GPUs of a node), issued on the current stream."""
+    import torch.distributed as dist
+
+    def reduce(t: torch.Tensor):
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    return reduce
+
+
+def merge_row_shards(parts: Sequence[dict], align: int = 64) -> dict:
+    """One matrix's .ltq fields from the fields of its consecutive row shards (in row order, as quantize_matrices
+    returns them under "ltq", on one device or on the host): packed data concatenated with every shard starting on an
+    `align`-byte boundary, slice rows and offsets moved accordingly, d_row and e stacked; suh must be the same in every
+    shard (the row-sharded refit makes it so)."""
+    if not parts:
+        raise ValueError("merge_row_shards: no shards")
+    suh = parts[0]["suh"]
+    data, slices, row0, off = [], [], 0, 0
+    for p in parts:
+        if not torch.equal(p["suh"].to(suh.device), suh):
+            raise ValueError("merge_row_shards: the shards disagree on suh")
+        pad = (-off) % align
+        if pad:
+            data.append(torch.zeros(pad, dtype=torch.uint8, device=p["data"].device))
+            off += pad
+        for r0, r1, fi, o in p["slices"]:
+            slices.append([r0 + row0, r1 + row0, fi, o + off])
+        data.append(p["data"].reshape(-1))
+        off += int(p["data"].numel())
+        row0 += int(p["d_row"].shape[0])
+    return {"data": torch.cat([d.to(parts[0]["data"].device) for d in data]), "slices": slices,
+            "d_row": torch.cat([p["d_row"] for p in parts]), "e": torch.cat([p["e"] for p in parts]), "suh": suh}
 
 
 _FIELDS = ("data", "d_row", "e", "suh")

@@ -56,6 +56,13 @@ def _worker(rank, world, port, mode, q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
     mine = assign(_shapes(2), world)[rank]
+    if mode == "reduce":  # the row sums of row-sharded matrices, over the same collective
+        from ltq_research_b200.shard import nccl_row_reduce
+        t = torch.arange(5, dtype=torch.float32) * (rank + 1)
+        nccl_row_reduce()(t)
+        q.put((rank, "ok" if torch.equal(t, torch.arange(5, dtype=torch.float32) * 3) else "mismatch", None))
+        dist.destroy_process_group()
+        return
     if mode == "leave" and rank == 1:
         os._exit(0)  # leaves between steps, with no collective in flight
     try:
@@ -81,7 +88,7 @@ def _run(mode):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
     for p in procs:
         p.start()
-    n = 2 if mode == "ok" else 1
+    n = 1 if mode == "leave" else 2
     res = sorted(q.get(timeout=120) for _ in range(n))
     for p in procs:
         p.join(timeout=60)
@@ -97,3 +104,48 @@ def test_gather_ltq_world2_gloo():
 def test_gather_ltq_peer_leaves_gloo():
     res = _run("leave")
     assert res[0][0] == 0 and res[0][1] == "error", res
+
+
+def test_row_reduce_world2_gloo():
+    assert _run("reduce") == [(0, "ok", None), (1, "ok", None)]
+
+
+def test_row_ranges():
+    from ltq_research_b200.shard import row_ranges
+    for M, world in ((96, 4), (1024, 3), (8192, 8), (16, 1), (48, 3)):
+        rr = row_ranges(M, world)
+        assert rr[0][0] == 0 and rr[-1][1] == M and len(rr) == world
+        assert all(a1 == b0 for (_, a1), (b0, _) in zip(rr, rr[1:]))
+        sizes = [r1 - r0 for r0, r1 in rr]
+        assert all(n > 0 and n % 16 == 0 for n in sizes) and max(sizes) - min(sizes) <= 16
+        assert sizes == sorted(sizes, reverse=True)
+    for M, world in ((100, 2), (32, 3), (0, 1)):
+        with pytest.raises(ValueError):
+            row_ranges(M, world)
+
+
+def test_merge_row_shards():
+    """Shards' packed fields joined into one matrix: every shard's bytes start on a 64-byte boundary, slice rows and
+    offsets move with them, d_row / e stack, and shards that disagree on suh are refused."""
+    from ltq_research_b200.shard import merge_row_shards
+    parts = [_fake_ltq(i) for i in (0, 1, 2)]
+    for p in parts[1:]:
+        p["suh"] = parts[0]["suh"].clone()
+    parts[1]["slices"] = [[0, 8, 0, 0], [8, 32, 1, 64]]
+    m = merge_row_shards(parts)
+    rows = [0, 16, 48]
+    offs, off = [], 0
+    for p in parts:
+        off += (-off) % 64
+        offs.append(off)
+        off += p["data"].numel()
+    assert m["data"].numel() == off
+    for p, r0, o in zip(parts, rows, offs):
+        assert torch.equal(m["data"][o:o + p["data"].numel()], p["data"])
+    assert m["slices"] == [[0, 16, 0, 0], [16, 24, 0, offs[1]], [24, 48, 1, offs[1] + 64], [48, 96, 0, offs[2]]]
+    assert torch.equal(m["d_row"], torch.cat([p["d_row"] for p in parts]))
+    assert torch.equal(m["e"], torch.cat([p["e"] for p in parts]))
+    assert torch.equal(m["suh"], parts[0]["suh"])
+    parts[2]["suh"] = parts[2]["suh"] + 1
+    with pytest.raises(ValueError):
+        merge_row_shards(parts)
