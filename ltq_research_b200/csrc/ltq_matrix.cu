@@ -484,6 +484,11 @@ __global__ void __launch_bounds__(544, 1) chol256_tiled_kernel(float* __restrict
             float* dst = Ab + (long long)(8 * bi + r) * ld + 8 * bk;
             *reinterpret_cast<float4*>(dst) = make_float4(a[r][0], a[r][1], a[r][2], a[r][3]);
             *reinterpret_cast<float4*>(dst + 4) = make_float4(a[r][4], a[r][5], a[r][6], a[r][7]);
+            if (bi != bk) {  // the mirror tile above the diagonal: zeros, so that the block holds exactly L
+                float* up = Ab + (long long)(8 * bk + r) * ld + 8 * bi;
+                *reinterpret_cast<float4*>(up) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4*>(up + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
     }
     // phase 2: Y = L~^-1, in the registers of the factor's tile
