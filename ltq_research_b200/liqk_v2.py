@@ -3,10 +3,13 @@
 Mirrors lumen-inference/ltq-research src/liqk_v2.py (same names, arguments, return values and ``PACK`` side channel):
   * ``compute_optimal_suh`` (:409-441) — column scale suh and the FWHT-256 rotations of W and H (ltq_fwht256 kernel);
   * ``_quantize_rows_tcq_ldlq`` (:872-1021, row-scale branch :956-980) — scale fit (ltq_scale_fit kernel), then per
-    256-column block 16 sub-blocks of tail-biting Viterbi (ltq_viterbi_tb) with the intra-block error feedback
-    (ltq_ldlq_gather / ltq_ldlq_feedback kernels) and the inter-block feedback GEMM (cuBLAS fp32 through torch);
-  * ``quantize_matrix_liqk_v2`` (:1029-1198) — damping, Cholesky factorisation (cuSOLVER through torch), row groups,
-    c_row and suh refits, PACK emission.
+    256-column block 16 sub-blocks of tail-biting Viterbi with the intra-block error feedback (one fused ltq_ldlq_block
+    launch per block) and the inter-block feedback GEMM;
+  * ``quantize_matrix_liqk_v2`` (:1029-1198) — damping, Cholesky factorisation, row groups, c_row and suh refits, PACK
+    emission.
+Two modes for the linear algebra (GEMM_MODES): "fp32" runs the reference's torch operations (cuBLAS fp32, cuSOLVER's
+Cholesky and solves) bit for bit; "bf16x6", the batch driver's default, runs the products as fp32-accurate six-product
+bf16 GEMMs on the tensor cores and the factorisations through hessian.cholesky_lower / tri_inv_lower.
 Only the tail-biting row-scale formats of TCQ_CONFIG (the .ltq formats) are handled; the reference's other quantizers
 (.liqk v2 banks, E8) are out of this path.  Everything runs on CUDA; there is no CPU path.
 """
