@@ -143,9 +143,9 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
         return i, gen, ev
 
     # every lane: one job in its block / refit steps on the lane's stream and, with prep_ahead, the next job's
-    # preparation already issued on the lane's preparation stream (its single-CTA Cholesky leaves and triangular-inverse
-    # kernels are latency-bound and overlap the other jobs' blocks).  Each round advances every lane's current job by one step
-    # (one 256-column block, or the refits), so that every stream keeps work queued.
+    # preparation already issued on the lane's preparation stream (its single-CTA Cholesky leaves and
+    # triangular-inverse kernels are latency-bound and overlap the other jobs' blocks).  Each round advances every
+    # lane's current job by one step (one 256-column block, or the refits), so that every stream keeps work queued.
     cur: List[Optional[tuple]] = [None] * len(streams)
     nxt: List[Optional[tuple]] = [None] * len(streams)
     while pending or any(c is not None for c in cur) or any(n is not None for n in nxt):
