@@ -170,3 +170,14 @@ def test_cholesky_lower_info_first_bad_minor(j, cuda_dev):
     _, info_lib = torch.linalg.cholesky_ex(A)
     assert int(info) == j + 1
     assert int(info_lib) == j + 1 or (j % 256 == 255 and int(info_lib) == j + 2)
+
+
+def test_factorization_entry_checks_cpu():
+    """cholesky_lower / tri_inv_lower take square fp32 CUDA matrices with a multiple of 256 rows and raise otherwise
+    (there is no CPU path)."""
+    from ltq_research_b200.hessian import cholesky_lower, tri_inv_lower
+    for bad in (torch.eye(256), torch.eye(256, dtype=torch.float64), torch.zeros(256, 512), torch.eye(200)):
+        with pytest.raises(ValueError):
+            cholesky_lower(bad)
+        with pytest.raises(ValueError):
+            tri_inv_lower(bad)
