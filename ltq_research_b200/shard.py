@@ -70,29 +70,92 @@ def nccl_row_reduce(group=None):
     return reduce
 
 
-def merge_row_shards(parts: Sequence[dict], align: int = 64) -> dict:
+def _region_words(f) -> List[int]:
+    """u16 words per tile of the four SoA regions of a packed slice: code bits, bit planes, low bits, gain bits
+    (src/ltq_file.py:79-102; each region starts on a 64-byte boundary, tiles by row group then 16-column block)."""
+    if getattr(f, "frac", 0) == 3:
+        raise ValueError(f"{f.name}: the EQ formats have no .ltq encoding")
+    return [16, 16 * max(f.K - 2, 0), f.lsb_words() if f.K > 1 else 0, f.gain_words()]
+
+
+def _slice_nbytes(rows: int, K: int, f, align: int = 64) -> int:
+    off = 0
+    for n in _region_words(f):
+        off = -(-off // align) * align + 2 * (rows // 16) * (K // 16) * n
+    return off
+
+
+def _coalesce(pieces: Sequence[Tuple[torch.Tensor, int]], K: int, f, align: int = 64) -> torch.Tensor:
+    """The bytes of one slice of format f made of consecutive slices [(bytes, rows)] of that format: region by region,
+    the pieces' tiles one after the other (their row groups continue), as if packed in one piece."""
+    out, off, src = [], 0, [0] * len(pieces)
+    for n in _region_words(f):
+        pad = (-off) % align
+        if pad:
+            out.append(torch.zeros(pad, dtype=torch.uint8, device=pieces[0][0].device))
+            off += pad
+        for i, (d, rows) in enumerate(pieces):
+            s0 = -(-src[i] // align) * align
+            nb = 2 * (rows // 16) * (K // 16) * n
+            out.append(d[s0:s0 + nb])
+            src[i] = s0 + nb
+            off += nb
+    return torch.cat(out) if out else torch.empty(0, dtype=torch.uint8, device=pieces[0][0].device)
+
+
+def merge_row_shards(parts: Sequence[dict], align: int = 64, formats: Optional[Sequence] = None) -> dict:
     """One matrix's .ltq fields from the fields of its consecutive row shards (in row order, as quantize_matrices
-    returns them under "ltq", on one device or on the host): packed data concatenated with every shard starting on an
-    `align`-byte boundary, slice rows and offsets moved accordingly, d_row and e stacked; suh must be the same in every
-    shard (the row-sharded refit makes it so)."""
+    returns them under "ltq", on one device or on the host): d_row and e stacked; suh must be the same in every shard
+    (the row-sharded refit makes it so).  Without `formats` the shards' packed data are concatenated, every shard
+    starting on an `align`-byte boundary, slice rows and offsets moved accordingly.  With `formats` (the format of each
+    slice index, as given to quantize_matrices' ltq_formats), slices of one format on consecutive rows become one
+    slice, packed region by region, so that the result is laid out exactly as the whole matrix packed at once."""
     if not parts:
         raise ValueError("merge_row_shards: no shards")
     suh = parts[0]["suh"]
-    data, slices, row0, off = [], [], 0, 0
     for p in parts:
         if not torch.equal(p["suh"].to(suh.device), suh):
             raise ValueError("merge_row_shards: the shards disagree on suh")
+    dev = parts[0]["data"].device
+    d_row = torch.cat([p["d_row"] for p in parts])
+    e = torch.cat([p["e"] for p in parts])
+    if formats is None:
+        data, slices, row0, off = [], [], 0, 0
+        for p in parts:
+            pad = (-off) % align
+            if pad:
+                data.append(torch.zeros(pad, dtype=torch.uint8, device=p["data"].device))
+                off += pad
+            for r0, r1, fi, o in p["slices"]:
+                slices.append([r0 + row0, r1 + row0, fi, o + off])
+            data.append(p["data"].reshape(-1))
+            off += int(p["data"].numel())
+            row0 += int(p["d_row"].shape[0])
+        return {"data": torch.cat([d.to(dev) for d in data]), "slices": slices, "d_row": d_row, "e": e, "suh": suh}
+    K = int(suh.numel())
+    runs: List[list] = []  # [r0, r1, fi, [(bytes, rows), ...]]
+    row0 = 0
+    for p in parts:
+        flat = p["data"].reshape(-1).to(dev)
+        for r0, r1, fi, o in sorted(p["slices"], key=lambda x: x[0]):
+            piece = (flat[o:o + _slice_nbytes(r1 - r0, K, formats[fi], align)], r1 - r0)
+            if runs and runs[-1][2] == fi and runs[-1][1] == r0 + row0:
+                runs[-1][1] = r1 + row0
+                runs[-1][3].append(piece)
+            else:
+                runs.append([r0 + row0, r1 + row0, fi, [piece]])
+        row0 += int(p["d_row"].shape[0])
+    data, slices, off = [], [], 0
+    for r0, r1, fi, pieces in runs:
         pad = (-off) % align
         if pad:
-            data.append(torch.zeros(pad, dtype=torch.uint8, device=p["data"].device))
+            data.append(torch.zeros(pad, dtype=torch.uint8, device=dev))
             off += pad
-        for r0, r1, fi, o in p["slices"]:
-            slices.append([r0 + row0, r1 + row0, fi, o + off])
-        data.append(p["data"].reshape(-1))
-        off += int(p["data"].numel())
-        row0 += int(p["d_row"].shape[0])
-    return {"data": torch.cat([d.to(parts[0]["data"].device) for d in data]), "slices": slices,
-            "d_row": torch.cat([p["d_row"] for p in parts]), "e": torch.cat([p["e"] for p in parts]), "suh": suh}
+        b = _coalesce(pieces, K, formats[fi], align)
+        slices.append([r0, r1, fi, off])
+        data.append(b)
+        off += int(b.numel())
+    return {"data": torch.cat(data), "slices": slices, "d_row": d_row, "e": e, "suh": suh}
 
 
 _FIELDS = ("data", "d_row", "e", "suh")

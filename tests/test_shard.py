@@ -149,3 +149,72 @@ def test_merge_row_shards():
     parts[2]["suh"] = parts[2]["suh"] + 1
     with pytest.raises(ValueError):
         merge_row_shards(parts)
+
+
+def _pack_fmts(names):
+    import numpy as np
+    from ltq_research_b200.formats import load_formats
+    from tests.test_oracle_golden import _ltq_fmt
+    fm = load_formats(names, "cpu")
+    return list(fm.values()), [_ltq_fmt(n, np.asarray(fm[n].gain_tab, np.float32)) for n in names]
+
+
+def test_slice_region_sizes_match_library():
+    """The region arithmetic of the coalescing merge gives the library's slice size for every .ltq format."""
+    from ltq_research_b200 import _lib
+    from ltq_research_b200.formats import TCQ_CONFIG
+    from ltq_research_b200.shard import _slice_nbytes
+    names = [n for n, c in TCQ_CONFIG.items() if int(c.get("pp", 0)) != 3]
+    fmts, _ = _pack_fmts(names)
+    for f in fmts:
+        for R, K in ((16, 256), (48, 512), (96, 768), (208, 3072)):
+            assert _slice_nbytes(R, K, f) == _lib.lib().ltq_slice_bytes(R, K, f.K, f.frac, f.h, f.sub), (f.name, R, K)
+
+
+def test_merge_row_shards_coalesces_to_whole_packing():
+    """Row shards packed separately and merged with their formats give the bytes and slice table of the whole matrix
+    packed at once (the oracle's restatement of the reference's pack_slice): one format split 48 / 48 rows, and a
+    two-format matrix whose second format spans the shard boundary."""
+    import numpy as np
+    from oracle import oracle as O
+    from ltq_research_b200.shard import merge_row_shards
+    fmts, ofmts = _pack_fmts(["TCQ3X", "TCQ25X"])
+    g = np.random.default_rng(3)
+    K = 512
+
+    def codes(rows, of):
+        idx = g.integers(0, of.n_labels * of.U, (rows, K))
+        gi = g.integers(0, max(1 << of.h, 1), (rows, K))
+        return idx, gi
+
+    def packed(idx, gi, fi):
+        return torch.from_numpy(np.frombuffer(O.pack_slice(idx, gi, ofmts[fi]), np.uint8).copy())
+
+    def part(slices, rows):  # slices: [(r0, r1, fi, idx, gi)] -> ltq fields with 64-byte aligned slices
+        data, table, off = [], [], 0
+        for r0, r1, fi, idx, gi in slices:
+            pad = (-off) % 64
+            data.append(torch.zeros(pad, dtype=torch.uint8))
+            off += pad
+            b = packed(idx, gi, fi)
+            table.append([r0, r1, fi, off])
+            data.append(b)
+            off += b.numel()
+        return {"data": torch.cat(data), "slices": table, "d_row": torch.ones(rows, dtype=torch.float16),
+                "e": torch.zeros(rows, K // 256, dtype=torch.int8), "suh": torch.ones(K, dtype=torch.float16)}
+
+    # one format, two shards of 48 rows
+    idx, gi = codes(96, ofmts[0])
+    m = merge_row_shards([part([(0, 48, 0, idx[:48], gi[:48])], 48), part([(0, 48, 0, idx[48:], gi[48:])], 48)],
+                         formats=fmts)
+    assert m["slices"] == [[0, 96, 0, 0]]
+    assert torch.equal(m["data"], packed(idx, gi, 0))
+    # rows 0-16 TCQ3X, rows 16-96 TCQ25X; shards [0, 48) and [48, 96)
+    i0, g0 = codes(16, ofmts[0])
+    i1, g1 = codes(80, ofmts[1])
+    a = part([(0, 16, 0, i0, g0), (16, 48, 1, i1[:32], g1[:32])], 48)
+    b = part([(0, 48, 1, i1[32:], g1[32:])], 48)
+    m = merge_row_shards([a, b], formats=fmts)
+    whole = part([(0, 16, 0, i0, g0), (16, 96, 1, i1, g1)], 96)
+    assert m["slices"] == whole["slices"]
+    assert torch.equal(m["data"], whole["data"])
