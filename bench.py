@@ -135,14 +135,15 @@ def alu_peak_gacs() -> tuple:
 
 
 # ------------------------------------------------------------------------------------------------
-# CPU: the oracle's restatement of the reference Viterbi on this workload's tiles (TCQ3X, tail-biting, window 32)
+# CPU: the reference's own CPU Viterbi (src/tcq_proto.py:363-419, torch) from its install in baseline/_ref; where that
+# install is absent, the oracle's C restatement of the reference Viterbi (oracle/tcq_oracle.c)
 # ------------------------------------------------------------------------------------------------
+CPU_TILES = 256           # tiles of 256 weights per CPU call, in both CPU legs
+CPU_PASSES = 1.0 + 2.0 * TB_WINDOW / 256.0  # trellis passes per weight of the GPU step's schedule (windowed first pass)
 
-def _cpu_format():
-    from ltq_research_b200.formats import TCQ_CONFIG
-    c = TCQ_CONFIG["TCQ3X"]
-    from ltq_research_b200.tcq_proto import make_gains
-    return c, make_gains(c["h"], c["step"], "cpu").numpy().astype(np.float32)
+
+def _cpu_threads() -> int:
+    return len(os.sched_getaffinity(0))
 
 
 def _cpu_tiles(n: int, seed: int = 0) -> tuple:
@@ -152,54 +153,100 @@ def _cpu_tiles(n: int, seed: int = 0) -> tuple:
     return x, w
 
 
-def _cpu_viterbi(x, w, c, gains, threads):
-    from oracle import oracle as O
-    return O.viterbi(x, np.asarray(c["lut"], np.float32), c["K"], 10, c["m"], gains, sub=16, wts=w,
-                     m_extra=tuple(c["m_extra"]), tail_biting=True, tb_window=TB_WINDOW, return_code=True,
-                     n_threads=threads)
+class _CpuViterbi:
+    """One CPU leg: `run(x, w)` quantizes tiles x [n, 256] with position weights w [256]; `per_weight_passes` is how
+    many trellis passes one call spends per weight; `desc` / `kind` / `threads` describe it.
+
+    The reference's CPU implementation is its torch viterbi_ub (4 label subsets, no tail-biting): it runs the
+    config-1 format of BASELINE (K = 2, 4 subsets, 2-bit gain index per 16 weights: 1024 states x 4 gain slots, the
+    same add-compare-selects per weight and pass as the GPU step's TCQ3X / TCQ25X), one free pass per call; the GPU
+    step's schedule needs CPU_PASSES passes per weight, so its rate is the pass rate / CPU_PASSES.  Without the
+    reference install, the oracle's C restatement runs the GPU step's own TCQ3X two-pass tail-biting schedule."""
+
+    def __init__(self):
+        self.threads = _cpu_threads()
+        from oracle.refroot import import_reference, reference_root
+        root = reference_root()
+        if root is not None:
+            import_reference(root)
+            os.environ["TCQ_NO_COMPILE"] = "1"  # its torch.compile step cannot build on these hosts (no Python headers)
+            torch.set_num_threads(self.threads)
+            import src.tcq_proto as tp
+            u = json.loads((root / "results" / "universal_gaussian.json").read_text())["tcq_K2_h2"]
+            self.tab = torch.tensor(u["tab"], dtype=torch.float32)
+            self.gains = tp.make_gains(2, u["step"], "cpu")
+            self.fn = tp.viterbi_ub
+            self.kind, self.per_weight_passes = "reference", 1.0
+            self.desc = ("the reference's torch viterbi_ub (src/tcq_proto.py:363-419, TCQ_NO_COMPILE=1, torch threads "
+                         f"= {self.threads}) on config-1 tiles (K 2, h 2, sub 16, mask 359), one free pass per call, "
+                         f"rate divided by {CPU_PASSES} passes per weight of the GPU step's schedule")
+        else:
+            from ltq_research_b200.formats import TCQ_CONFIG
+            from ltq_research_b200.tcq_proto import make_gains
+            self.c = TCQ_CONFIG["TCQ3X"]
+            self.gains = make_gains(self.c["h"], self.c["step"], "cpu").numpy().astype(np.float32)
+            self.fn = None
+            self.kind, self.per_weight_passes = "port", CPU_PASSES
+            self.desc = ("the C restatement of the reference Viterbi (oracle/tcq_oracle.c, OpenMP, "
+                         f"{self.threads} threads) on TCQ3X tiles, two-pass tail-biting with window {TB_WINDOW}")
+
+    def run(self, x, w):
+        if self.fn is not None:
+            xt = torch.from_numpy(x)
+            self.fn(xt, self.tab, 2, 10, 359, self.gains, sub=16, wts=torch.from_numpy(w))
+        else:
+            from oracle import oracle as O
+            c = self.c
+            O.viterbi(x, np.asarray(c["lut"], np.float32), c["K"], 10, c["m"], self.gains, sub=16, wts=w,
+                      m_extra=tuple(c["m_extra"]), tail_biting=True, tb_window=TB_WINDOW, return_code=True,
+                      n_threads=self.threads)
+
+    def rate(self, weights: int, seconds: float) -> float:
+        """Mweights/s of the GPU step's schedule for `weights` weights quantized by calls that took `seconds`."""
+        return weights / seconds / 1e6 * self.per_weight_passes / CPU_PASSES
 
 
 def cpu_baseline_sample(seconds: float = 15.0) -> dict:
-    c, gains = _cpu_format()
-    threads = len(os.sched_getaffinity(0))
-    step = max(threads, 8) * 4
-    x, w = _cpu_tiles(step * 16)
-    done, t0, i = 0, time.perf_counter(), 0
+    """The CPU leg on rank 0 at N = 1: CPU_TILES tiles per call, calls until `seconds` have passed."""
+    cv = _CpuViterbi()
+    x, w = _cpu_tiles(CPU_TILES * 4)
+    cv.run(x[:CPU_TILES], w)  # untimed first call
+    done, calls, t0 = 0, 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds:
-        j = i % 16
-        _cpu_viterbi(x[j * step:(j + 1) * step], w, c, gains, threads)
-        done += step * 256
-        i += 1
+        j = calls % 4
+        cv.run(x[j * CPU_TILES:(j + 1) * CPU_TILES], w)
+        done += CPU_TILES * 256
+        calls += 1
     el = time.perf_counter() - t0
-    return {"value": done / el / 1e6, "unit": METRIC, "cores": threads, "kind": "port",
-            "sample": f"{done // 256} TCQ3X tiles of 256 (two-pass tail-biting Viterbi, window 32) in {el:.1f} s with "
-                      f"the C restatement of the reference Viterbi (oracle/tcq_oracle.c), {threads} threads; the "
-                      f"Viterbi only (the LDLQ / refit linear algebra of the GPU step is not timed on the CPU)"}
+    return {"value": cv.rate(done, el), "unit": METRIC, "cores": cv.threads, "kind": cv.kind,
+            "sample": f"{calls} calls of {CPU_TILES} tiles of 256 in {el:.1f} s: {cv.desc}; the Viterbi search only "
+                      f"(the LDLQ / refit linear algebra of the GPU step is not timed on the CPU)"}
 
 
 def run_reference(args, rank: int, world: int):
-    """--impl reference: the reference algorithm on the host cores (the oracle port), rank 0 only."""
+    """--impl reference: the reference's CPU implementation of the path on the host cores, rank 0 only; each step one
+    call of CPU_TILES tiles (a bounded sample of one layer's sub-block tiles)."""
     if rank != 0:
         return
-    c, gains = _cpu_format()
-    threads = len(os.sched_getaffinity(0))
-    n = max(threads * 8, 64)  # tiles per step: a bounded sample of one layer's sub-block tiles
-    x, w = _cpu_tiles(n * (args.steps + args.warmup + 1), seed=1)
+    cv = _CpuViterbi()
+    n = CPU_TILES
+    x, w = _cpu_tiles(n * (args.steps + args.warmup), seed=1)
     for k in range(args.warmup):
-        _cpu_viterbi(x[k * n:(k + 1) * n], w, c, gains, threads)
+        cv.run(x[k * n:(k + 1) * n], w)
     t0 = time.perf_counter()
     for k in range(args.steps):
         s = (args.warmup + k) * n
-        _cpu_viterbi(x[s:s + n], w, c, gains, threads)
+        cv.run(x[s:s + n], w)
     el = time.perf_counter() - t0
-    v = args.steps * n * 256 / el / 1e6
-    sample = (f"{n} TCQ3X tiles of 256 per step (two-pass tail-biting Viterbi, window 32), C restatement of the "
-              f"reference Viterbi (oracle/tcq_oracle.c), {threads} threads; Viterbi only")
+    v = cv.rate(args.steps * n * 256, el)
+    sample = f"{n} tiles of 256 per step: {cv.desc}; the Viterbi search only"
     line = {"metric": METRIC, "value": v, "unit": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "tiles_per_step": n, "parallelism": "host threads"},
-            "cpu_baseline": {"value": v, "unit": METRIC, "cores": threads, "kind": "port", "sample": sample},
+            "config": {"workload": WORKLOAD, "tiles_per_step": n, "parallelism": "host threads",
+                       "reference_scope": "Viterbi search of the path (the reference's CPU code for it); the GPU arm's "
+                                          "step also includes rotation, factorisation, LDLQ feedback, refits, packing"},
+            "cpu_baseline": {"value": v, "unit": METRIC, "cores": cv.threads, "kind": cv.kind, "sample": sample},
             "e2e": {"value": v, "unit": METRIC, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -418,10 +465,11 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3 (untimed warm-up steps before the timed region)")
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
-    args.warmup = max(args.warmup, 3)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
@@ -465,10 +513,8 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # inputs of the warm-up and timed layers, resident in HBM (each layer's H and W, ~0.7 GB, far above the 126 MB L2).
-    # The warm-up quantizes as many layers as the timed region (at least --warmup), so that the timed region starts
-    # with the memory pools of all streams grown to the size it needs.
-    args.warmup = max(args.warmup, args.steps)
+    # inputs of the warm-up and timed layers, resident in HBM (each layer's H and W, ~0.7 GB, far above the 126 MB L2);
+    # the warm-up quantizes --warmup layers untimed
     warm = [j for l in range(args.warmup) for j in layer_jobs(10_000 + l, rank, dev)]
     timed = [j for l in range(args.steps) for j in layer_jobs(l, rank, dev)]
     quantize_matrices(warm, n_streams=args.streams, ltq_formats=fmts, pack=False)

@@ -7,7 +7,9 @@
  *    -1   unsupported or invalid parameters (the same validation table as the reference, plus the limits named below),
  *    >0   a cudaError_t from the launch.
  * No entry point allocates device memory: outputs and scratch are passed in by the caller.  All entry points are
- * re-entrant; calls on different streams may run concurrently.
+ * re-entrant; calls on different streams may run concurrently.  One exception, ltq_viterbi_tb_noalloc (end of this
+ * file): its scratch is one array inside the library shared by all its calls on a device, so calls of it that overlap
+ * on the GPU must be serialised by the caller, and it returns -2 for a problem larger than that array.
  *
  * Reference: lumen-inference/ltq-research (paths below are relative to its root).
  */
@@ -164,6 +166,14 @@ int lut_subs_quant(const float* xs, const float* dh, const float* lut, float* ou
                    int nb, void* stream);
 
 /*
+ * int8 ring format of the row tables, the comparison baseline of the ring quantizer (replaces int8_rows,
+ * src/ple_quant.py:68-77): per ring of 256 consecutive values, d = max(fp16(max |x| / 127), 1e-10) and
+ * out = clamp(round_half_even(x / d), -127, 127) * d, in the input's dtype (bf16 = 1: bf16, else fp32); NaN propagates
+ * as in the reference's torch operations.  in / out hold n_rings * 256 values, 16-byte aligned.
+ */
+int ltq_int8_rings(const void* in, void* out, long long n_rings, int bf16, void* stream);
+
+/*
  * .ltq tile packing and spec decode (src/ltq_file.py:54-148; tile fields src/ltq_format.py:104-147).  A row slice
  * [R, K] (R, K multiples of 16) is (R/16)(K/16) tiles of 16 x 16; the packed slice is four structure-of-arrays regions
  * (codes, planes, lsb, gains), each at a multiple of 64 bytes — byte for byte what the reference's pack_slice writes.
@@ -203,7 +213,9 @@ int ltq_matvec_slice(const uint8_t* data, int R, int K, int kbits, int frac, int
  * held on every GPU that loads the library until the process exits.  Returns -2 when
  * ltq_viterbi_tb_workspace_bytes(...) exceeds that capacity.  Every call on a device shares the array: calls that
  * overlap on the GPU race and must be serialised.  The first call on a device looks up the array's address (make it
- * before any stream capture).  Calls no allocator.
+ * before any stream capture) and keeps it for the life of the process: after cudaDeviceReset on that device the kept
+ * address is stale, so a process that resets a device must not call this entry on it again.  Calls no allocator.
+ * Errors: -1 invalid parameters, -2 too large for the array, >0 the cudaError_t of the address lookup or the launch.
  */
 size_t ltq_viterbi_tb_noalloc_capacity(void);
 int ltq_viterbi_tb_noalloc(const float* x, const float* w, int w_stride, const float* tab, const float* gains,

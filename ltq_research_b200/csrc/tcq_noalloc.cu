@@ -15,7 +15,9 @@
 // pass.
 //
 // Set-up: the first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
-// current) and caches it; make that first call before any stream capture on that device.
+// current) and caches it for the life of the process; make that first call before any stream capture on that device.
+// A process that resets the device (cudaDeviceReset) must not call this entry on it afterwards: the cached address
+// would be stale.  A failed lookup returns its own cudaError_t.
 #include <cuda_runtime.h>
 #include <mutex>
 #include "ltq_b200.h"
@@ -29,18 +31,25 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_ptr[kMaxDevices];  // device address of g_noalloc_scratch per device, set once
 
-// Device address of the scratch on the current device (looked up once per device); nullptr on failure.
-void* scratch_on_current_device()
+// Device address of the scratch on the current device, looked up once per device and kept for the life of the
+// process (a cudaDeviceReset of that device makes the kept address stale).  Returns the CUDA error of the lookup
+// (cudaErrorInvalidDevice for a device ordinal beyond the table).
+cudaError_t scratch_on_current_device(void** out)
 {
+    *out = nullptr;
     int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_ptr[dev]) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
         g_ptr[dev] = p;
     }
-    return g_ptr[dev];
+    *out = g_ptr[dev];
+    return cudaSuccess;
 }
 }  // namespace
 
@@ -54,8 +63,9 @@ extern "C" int ltq_viterbi_tb_noalloc(const float* x, const float* w, int w_stri
 {
     const size_t need = ltq_viterbi_tb_workspace_bytes(N, T, Gfull, n_cand, sub, pp, tb_window, tb_cand1);
     if (need > LTQ_NOALLOC_SCRATCH_BYTES) return -2;
-    void* ws = scratch_on_current_device();
-    if (!ws) return (int)cudaErrorInvalidDevice;
+    void* ws = nullptr;
+    const cudaError_t e = scratch_on_current_device(&ws);
+    if (e != cudaSuccess) return (int)e;
     return ltq_viterbi_tb(x, w, w_stride, tab, gains, tab_hi, gains_hi, rec, code, N, T, nu, K, m, m_extra, n_extra,
                           Gfull, n_cand, sub, U_hi, mix, pp, tb_passes, tb_cand1, tb_window, ws,
                           LTQ_NOALLOC_SCRATCH_BYTES, stream);

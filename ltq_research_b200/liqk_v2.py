@@ -211,62 +211,77 @@ def get_warp_register_bank(spec_name: str, device) -> Dict[str, torch.Tensor]:
     return _WARP_BANK_CACHE[key]
 
 
+LUT_PICK_CHUNK = 32768  # sub-blocks per torch evaluation of the table pick (bounds the [chunk, 16, C] temporaries)
+
+
+def _lut_pick_torch(xs: torch.Tensor, dh: torch.Tensor, lut_val: torch.Tensor, inv_step: float,
+                    half_b: float) -> torch.Tensor:
+    """Table pick of one batch of sub-blocks in torch arithmetic: every weight's bucket round(x * inv_step + half_b)
+    (product rounded before the add, ties to even, clamped to the table), the weighted squared error of every column
+    summed over the sub-block, the first column of least error, and the sub-block's values from that column."""
+    nb, C = lut_val.shape
+    bucket = torch.clamp((xs * inv_step + half_b).round().long(), 0, nb - 1)          # [s, 16]
+    cand = lut_val[bucket]                                                             # [s, 16, C]
+    score = ((xs.unsqueeze(-1) - cand).square() * dh.unsqueeze(-1)).sum(dim=1)        # [s, C]
+    col = score.argmin(dim=-1)                                                         # [s]
+    return cand.gather(2, col.view(-1, 1, 1).expand(-1, xs.shape[1], 1)).squeeze(2)
+
+
 @torch.no_grad()
 def quantize_subs_lut_chunked(x_subs: torch.Tensor, dhs: torch.Tensor, lut_val: torch.Tensor, inv_step: float,
                               half_b: float) -> torch.Tensor:
-    """The DP profile's torch path (src/liqk_v2.py:444-466), for tables with other than 64 columns: per sub-block the
-    column of lut_val with the smallest weighted error, buckets round(x * inv_step + half_b) (product rounded before
-    the sum), in chunks of 32768 sub-blocks."""
-    S_tot = x_subs.shape[0]
-    G_out = torch.empty((S_tot, SUBBLOCK_SIZE), dtype=torch.float32, device=x_subs.device)
-    chunk = 32768
-    for i0 in range(0, S_tot, chunk):
-        i1 = min(i0 + chunk, S_tot)
-        xs = x_subs[i0:i1]
-        dh = dhs[i0:i1]
-        b_idx = (xs * inv_step + half_b).round().long().clamp(0, N_LUT_BUCKETS - 1)
-        g_cand = lut_val[b_idx]
-        err2 = (xs.unsqueeze(-1) - g_cand).square()
-        bc = (err2 * dh).sum(dim=1).argmin(dim=-1)
-        ar = torch.arange(i1 - i0, device=x_subs.device)
-        G_out[i0:i1] = g_cand[ar, :, bc]
-    return G_out
+    """The DP profile's table pick for tables of any width (src/liqk_v2.py:444-466, the reference's path for tables
+    other than 64 columns): x_subs [S, 16], dhs [S, 16] or [S, 16, 1] -> [S, 16], evaluated LUT_PICK_CHUNK sub-blocks
+    at a time (the reference's batch size, so each batch's reductions see the same shapes)."""
+    S = x_subs.shape[0]
+    dh = dhs.reshape(S, SUBBLOCK_SIZE)
+    parts = [_lut_pick_torch(x_subs[i: i + LUT_PICK_CHUNK], dh[i: i + LUT_PICK_CHUNK], lut_val, inv_step, half_b)
+             for i in range(0, S, LUT_PICK_CHUNK)]
+    if not parts:
+        return torch.empty((0, SUBBLOCK_SIZE), dtype=torch.float32, device=x_subs.device)
+    return torch.cat(parts, dim=0)
+
+
+def _fp16_scale(v: torch.Tensor) -> torch.Tensor:
+    """A block scale as stored: rounded to fp16, back in fp32, at least 1e-8."""
+    return v.to(torch.float16).float().clamp(min=1e-8)
 
 
 @torch.no_grad()
 def quantize_liqk_v2_diag_rot(W_rot: torch.Tensor, diag_h: torch.Tensor, spec_name: str) -> torch.Tensor:
-    """The DP profile's diagonal quantization in the rotated basis (src/liqk_v2.py:469-506): per 256-block scale
-    d = fp16(max|w| / max_g), then LIQK_PROFILE_ITERS (default 2) rounds of sub-block quantization through the bank's
-    1-D table (the lut_subs_quant kernel for 64-column tables unless LIQK_PROFILE_CUDA=0, else the torch path) and the
-    weighted least-squares refit of d.  Returns d * G [M, K]."""
+    """The DP profile's diagonal quantization in the rotated basis (src/liqk_v2.py:469-506), on the device.
+
+    Per 256-column block b of row m: scale d = fp16(max |w| / max_grid); then LIQK_PROFILE_ITERS rounds (default 2)
+    of (a) the table pick of every 16-weight sub-block of w / d with the Hessian diagonal as weights — the
+    lut_subs_quant kernel for 64-column tables (unless LIQK_PROFILE_CUDA=0), the torch pick otherwise — and (b) the
+    weighted least-squares refit d = fp16(sum(h w q) / max(sum(h q q), 1e-12)).  Returns d * q [M, K]."""
     _lib.require_cuda(W_rot, diag_h)
-    device = W_rot.device
     M, K = W_rot.shape
-    nblocks = K // QK_K
-    bank = get_warp_register_bank(spec_name, device)
-    lut_val = bank["lut_val"]
-    max_g = bank["max_grid"]
+    nblk = M * (K // QK_K)
+    bank = get_warp_register_bank(spec_name, W_rot.device)
+    table, max_g = bank["lut_val"], bank["max_grid"]
     inv_step = (N_LUT_BUCKETS - 1) / (2.0 * max_g)
     half_b = (N_LUT_BUCKETS - 1) * 0.5
-    w_blks = W_rot.float().contiguous().view(M * nblocks, QK_K)
-    dh_blks = diag_h.float().view(1, nblocks, QK_K).expand(M, nblocks, QK_K).reshape(M * nblocks, QK_K).contiguous()
-    B_tot = M * nblocks
-    S_tot = B_tot * NUM_SUBBLOCKS
-    d_cur = (w_blks.abs().amax(dim=1) / max_g).to(torch.float16).to(torch.float32).clamp(min=1e-8)
-    dhs = dh_blks.view(S_tot, SUBBLOCK_SIZE, 1)
-    G_blk = None
-    for _ in range(int(os.environ.get("LIQK_PROFILE_ITERS", "2"))):
-        x_subs = (w_blks / d_cur.unsqueeze(1)).view(S_tot, SUBBLOCK_SIZE)
-        if lut_val.shape[1] == 64 and os.environ.get("LIQK_PROFILE_CUDA", "1") == "1":
+    use_kernel = table.shape[1] == 64 and os.environ.get("LIQK_PROFILE_CUDA", "1") == "1"
+    rounds = int(os.environ.get("LIQK_PROFILE_ITERS", "2"))
+
+    w = W_rot.float().reshape(nblk, QK_K).contiguous()
+    # the Hessian diagonal repeated for every row: [nblk, 256] (materialised: the pick reads it per sub-block)
+    h = diag_h.float().view(1, K // QK_K, QK_K).expand(M, -1, -1).reshape(nblk, QK_K).contiguous()
+    d = _fp16_scale(w.abs().amax(dim=1) / max_g)
+    q = None
+    for _ in range(rounds):
+        x = (w / d[:, None]).reshape(-1, SUBBLOCK_SIZE)
+        hs = h.view(-1, SUBBLOCK_SIZE)
+        if use_kernel:
             from .tcq_proto import lut_subs_quant_cuda
-            G_blk = lut_subs_quant_cuda(x_subs, dh_blks.view(S_tot, SUBBLOCK_SIZE), lut_val, inv_step,
-                                        half_b).view(B_tot, QK_K)
+            q = lut_subs_quant_cuda(x, hs, table, inv_step, half_b)
         else:
-            G_blk = quantize_subs_lut_chunked(x_subs, dhs, lut_val, inv_step, half_b).view(B_tot, QK_K)
-        num = (dh_blks * w_blks * G_blk).sum(dim=1)
-        den = (dh_blks * G_blk * G_blk).sum(dim=1).clamp(min=1e-12)
-        d_cur = (num / den).to(torch.float16).to(torch.float32).clamp(min=1e-8)
-    return (d_cur.unsqueeze(1) * G_blk).view(M, K)
+            q = quantize_subs_lut_chunked(x, hs, table, inv_step, half_b)
+        q = q.view(nblk, QK_K)
+        # the reference's products in its order: (h w) q and (h q) q
+        d = _fp16_scale((h * w * q).sum(dim=1) / (h * q * q).sum(dim=1).clamp(min=1e-12))
+    return (d[:, None] * q).view(M, K)
 
 
 @torch.no_grad()
@@ -428,6 +443,18 @@ def _rows_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: torch.Tensor, d
     return _drive(_rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name, fused, gemm))
 
 
+def _scale_fit_reference(W_rot: torch.Tensor, cfg: dict):
+    """The row-scale fit as the reference computes it with torch (src/liqk_v2.py:938-946): block RMS, fp16 geometric
+    mean per row, 5-bit exponents; returns (d_row fp32 [M], e int8 [M, K/256], d_rb fp32 [M, K/256])."""
+    M, K = W_rot.shape
+    rms_rb = W_rot.float().view(M, K // QK_K, QK_K).square().mean(dim=2).sqrt().clamp(min=1e-10) * cfg.get("scale", 1.0)
+    d_row = torch.exp(torch.log(rms_rb).mean(dim=1)).to(torch.float16).to(torch.float32).clamp(min=1e-8)
+    e_step, e_max = cfg.get("e_step", 0.25), 1 << (cfg.get("e_bits", 5) - 1)
+    e_rb = torch.round(torch.log2(rms_rb / d_row.unsqueeze(1)) / e_step).clamp(-e_max, e_max - 1)
+    d_rb = d_row.unsqueeze(1) * torch.exp2(e_step * e_rb)
+    return d_row, e_rb.to(torch.int8), d_rb.contiguous()
+
+
 def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool = True, gemm: str = "fp32",
                      U_parts: Optional[tuple] = None):
     """_rows_ldlq as a generator that yields after each 256-column block's launches (for interleaved issue).
@@ -450,11 +477,14 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
 
     # d(row, block) = d_row * 2^(0.25 e), e 5-bit in [-16, 15]; d_row fp16 = geometric mean of the row's block rms
     e_step, e_bits = cfg.get("e_step", 0.25), cfg.get("e_bits", 5)
-    d_row = torch.empty(M, dtype=torch.float32, device=device)
-    e_rb = torch.empty((M, nblocks), dtype=torch.int8, device=device)
-    d_rb_all = torch.empty((M, nblocks), dtype=torch.float32, device=device)
-    _check(L.ltq_scale_fit(ptr(W_work), W_work.stride(0), M, K, float(cfg.get("scale", 1.0)), float(e_step), int(e_bits),
-                           None, ptr(d_row), ptr(e_rb), ptr(d_rb_all), st), "ltq_scale_fit")
+    if gemm == "fp32":  # the reference's own expressions (src/liqk_v2.py:938-946): its reduction order, its bits
+        d_row, e_rb, d_rb_all = _scale_fit_reference(W_work, cfg)
+    else:
+        d_row = torch.empty(M, dtype=torch.float32, device=device)
+        e_rb = torch.empty((M, nblocks), dtype=torch.int8, device=device)
+        d_rb_all = torch.empty((M, nblocks), dtype=torch.float32, device=device)
+        _check(L.ltq_scale_fit(ptr(W_work), W_work.stride(0), M, K, float(cfg.get("scale", 1.0)), float(e_step),
+                               int(e_bits), None, ptr(d_row), ptr(e_rb), ptr(d_rb_all), st), "ltq_scale_fit")
     group = {"spec": spec_name, "d_row": d_row, "e": e_rb, "idx": idx, "gi": gi, "G": G}
 
     Uc = U.contiguous()

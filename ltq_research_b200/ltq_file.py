@@ -12,6 +12,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import os
 import struct
 from pathlib import Path
 from typing import Dict, List, Optional
@@ -23,12 +24,20 @@ from . import _lib
 from ._lib import ptr
 from .formats import TILE, LtqFormat
 
+# File layout (the .ltq container read by the reference and by lumen-format):
+#   bytes 0..3   b"LTQ\0"
+#   bytes 4..7   u32 container version (1), little endian
+#   bytes 8..15  u64 H = length of the JSON header area, little endian
+#   16 .. 16+H   UTF-8 JSON header, space-padded to H bytes; its "tensors" maps a name to {dtype, shape, offset}
+#   16+H ..      data area (16 + H is a multiple of 4096); each tensor starts at a multiple of 64 bytes of it
 MAGIC = b"LTQ\0"
 VERSION = 1
-DTYPES = {"f32": (np.float32, torch.float32), "f16": (np.float16, torch.float16), "bf16": (np.uint16, torch.bfloat16),
-          "i32": (np.int32, torch.int32), "i8": (np.int8, torch.int8), "u8": (np.uint8, torch.uint8)}
-TORCH_TO_LTQ = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16", torch.int32: "i32", torch.int8: "i8",
-                torch.uint8: "u8"}
+DATA_ALIGN = 64
+PAGE = 4096
+# element type names of the header and their torch types (the container's dtype vocabulary)
+LTQ_DTYPES = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16, "i32": torch.int32,
+              "i8": torch.int8, "u8": torch.uint8}
+_DTYPE_NAME = {v: k for k, v in LTQ_DTYPES.items()}
 FRAC_NAMES = ["none", "d2", "d4"]
 
 
@@ -230,122 +239,191 @@ def pack_matrix_device(m: dict, formats: Dict[str, LtqFormat], verify: bool = Tr
     return buf[:off], rows, bad
 
 
+def _host_bytes(t: torch.Tensor) -> np.ndarray:
+    """The little-endian bytes of a tensor's elements in row-major order, as a uint8 host array (any element type,
+    bf16 included: the tensor is reinterpreted, not converted)."""
+    t = t.detach()
+    if t.dtype not in _DTYPE_NAME:
+        raise TypeError(f"no .ltq element type for {t.dtype}")
+    return t.contiguous().reshape(-1).view(torch.uint8).cpu().numpy()
+
+
 class LtqWriter:
-    """Writes data straight to the file: `reserve` bytes are reserved for the header (data starts at 16 + reserve, a
-    multiple of 4096); `finalize` writes the header, space-padded to the same length (src/ltq_file.py:163-223)."""
+    """Streams an .ltq container to `path`.
+
+    The first 16 + `reserve` bytes are the preamble and the header area, filled in by `finalize` (the header JSON is
+    only complete once every tensor is placed); tensors go to the data area as they arrive, each at the next multiple
+    of 64 bytes, by positioned writes (the gaps are file holes and read as zeros).  `add_matrix` takes a quantized
+    matrix (liqk_v2.PACK["matrix"] fields on the device), packs its row slices on the device and checks them there
+    before any byte is written.  Usable as a context manager; leaving the block without `finalize` closes the file
+    with the header area still blank."""
 
     def __init__(self, path: Path, formats: List[LtqFormat], reserve: int = (64 << 20) - 16):
-        assert (16 + reserve) % 4096 == 0
-        self.path, self.reserve = Path(path), reserve
-        self.formats = formats
-        self.fmt_index = {f.name: i for i, f in enumerate(formats)}
-        self.f = open(self.path, "wb")
-        self.f.write(bytes(16 + reserve))
-        self.cur = 0
-        self.tensors = {}
-        self.quantized = []
+        if (16 + reserve) % PAGE:
+            raise ValueError(f"reserve + 16 must be a multiple of {PAGE} (the data area starts on a page)")
+        self.path = Path(path)
+        self.reserve = int(reserve)
+        self.formats = list(formats)
+        self.fmt_index = {f.name: k for k, f in enumerate(self.formats)}
+        self.tensors: Dict[str, dict] = {}
+        self.quantized: List[str] = []
+        self._data_start = 16 + self.reserve
+        self._end = 0  # bytes of the data area used so far
+        self._fd = os.open(self.path, os.O_RDWR | os.O_CREAT | os.O_TRUNC, 0o644)
+        os.ftruncate(self._fd, self._data_start)
 
-    def _write(self, name: str, raw: bytes, dtype: str, shape: list, align: int = 64):
-        pad = _align(self.cur, align) - self.cur
-        if pad:
-            self.f.write(bytes(pad))
-            self.cur += pad
-        self.tensors[name] = {"dtype": dtype, "shape": [int(s) for s in shape], "offset": self.cur}
-        self.f.write(raw)
-        self.cur += len(raw)
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def close(self):
+        if self._fd is not None:
+            os.close(self._fd)
+            self._fd = None
+
+    def _put(self, name: str, payload: np.ndarray, dtype: str, shape) -> int:
+        """Places `payload` (uint8) at the next aligned offset of the data area and records it; returns the offset."""
+        if name in self.tensors:
+            raise KeyError(f"tensor {name} written twice")
+        off = _align(self._end, DATA_ALIGN)
+        view = memoryview(np.ascontiguousarray(payload, dtype=np.uint8))
+        done = 0
+        while done < len(view):
+            done += os.pwrite(self._fd, view[done:], self._data_start + off + done)
+        self._end = off + len(view)
+        self.tensors[name] = {"dtype": dtype, "shape": [int(d) for d in shape], "offset": off}
+        return off
 
     def add_tensor(self, name: str, t: torch.Tensor):
-        t = t.detach().cpu().contiguous()
-        dt = TORCH_TO_LTQ[t.dtype]
-        raw = t.view(torch.int16).numpy().tobytes() if t.dtype == torch.bfloat16 else t.numpy().tobytes()
-        self._write(name, raw, dt, list(t.shape))
+        """A plain tensor (f32 / f16 / bf16 / i32 / i8 / u8), copied to the host as its raw element bytes."""
+        self._put(name, _host_bytes(t), _DTYPE_NAME[t.dtype], tuple(t.shape))
 
     def add_matrix(self, p: str, m: dict, verify: bool = True) -> int:
-        """Matrix from liqk_v2.PACK["matrix"]; returns the byte size of its fields.  verify: the spec decode of each
-        slice from the packed bytes must match the quantizer's tile values bit for bit (checked on the device)."""
+        """The five tensors of quantized matrix `p` (`{p}.ltq.slices` [n, 4] i32 rows [r0, r1, format, offset],
+        `.data` the packed slices, `.d_row` f16, `.e` i8, `.suh` f16); returns their total bytes.  With verify the spec
+        decode of every packed slice must reproduce the quantizer's tile values bit for bit (checked on the device)."""
         M, K = m["idx"].shape
-        fmts = {f.name: f for f in self.formats}
-        used = {sp: fmts[sp] for _, _, sp in m["row_slices"]}
+        used: Dict[str, LtqFormat] = {}
+        for _, _, spec in m["row_slices"]:
+            if spec not in self.fmt_index:
+                raise KeyError(f"{p}: format {spec} is not among the writer's formats")
+            used.setdefault(spec, self.formats[self.fmt_index[spec]])
         data, rows, bad = pack_matrix_device(m, used, verify)
-        if verify and int(bad.item()):
-            raise RuntimeError(f"{p}: decode disagrees with the quantizer in {int(bad.item())} weights")
-        rows = [[r0, r1, self.fmt_index[list(used)[fi]], o] for r0, r1, fi, o in rows]
-        self.add_tensor(f"{p}.ltq.slices", torch.tensor(rows, dtype=torch.int32))
-        self._write(f"{p}.ltq.data", data.cpu().numpy().tobytes(), "u8", [int(data.numel())])
-        self.add_tensor(f"{p}.ltq.d_row", m["d_row"].to(torch.float16))
-        self.add_tensor(f"{p}.ltq.e", m["e"].to(torch.int8))
-        self.add_tensor(f"{p}.ltq.suh", m["suh"].to(torch.float16))
+        if verify:
+            n_bad = int(bad.item())
+            if n_bad:
+                raise RuntimeError(f"{p}: decode disagrees with the quantizer in {n_bad} weights")
+        local = list(used)
+        table = torch.tensor([[r0, r1, self.fmt_index[local[fi]], o] for r0, r1, fi, o in rows], dtype=torch.int32)
+        fields = [("slices", table), ("data", data), ("d_row", m["d_row"].to(torch.float16)),
+                  ("e", m["e"].to(torch.int8)), ("suh", m["suh"].to(torch.float16))]
+        total = 0
+        for key, t in fields:
+            self.add_tensor(f"{p}.ltq.{key}", t)
+            total += t.numel() * t.element_size()
         self.quantized.append(p)
-        return int(data.numel()) + 16 * len(rows) + 2 * M + M * (K // TILE) + 2 * K
+        return total
 
     def finalize(self, header: dict):
-        header = dict(header, tensors=self.tensors)
-        raw = json.dumps(header, ensure_ascii=False, separators=(",", ":")).encode("utf-8")
-        assert len(raw) <= self.reserve, f"header of {len(raw)} B does not fit in the {self.reserve} B reserve"
-        self.f.seek(0)
-        self.f.write(MAGIC + struct.pack("<IQ", VERSION, self.reserve) + raw + b" " * (self.reserve - len(raw)))
-        self.f.close()
+        """Writes the preamble and the header (the caller's fields plus "tensors") and closes the file."""
+        blob = json.dumps(dict(header, tensors=self.tensors), ensure_ascii=False, separators=(",", ":")).encode("utf-8")
+        if len(blob) > self.reserve:
+            raise ValueError(f"header of {len(blob)} bytes does not fit the {self.reserve}-byte header area")
+        pre = MAGIC + struct.pack("<IQ", VERSION, self.reserve)
+        os.pwrite(self._fd, pre + blob.ljust(self.reserve, b" "), 0)
+        self.close()
 
 
 class LtqFile:
-    """Reader (src/ltq_file.py:245-277)."""
+    """Read access to an .ltq container: the header, each tensor's bytes (memory-mapped), tensors, and the quantized
+    matrices decoded (or multiplied with a vector) on the device from their packed tiles."""
 
     def __init__(self, path: Path):
-        with open(path, "rb") as f:
-            magic, (ver, H) = f.read(4), struct.unpack("<IQ", f.read(12))
-            assert magic == MAGIC and ver == VERSION, (magic, ver)
-            self.header = json.loads(f.read(H).decode("utf-8"))
-        self.data_off = 16 + H
-        assert self.data_off % 4096 == 0
-        self.mm = np.memmap(path, dtype=np.uint8, mode="r")
+        self.path = Path(path)
+        with open(self.path, "rb") as fh:
+            pre = fh.read(16)
+            if len(pre) < 16 or pre[:4] != MAGIC:
+                raise ValueError(f"{self.path}: not an .ltq file")
+            version, hlen = struct.unpack("<IQ", pre[4:])
+            if version != VERSION:
+                raise ValueError(f"{self.path}: container version {version}, expected {VERSION}")
+            self.header = json.loads(fh.read(hlen).decode("utf-8"))
+        self.data_off = 16 + hlen
+        if self.data_off % PAGE:
+            raise ValueError(f"{self.path}: the data area starts at {self.data_off}, not on a {PAGE}-byte page")
+        self.mm = np.memmap(self.path, dtype=np.uint8, mode="r")
         self.formats = [format_from_json(d) for d in self.header["quantization"]["formats"]]
 
+    def _entry(self, name: str):
+        e = self.header["tensors"][name]
+        dt = LTQ_DTYPES[e["dtype"]]
+        count = 1
+        for d in e["shape"]:
+            count *= int(d)
+        return e, dt, count * torch.empty((), dtype=dt).element_size()
+
     def raw(self, name: str) -> memoryview:
-        t = self.header["tensors"][name]
-        n = int(np.prod(t["shape"])) * np.dtype(DTYPES[t["dtype"]][0]).itemsize
-        o = self.data_off + t["offset"]
-        return memoryview(self.mm[o: o + n])
+        """The tensor's bytes in the file (no copy)."""
+        e, _, nbytes = self._entry(name)
+        o = self.data_off + e["offset"]
+        return memoryview(self.mm[o: o + nbytes])
 
     def tensor(self, name: str) -> torch.Tensor:
-        t = self.header["tensors"][name]
-        np_dt, th_dt = DTYPES[t["dtype"]]
-        arr = torch.from_numpy(np.frombuffer(self.raw(name), dtype=np_dt).copy()).reshape(t["shape"])
-        return arr.view(torch.bfloat16) if t["dtype"] == "bf16" else arr
+        """The tensor as a host torch tensor of its stored element type and shape."""
+        e, dt, nbytes = self._entry(name)
+        if nbytes == 0:
+            return torch.empty(e["shape"], dtype=dt)
+        return torch.frombuffer(bytearray(self.raw(name)), dtype=dt).reshape(e["shape"])
+
+    def matrices(self) -> List[str]:
+        """Names of the quantized matrices in the file, in data order."""
+        tail = ".ltq.data"
+        found = [(e["offset"], k[: -len(tail)]) for k, e in self.header["tensors"].items() if k.endswith(tail)]
+        return [k for _, k in sorted(found)]
+
+    def _device_fields(self, p: str, device):
+        d_row, e, suh = (self.tensor(f"{p}.ltq.{k}").to(device) for k in ("d_row", "e", "suh"))
+        raw = self.tensor(f"{p}.ltq.data")
+        data = torch.zeros(_align(max(raw.numel(), 1), DATA_ALIGN), dtype=torch.uint8, device=device)
+        data[: raw.numel()].copy_(raw)
+        return data, self.tensor(f"{p}.ltq.slices").tolist(), d_row, e, suh
 
     def decode_matrix(self, p: str, device="cuda") -> torch.Tensor:
-        """Matrix W [M, K] float32, as reconstructed by the engine (spec decode on the device)."""
-        d_row, e, suh = (self.tensor(f"{p}.ltq.{k}").to(device) for k in ("d_row", "e", "suh"))
+        """Matrix `p` [M, K] fp32 as an inference engine rebuilds it: spec decode of every slice on the device, block
+        scales, inverse rotation, column scales."""
+        data, slices, d_row, e, suh = self._device_fields(p, device)
         M, K = d_row.shape[0], suh.shape[0]
-        raw = np.frombuffer(self.raw(f"{p}.ltq.data"), dtype=np.uint8)
-        data = torch.empty(_align(max(raw.size, 1), 64), dtype=torch.uint8, device=device)
-        data[: raw.size].copy_(torch.from_numpy(raw.copy()))
         G = torch.empty((M, K), device=device)
-        for r0, r1, fi, off in self.tensor(f"{p}.ltq.slices").tolist():
+        for r0, r1, fi, off in slices:
             decode_slice_device(data[off:], r1 - r0, K, self.formats[fi], out=G[r0:r1])
         return assemble(G, d_row, e, suh)
 
     def matvec(self, p: str, x: torch.Tensor, device="cuda") -> torch.Tensor:
         """y = W x for matrix p, computed from its packed tiles on the device (ltq_matvec_slice)."""
-        d_row, e, suh = (self.tensor(f"{p}.ltq.{k}").to(device) for k in ("d_row", "e", "suh"))
-        raw = np.frombuffer(self.raw(f"{p}.ltq.data"), dtype=np.uint8)
-        data = torch.empty(_align(max(raw.size, 1), 64), dtype=torch.uint8, device=device)
-        data[: raw.size].copy_(torch.from_numpy(raw.copy()))
-        return matvec(data, self.tensor(f"{p}.ltq.slices"), self.formats, d_row, e, suh, x)
+        data, slices, d_row, e, suh = self._device_fields(p, device)
+        return matvec(data, slices, self.formats, d_row, e, suh, x)
 
 
-def main():
-    ap = argparse.ArgumentParser()
+def main(argv=None):
+    """`--check FILE`: reads the container, lists its size and formats, and rebuilds a spread of its matrices on the
+    device (finite values, RMS)."""
+    ap = argparse.ArgumentParser(description="inspect an .ltq file")
     ap.add_argument("--check", type=Path, required=True)
-    ap.add_argument("--n", type=int, default=4, help="how many matrices to decode in full")
-    args = ap.parse_args()
-    lf = LtqFile(args.check)
-    q = lf.header["quantization"]
-    print(f"{args.check}: {args.check.stat().st_size / 1e9:.2f} GB, tensors {len(lf.header['tensors'])}, formats "
-          f"{len(q['formats'])}, bits/weight {q.get('bits_per_weight')}")
-    names = sorted({k[: -len(".ltq.data")] for k in lf.header["tensors"] if k.endswith(".ltq.data")})
-    for p in names[:: max(1, len(names) // args.n)][: args.n]:
+    ap.add_argument("--n", type=int, default=4, help="number of matrices to rebuild")
+    a = ap.parse_args(argv)
+    lf = LtqFile(a.check)
+    quant = lf.header["quantization"]
+    names = lf.matrices()
+    size_gb = a.check.stat().st_size / 1e9
+    print(f"{a.check}: {size_gb:.2f} GB; {len(lf.header['tensors'])} tensors, {len(names)} quantized matrices; formats "
+          f"{', '.join(f.name for f in lf.formats)}; bits/weight {quant.get('bits_per_weight')}")
+    step = max(1, len(names) // max(a.n, 1))
+    for p in names[::step][: a.n]:
         W = lf.decode_matrix(p)
-        print(f"{p}: {tuple(W.shape)}, rms {W.square().mean().sqrt():.4g}, finite {bool(torch.isfinite(W).all())}")
+        rms = float(W.double().square().mean().sqrt())
+        print(f"  {p}: {list(W.shape)}  rms {rms:.4g}  all finite: {bool(torch.isfinite(W).all())}")
 
 
 if __name__ == "__main__":

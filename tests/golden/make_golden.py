@@ -16,17 +16,16 @@ run it.  Fixtures written next to this file:
 from __future__ import annotations
 
 import json
-import os
 import sys
 from pathlib import Path
 
 import numpy as np
 
 OUT = Path(__file__).resolve().parent
-REF = Path(os.environ.get("LTQ_REF_ROOT", "/root/reference"))
-os.environ.setdefault("TCQ_NO_COMPILE", "1")
-sys.dont_write_bytecode = True
-sys.path.insert(0, str(REF))
+sys.path.insert(0, str(OUT.parent.parent))
+from oracle.refroot import import_reference  # noqa: E402
+
+REF = import_reference()  # the tree named by LTQ_REF_ROOT, else the install in baseline/_ref
 
 import torch  # noqa: E402
 

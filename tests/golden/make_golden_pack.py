@@ -7,7 +7,6 @@ TCQ_CONFIG (fractional modes none / D2 / D4) and slice shapes with several row g
 from __future__ import annotations
 
 import json
-import os
 import sys
 from pathlib import Path
 
@@ -15,10 +14,10 @@ import numpy as np
 
 OUT = Path(__file__).resolve().parent
 ROOT = OUT.parent.parent
-REF = Path(os.environ.get("LTQ_REF_ROOT", "/root/reference"))
-sys.dont_write_bytecode = True
-sys.path.insert(0, str(REF))
-sys.path.insert(1, str(ROOT))
+sys.path.insert(0, str(ROOT))
+from oracle.refroot import import_reference  # noqa: E402
+
+REF = import_reference()  # the tree named by LTQ_REF_ROOT, else the install in baseline/_ref
 
 import torch  # noqa: E402
 

@@ -15,15 +15,16 @@ CASES = [
 ]
 
 
-def synth(M: int, K: int, seed: int):
-    g = torch.Generator().manual_seed(seed)
-    z = torch.randn(M, K, generator=g)
-    chi2 = torch.randn(M, K, 5, generator=g).square().sum(-1)   # Student-t(5) = N(0,1) / sqrt(chi2_5 / 5)
+def synth(M: int, K: int, seed: int, device="cpu"):
+    """(W bf16 [M, K], H fp32 [K, K]) from a generator on `device` (the values depend on the device's generator)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    z = torch.randn(M, K, generator=g, device=device)
+    chi2 = torch.randn(M, K, 5, generator=g, device=device).square().sum(-1)   # Student-t(5) = N(0,1) / sqrt(chi2_5 / 5)
     W = z / (chi2 / 5).sqrt() * 0.02
     n_out = max(1, int(round(0.005 * K)))
-    cols = torch.randperm(K, generator=g)[:n_out]
+    cols = torch.randperm(K, generator=g, device=device)[:n_out]
     W[:, cols] *= 20
     W = W.to(torch.bfloat16)
-    X = torch.randn(4 * K, K, generator=g) * torch.exp(torch.randn(1, K, generator=g))
+    X = torch.randn(4 * K, K, generator=g, device=device) * torch.exp(torch.randn(1, K, generator=g, device=device))
     H = (X.T @ X) / X.shape[0]
     return W, H

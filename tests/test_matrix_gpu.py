@@ -180,15 +180,19 @@ def test_quantize_matrix_vs_reference_run(case, cuda_dev, monkeypatch):
 
 
 def test_make_gains_cpu_vs_cuda(cuda_dev):
-    """Informative: the gain tables evaluated on CPU and on the B200 (the format stores whichever the quantizer used)."""
+    """The gain tables 2^((g - (G - 1) / 2) step) evaluated by torch on the CPU and on the B200 (the format stores
+    whichever the quantizer used): each within 2 ulp of the float64 value, and the two within 2 ulp of each other."""
     from ltq_research_b200.tcq_proto import make_gains
-    diff = 0
+    ulp = 2.0 ** -23
     for name in VC.MENU:
         c = VC.F[name]
-        a = make_gains(c["h"], c["step"], "cpu")
-        b = make_gains(c["h"], c["step"], cuda_dev).cpu()
-        diff += int((a != b).sum())
-    assert diff >= 0
+        G = 1 << c["h"]
+        exact = torch.tensor([2.0 ** ((g - (G - 1) / 2) * c["step"]) for g in range(G)], dtype=torch.float64)
+        a = make_gains(c["h"], c["step"], "cpu").double()
+        b = make_gains(c["h"], c["step"], cuda_dev).cpu().double()
+        for t in (a, b):
+            assert ((t - exact).abs() <= 2 * ulp * exact).all(), (name, t, exact)
+        assert ((a - b).abs() <= 2 * ulp * exact).all(), (name, a, b)
 
 
 def _ldlq_inputs(M, K, seed, dev, damp=0.2):

@@ -78,11 +78,37 @@ def test_quantize_rings_on_oracle_viterbi(cuda_dev, monkeypatch):
     assert torch.equal(got, want)
 
 
-def test_int8_rows(cuda_dev):
-    from ltq_research_b200.rings import int8_rows
-    W = _table(32, 512, 11)
-    got, bpv = int8_rows(W)
-    x = W.view(-1, 256).float()
+def _int8_reference(W):
+    """src/ple_quant.py:68-77 restated: fp16 absmax scale per ring, round half to even, clamp, rescale (torch, CPU)."""
+    x = W.reshape(-1, 256).float()
     d = (x.abs().amax(dim=1, keepdim=True) / 127).half().float().clamp(min=1e-10)
-    want = ((x / d).round().clamp(-127, 127) * d).to(W.dtype).view_as(W)
-    assert torch.equal(got, want) and bpv == 8 + 16 / 256
+    return ((x / d).round().clamp(-127, 127) * d).to(W.dtype).view_as(W)
+
+
+def _same(a, b):
+    """Equal values, NaN where NaN (bit patterns of NaN aside)."""
+    an, bn = torch.isnan(a.float()), torch.isnan(b.float())
+    return torch.equal(an, bn) and torch.equal(a[~an], b[~bn])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_int8_rows(cuda_dev, dtype):
+    """ltq_int8_rings (one warp per ring) against the reference's torch expression: a seeded table, plus rings of
+    zeros, exact half-steps (ties to even), a NaN, an infinity and values beyond fp16's range."""
+    from ltq_research_b200.rings import int8_rows
+    W = _table(32, 512, 11).to(dtype)
+    got, bpv = int8_rows(W)
+    assert got.dtype == W.dtype and got.device == W.device and bpv == 8 + 16 / 256
+    assert torch.equal(got, _int8_reference(W))
+    S = torch.zeros(6, 256, dtype=torch.float32)
+    S[1] = (torch.arange(256) % 200 - 100) + 0.5  # max |x| = 127 below gives d = 1: x / d = k + 0.5, ties to even
+    S[1, 0] = 127.0
+    S[2] = torch.randn(256, generator=torch.Generator().manual_seed(3))
+    S[2, 5] = float("nan")
+    S[3] = torch.randn(256, generator=torch.Generator().manual_seed(4))
+    S[3, 9] = float("inf")
+    S[4] = torch.randn(256, generator=torch.Generator().manual_seed(5)) * 1e7   # max / 127 above fp16's range
+    S[5] = torch.randn(256, generator=torch.Generator().manual_seed(6)) * 1e-12  # scale clamped to 1e-10
+    S = S.to(dtype)
+    got, _ = int8_rows(S.to(cuda_dev))
+    assert _same(got.cpu(), _int8_reference(S))
