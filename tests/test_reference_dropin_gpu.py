@@ -16,9 +16,9 @@ would rebind it.
   1024 x 3072 TCQ25X, seeded inputs with the config's distributions) with the reference kernel and with
   libltq_b200.so as its Viterbi: identical .ltq fields (codes, gain indices, tile values, d_row, e, suh), W_hat and loss.
 * This package's own pipeline against that reference run, same inputs, same GPU: gemm "fp32" (quantize_matrix_liqk_v2)
-  and the benched fast mode (batch.quantize_matrices, bf16x6 tensor-core products).  The statistics (code agreement,
-  per-tile-group weighted MSE relative differences, rel_loss) go to $LTQ_REPORT_DIR/parity_<case>.json when that
-  variable is set; the bounds asserted are written in the test.
+  bit for bit; the benched fast mode (batch.quantize_matrices, bf16x6 tensor-core products) within the bounds written
+  in its test.  The statistics (code agreement, per-tile-group H-weighted error relative differences, rel_loss) go to
+  $LTQ_REPORT_DIR/parity_<case>.json when that variable is set.
 """
 from __future__ import annotations
 
@@ -39,7 +39,9 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(reference_root() is None or not ref_kernel.available(),
                                  reason="reference install (baseline/_ref) or reference kernel (oracle/_ref) missing")]
 
-CONFIG2 = [("q3072x3072_TCQ3X", 3072, 3072, "TCQ3X", 11), ("k1024x3072_TCQ25X", 1024, 3072, "TCQ25X", 12)]
+# the four distinct matrix shapes of the config-2 layer (q / o, k / v, gate / up, down), both formats of the bench
+CONFIG2 = [("q3072x3072_TCQ3X", 3072, 3072, "TCQ3X", 11), ("k1024x3072_TCQ25X", 1024, 3072, "TCQ25X", 12),
+           ("gate8192x3072_TCQ25X", 8192, 3072, "TCQ25X", 13), ("down3072x8192_TCQ3X", 3072, 8192, "TCQ3X", 14)]
 
 
 @pytest.fixture(scope="module")
@@ -183,9 +185,10 @@ def _compare(name, mode, W, H, ref_pm, ref_wh, ref_rel, pm, w_hat, rel) -> dict:
 
 @pytest.mark.parametrize("case", [c[0] for c in CONFIG2])
 def test_fp32_pipeline_against_reference_run(ref_runs, case):
-    """gemm "fp32": the reference's torch operations everywhere except the Viterbi and the fused LDLQ block kernel
-    (whose intra-block feedback is sequential fma chains).  Bounds: rel_loss within 0.5 % of the reference run's, the
-    mean H-weighted error of the tile groups within 0.5 %, d_row / e / suh of the unrefined scale fit all equal."""
+    """gemm "fp32" — the reference's torch operations for the rotation statistics, factorisation, scale fit, inter-block
+    update and refits; this package's kernels for the FWHT, the Viterbi and the fused LDLQ block (intra-block feedback
+    as sequential fma chains): bit for bit the reference run on the same GPU — every .ltq field, W_hat, the loss, so
+    every tile group's H-weighted error is equal (relative difference 0, within north_star's 1e-6)."""
     import ltq_research_b200.liqk_v2 as L
     W, H, spec, (pm0, wh0, rel0) = ref_runs[case]
     L.PACK = {}
@@ -195,18 +198,27 @@ def test_fp32_pipeline_against_reference_run(ref_runs, case):
     finally:
         L.PACK = None
     s = _compare(case, "fp32", W, H, pm0, wh0, rel0, pm, w_hat, rel)
-    assert s["e_equal"] == 1.0, s
-    assert s["rel_loss_rel_diff"] < 5e-3, s
-    assert s["tile_group_wmse_mean_rel_diff"] < 5e-3, s
+    for k in ("idx", "gi", "G", "d_row", "e", "suh"):
+        a, b = pm0[k], pm[k]
+        assert torch.equal(a.view(torch.int32) if a.dtype == torch.float32 else a,
+                           b.view(torch.int32) if b.dtype == torch.float32 else b), (k, s)
+    assert torch.equal(w_hat.view(torch.int32), wh0.view(torch.int32)) and rel == rel0, s
+    assert s["tile_group_wmse_rel_diff"]["max"] == 0.0, s
 
 
 @pytest.mark.parametrize("case", [c[0] for c in CONFIG2])
 def test_fast_pipeline_against_reference_run(ref_runs, case):
-    """The benched mode (batch.quantize_matrices, bf16x6 tensor-core products, blocked Cholesky, scale-fit kernel):
-    rel_loss within 1 % of the reference run's, the mean H-weighted error of the tile groups within 1 %."""
+    """The benched mode (batch.quantize_matrices: bf16x6 tensor-core products accurate to fp32's error bound, blocked
+    tensor-core Cholesky, scale-fit kernel) against the reference run.  Its products round differently from cuBLAS's
+    fp32 GEMMs in the last bits; where that moves a Viterbi decision near a tie, the LDLQ feedback carries the change
+    along the row.  Bounds (measured on a B200: codes 99.6-100 % equal, rel_loss within 3.2e-6, 97.9-100 % of tile
+    groups' H-weighted error within 1e-6): codes >= 99 % equal, rel_loss within 1e-4 relative, the summed H-weighted
+    error of the tile groups within 1e-5, >= 95 % of tile groups within 1e-6 of the reference's."""
     from ltq_research_b200.batch import quantize_matrices
     W, H, spec, (pm0, wh0, rel0) = ref_runs[case]
     r = quantize_matrices([(W, H, spec)], keep_w_hat=True, gemm="bf16x6")[0]
     s = _compare(case, "bf16x6", W, H, pm0, wh0, rel0, r["pack"], r["W_hat"], r["rel_loss"])
-    assert s["rel_loss_rel_diff"] < 1e-2, s
-    assert s["tile_group_wmse_mean_rel_diff"] < 1e-2, s
+    assert s["codes_equal"] >= 0.99, s
+    assert s["rel_loss_rel_diff"] < 1e-4, s
+    assert s["tile_group_wmse_mean_rel_diff"] < 1e-5, s
+    assert s["tile_group_wmse_rel_diff"]["frac_within_1e-6"] >= 0.95, s
