@@ -437,12 +437,370 @@ def write_kernel_list(args, timed, fmts):
     print(head.strip(), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------
+# The other BASELINE configs (--workload): config 1 (the Gaussian Viterbi rig), config 3 (a Qwen3-8B-shaped model
+# sharded by whole matrices, strong scaling), config 4 (a Qwen3-30B-A3B-shaped MoE, every matrix's rows split across
+# the ranks), config 5 (a Gemma-style 262,144 x 2,560 embedding table as tail-biting rings, rows split across ranks).
+# ------------------------------------------------------------------------------------------------
+def synth_weight(M: int, K: int, seed: int, device) -> torch.Tensor:
+    """bf16 Student-t(5) * 0.02 [M, K] with 0.5 % of the input columns x 20 (the config-2 weight distribution)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    W = torch.randn(M, K, device=device, generator=g)
+    chi2 = torch.zeros(M, K, device=device)
+    for _ in range(5):
+        chi2.add_(torch.randn(M, K, device=device, generator=g).square_())
+    W.div_(chi2.div_(5.0).sqrt_()).mul_(0.02)
+    del chi2
+    W[:, torch.randperm(K, device=device, generator=g)[: max(1, round(0.005 * K))]] *= 20.0
+    return W.to(torch.bfloat16)
+
+
+def synth_hessian(K: int, rows: int, seed: int, device) -> torch.Tensor:
+    """H = X^T X / rows, X = N(0, 1) [rows, K] with log-normal(0, 1) per-channel scales (the config-2 Hessians)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    X = torch.randn(rows, K, device=device, generator=g) * torch.exp(torch.randn(1, K, device=device, generator=g))
+    return (X.T @ X) / float(rows)
+
+
+def qwen3_8b_matrices() -> list:
+    """The 252 matrices of config 3 as (name, M, K, format, Hessian key): 36 layers of q / k / v (sharing the
+    attention input's Hessian), o, gate / up (sharing the MLP input's) and down; formats cycle the 19-format TCQPQ menu
+    (K = 2..5, 8- and 16-subset labels, D2 and D4 parity, 32-weight gain groups)."""
+    from ltq_research_b200.formats import MENU_TCQPQ
+    shapes = [("q_proj", 4096, 4096, "attn"), ("k_proj", 1024, 4096, "attn"), ("v_proj", 1024, 4096, "attn"),
+              ("o_proj", 4096, 4096, "o"), ("gate_proj", 12288, 4096, "mlp"), ("up_proj", 12288, 4096, "mlp"),
+              ("down_proj", 4096, 12288, "down")]
+    return [(f"layers.{l}.{nm}", M, K, MENU_TCQPQ[(7 * l + j) % len(MENU_TCQPQ)], (l, hk))
+            for l in range(36) for j, (nm, M, K, hk) in enumerate(shapes)]
+
+
+def moe_layer_matrices(layer: int) -> list:
+    """Config 4, one Qwen3-30B-A3B-shaped layer as (name, M, K, format, Hessian key): attention q 4096 x 2048,
+    k / v 512 x 2048 (sharing the attention input's Hessian), o 2048 x 4096 at TCQ45X (4.5 bpw); 128 experts, each
+    gate_up 1536 x 2048 (gate and up fused, as the reference's MoE path stores them) and down 2048 x 768 with Hessians
+    of their own, at TCQ275X (2.75 bpw)."""
+    out = [(f"layers.{layer}.q_proj", 4096, 2048, "TCQ45X", (layer, "attn")),
+           (f"layers.{layer}.k_proj", 512, 2048, "TCQ45X", (layer, "attn")),
+           (f"layers.{layer}.v_proj", 512, 2048, "TCQ45X", (layer, "attn")),
+           (f"layers.{layer}.o_proj", 2048, 4096, "TCQ45X", (layer, "o"))]
+    for e in range(128):
+        out.append((f"layers.{layer}.experts.{e}.gate_up_proj", 1536, 2048, "TCQ275X", (layer, f"gu{e}")))
+        out.append((f"layers.{layer}.experts.{e}.down_proj", 2048, 768, "TCQ275X", (layer, f"dn{e}")))
+    return out
+
+
+def _seed_of(key) -> int:
+    """A stable seed from a matrix or Hessian key (independent of the rank that generates it)."""
+    import zlib
+    return zlib.crc32(repr(key).encode()) & 0x7FFFFFFF
+
+
+def _block_roofline(ev: list, t0) -> dict:
+    """The fused block kernel's live ACS rate over the launches in `ev` (BLOCK_EVENTS), timed from event t0."""
+    peak, sm_mhz = alu_peak_gacs()
+    if not ev:
+        return None
+    iv = [(t0.elapsed_time(a), t0.elapsed_time(b)) for a, b, _, _ in ev]
+    ms = union_ms(iv)
+    acs = sum(c for _, _, c, _ in ev)
+    ach = acs / (ms * 1e-3) / 1e9
+    return {"bound": "alu", "kernel": "ldlq_block_kernel (fused LDLQ block: Viterbi ACS)", "achieved": ach,
+            "peak": peak, "unit": "GACS/s", "frac": ach / peak, "traffic": None,
+            "basis": f"sum of the launches' add-compare-selects / union of their CUDA-event intervals ({ms:.1f} ms)",
+            "peak_basis": f"148 SMs x 128 issue slots/clk x {sm_mhz:.0f} MHz / {ALU_SLOTS_PER_ACS} slots per ACS"}
+
+
+def _timed(fn, barrier, local):
+    """Run fn() between barriers, timed by CUDA events on the current stream; returns (result, ms, clocks)."""
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        a.record()
+        r = fn()
+        b.record()
+        barrier()
+    return r, a.elapsed_time(b), clk.summary(), a
+
+
+def _max_over_ranks(dist, dev, *vals) -> list:
+    t = torch.tensor([float(v) for v in vals], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def run_matrix_model(args, rank, world, dev, dist, barrier, local):
+    """Config 3 (qwen3-8b) or 4 (qwen3-30b-a3b).  Inputs (W bf16, H fp32) are generated on the device from seeds of
+    their matrix / Hessian keys, so every rank makes exactly its own share.
+    qwen3-8b: the 252 matrices go to ranks whole (shard.assign, longest first), a step is the whole model, strong
+    scaling (same model at every N), no collective until one NCCL gather of the packed .ltq tensors to rank 0.
+    qwen3-30b-a3b: a step is one MoE layer (260 matrices); every matrix's rows are split across the ranks
+    (shard.row_ranges, 16-row units) with the whole H on every rank and five all-reduces of row sums per matrix
+    (shard.nccl_row_reduce), so every rank reaches the same suh; --steps layers are timed after --warmup layers."""
+    from ltq_research_b200 import _lib
+    import ltq_research_b200.liqk_v2 as Lq
+    from ltq_research_b200.batch import quantize_matrices
+    from ltq_research_b200.formats import MENU_TCQPQ, load_formats
+    from ltq_research_b200.shard import assign, gather_ltq, nccl_row_reduce, row_ranges
+    moe = args.workload == "qwen3-30b-a3b"
+    if moe:
+        warm_m = [m for l in range(args.warmup) for m in moe_layer_matrices(1000 + l)]
+        timed_m = [m for l in range(args.steps) for m in moe_layer_matrices(l)]
+        mine_w, mine_t = list(range(len(warm_m))), list(range(len(timed_m)))
+        rows = {M: row_ranges(M, world)[rank] for M in {m[1] for m in warm_m + timed_m}}
+        row_reduce = nccl_row_reduce() if world > 1 else None
+        fmts = load_formats(["TCQ45X", "TCQ275X"], dev)
+    else:
+        allm = qwen3_8b_matrices()
+        shard = assign([(M, K, sp) for _, M, K, sp, _ in allm], world)[rank]
+        timed_m, mine_t = allm, shard
+        # warm-up: this rank's first matrices, `--warmup` of them per format it will use (kernels, pools, handles)
+        seen, mine_w = {}, []
+        for i in shard:
+            if seen.get(allm[i][3], 0) < args.warmup:
+                seen[allm[i][3]] = seen.get(allm[i][3], 0) + 1
+                mine_w.append(i)
+        warm_m = allm
+        rows, row_reduce = None, None
+        fmts = load_formats(list(MENU_TCQPQ), dev)
+    damp = 0.02
+    hcache: dict = {}
+
+    def jobs_of(mats, idx):
+        out = []
+        for i in idx:
+            name, M, K, sp, hk = mats[i]
+            if hk not in hcache:
+                hcache[hk] = synth_hessian(K, 1024 if moe and hk[1][:2] in ("gu", "dn") else 4096, _seed_of(hk), dev)
+            W = synth_weight(M, K, _seed_of(name), dev)
+            if rows is not None:
+                r0, r1 = rows[M]
+                W = W[r0:r1].contiguous()
+            out.append((W, hcache[hk], sp))
+        return out
+
+    warm = jobs_of(warm_m, mine_w)
+    quantize_matrices(warm, damp=damp, n_streams=args.streams, ltq_formats=fmts, pack=False, row_reduce=row_reduce)
+    del warm
+    timed = jobs_of(timed_m, mine_t)
+    weights_total = sum(M * K for _, M, K, _, _ in (timed_m[i] for i in range(len(timed_m))))
+    weights_mine = sum(W.numel() for W, _, _ in timed)
+    barrier()
+    Lq.BLOCK_EVENTS = []
+    k0 = _lib.kernels_launched()
+    res, dev_ms, clocks, t0 = _timed(lambda: quantize_matrices(timed, damp=damp, n_streams=args.streams,
+                                                              ltq_formats=fmts, pack=False, row_reduce=row_reduce),
+                                     barrier, local)
+    launches = _lib.kernels_launched() - k0
+    ev, Lq.BLOCK_EVENTS = Lq.BLOCK_EVENTS, None
+    roof = _block_roofline(ev, t0)
+    rel = float(np.mean([r["rel_loss"] for r in res]))
+    packed = sum(int(r["ltq"]["data"].numel()) for r in res)
+
+    e2e_ms, h2d, d2h = None, 0, 0
+    host_need = sum(W.numel() * 2 for W, _, _ in timed) + sum(H.numel() * 4 for H in hcache.values())
+    host_ram = os.sysconf("SC_PHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+    if not args.no_e2e and host_need * world > 0.6 * host_ram:
+        print(f"rank {rank}: e2e skipped: {host_need * world / 1e9:.0f} GB of pinned inputs on a "
+              f"{host_ram / 1e9:.0f} GB host", file=sys.stderr, flush=True)
+        args.no_e2e = True
+    if not args.no_e2e:
+        # from pinned host memory to the packed tensors of every matrix in rank 0's host memory: host-to-device copies
+        # on the matrices' streams, quantization, one NCCL gather of all ranks' packed tensors, device-to-host copies
+        hosts = {}
+        host = []
+        for W, H, sp in timed:
+            if id(H) not in hosts:
+                hosts[id(H)] = H.cpu().pin_memory()
+            host.append((W.cpu().pin_memory(), hosts[id(H)], sp))
+        del res
+        h2d = sum(W.numel() * 2 + H.numel() * 4 for W, H, _ in host)
+        gid = [(i if not moe else (i * world + rank)) for i in mine_t]
+
+        def e2e():
+            r = quantize_matrices(host, damp=damp, n_streams=args.streams, ltq_formats=fmts, pack=False,
+                                  row_reduce=row_reduce, to_host=dist is None)
+            if dist is None:
+                return {g: x["ltq"] for g, x in zip(gid, r)}
+            return gather_ltq({g: x["ltq"] for g, x in zip(gid, r)}, dst=0)
+        e2e()  # untimed once: pinned output buffers; with several ranks, NCCL's point-to-point connections
+        got, e2e_ms, _, _ = _timed(e2e, barrier, local)
+        if rank == 0 and got is not None:
+            d2h = sum(sum(t.numel() * t.element_size() for k, t in d.items() if k in ("data", "d_row", "e", "suh"))
+                      for d in got.values())
+        del host, hosts, got
+    dev_ms, e2e_max, per_rank_weights = _max_over_ranks(dist, dev, dev_ms, e2e_ms or 0.0, weights_mine)
+    if rank != 0:
+        return
+    steps = 1 if not moe else args.steps
+    line = {
+        "metric": METRIC, "value": weights_total / (dev_ms * 1e-3) / 1e6, "unit": METRIC, "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": dev_ms / steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; config-2 weight and Hessian distributions)",
+        "config": ({"workload": "qwen3-30b-a3b_moe_rowshard_tcq45x_attn_tcq275x_experts",
+                    "step": "one MoE layer: q 4096x2048, k/v 512x2048, o 2048x4096 at TCQ45X; 128 experts x "
+                            "(gate_up 1536x2048, down 2048x768) at TCQ275X; 623 M weights",
+                    "layers_timed": args.steps, "hessian_rows": "4096 (attention), 1024 per expert",
+                    "parallelism": f"rows of every matrix over {world} ranks, 5 NCCL all-reduces per matrix"}
+                   if moe else
+                   {"workload": "qwen3-8b_model_by_matrix_tcqpq_menu",
+                    "step": "the whole model: 36 layers x (q/o 4096x4096, k/v 1024x4096, gate/up 12288x4096, down "
+                            "4096x12288) = 6.946 G weights, formats cycling the 19-format TCQPQ menu",
+                    "hessians": "one per input: attention (q/k/v), o, MLP (gate/up), down",
+                    "parallelism": f"whole matrices over {world} ranks (longest first), no data-path collective",
+                    "model_seconds": dev_ms / 1e3}) | {
+            "damp": damp * 10, "tb_window": TB_WINDOW, "streams": args.streams, "weights_total": weights_total,
+            "max_weights_per_rank": int(per_rank_weights), "rel_loss_mean_rank0": rel, "ltq_bytes_rank0": packed,
+            "l2": "inputs larger than L2"},
+        "roofline": roof, "cpu_baseline": None,
+        "e2e": None if e2e_ms is None else {
+            "value": weights_total / (e2e_max * 1e-3) / 1e6, "unit": METRIC, "seconds": e2e_max / 1e3,
+            "h2d_bytes_per_step": int(h2d // steps), "d2h_bytes_per_step": int(d2h // steps),
+            "scope": "pinned host W / H -> packed .ltq tensors of every matrix in rank 0's host memory"},
+        "gpu_launches": int(launches), "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
+def run_rings(args, rank, world, dev, dist, barrier, local):
+    """Config 5: a 262,144 x 2,560 bf16 table (N(0, 0.03) x a log-normal(0, 0.5) row scale) quantized as 256-value
+    tail-biting rings of TCQ4X after the Hadamard-256 rotation, three ring-scale tries (src/ple_quant.py:37-65).  The
+    rows are split across the ranks (independent rings, no collective); a step is the whole table, strong scaling."""
+    from ltq_research_b200 import _lib
+    from ltq_research_b200.rings import quantize_rings
+    from ltq_research_b200.shard import row_ranges
+    R, C = args.ring_rows, 2560
+    r0, r1 = row_ranges(R, world, multiple=16)[rank]
+
+    def table(a, b, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        T = torch.empty(b - a, C, dtype=torch.bfloat16, device=dev)
+        for c0 in range(0, b - a, 16384):  # row blocks, each from its own seed: any rank split gives the same table
+            n = min(16384, b - a - c0)
+            g.manual_seed(seed + a + c0)
+            T[c0:c0 + n] = (torch.randn(n, C, device=dev, generator=g) * 0.03 *
+                            torch.exp(0.5 * torch.randn(n, 1, device=dev, generator=g))).to(torch.bfloat16)
+        return T
+
+    Tm = table(r0, r1, 5)
+    warm = Tm[: min(Tm.shape[0], 2048)]
+    for _ in range(args.warmup):
+        quantize_rings(warm, "TCQ4X", True)
+    barrier()
+    k0 = _lib.kernels_launched()
+    out, dev_ms, clocks, _ = _timed(lambda: quantize_rings(Tm, "TCQ4X", True), barrier, local)
+    launches = _lib.kernels_launched() - k0
+    rel = float(((out.float() - Tm.float()).square().sum() / Tm.float().square().sum()).item())
+    del out
+    e2e_ms = None
+    if not args.no_e2e:
+        host = Tm.cpu().pin_memory()
+        quantize_rings(host[:2048], "TCQ4X", True, device=dev)
+        _, e2e_ms, _, _ = _timed(lambda: quantize_rings(host, "TCQ4X", True, device=dev), barrier, local)
+    dev_ms, e2e_max = _max_over_ranks(dist, dev, dev_ms, e2e_ms or 0.0)
+    if rank != 0:
+        return
+    values = R * C
+    peak, sm_mhz = alu_peak_gacs()
+    acs = values * 2 * 1024 * 4 * 3  # two full passes x 1024 states x 4 gain candidates x 3 scale tries
+    line = {
+        "metric": METRIC, "value": values / (dev_ms * 1e-3) / 1e6, "unit": METRIC, "n_gpus": world, "steps": 1,
+        "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; N(0, 0.03) x log-normal(0, 0.5) row scale)",
+        "config": {"workload": "ple_rings_262144x2560_tcq4x_rot_3tries", "table": [R, C], "format": "TCQ4X",
+                   "rotation": "Hadamard-256 with signs(4242)", "tries": [0.9, 1.0, 1.12], "rel_mse": rel,
+                   "parallelism": f"rows over {world} ranks, no collective", "unit_note": "weights = table values"},
+        "roofline": {"bound": "alu", "kernel": "vit_fwd_kernel (stand-alone tail-biting Viterbi) and the whole step",
+                     "achieved": acs / world / (dev_ms * 1e-3) / 1e9, "peak": peak, "unit": "GACS/s",
+                     "frac": acs / world / (dev_ms * 1e-3) / 1e9 / peak, "traffic": None,
+                     "basis": "per GPU: its values x 2 passes x 1024 states x 4 slots x 3 tries / the step's time"},
+        "cpu_baseline": None,
+        "e2e": None if e2e_ms is None else {
+            "value": values / (e2e_max * 1e-3) / 1e6, "unit": METRIC, "seconds": e2e_max / 1e3,
+            "h2d_bytes_per_step": int(values * 2), "d2h_bytes_per_step": int(values * 2),
+            "scope": "pinned host table rows -> reconstructed rows in each rank's host memory"},
+        "gpu_launches": int(launches), "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
+def run_gaussian(args, rank, world, dev, dist, barrier, local):
+    """Config 1, the reference's Gaussian rig (src/universal_bench.py:120-130 with the BASELINE choices): a 4096 x 4096
+    N(0, 1) matrix from torch's CPU generator seeded 0 (rank r: seed r, weak scaling), cut into 65,536 tiles of
+    16 x 16 (src/ltq_file.py:69-72), each divided by its fp16 RMS and quantized with the K = 2, 4-subset, 2-bit-gain
+    tail-biting TCQ of results/universal_gaussian.json (full first pass, unit weights); per-weight MSE reported."""
+    from ltq_research_b200 import _lib
+    from ltq_research_b200.formats import GAUSSIAN_RIG_K2H2 as RIG
+    from ltq_research_b200.tcq_proto import make_gains, viterbi_ub_cuda
+    W = torch.randn(4096, 4096, generator=torch.Generator().manual_seed(rank)).to(dev)
+    x = W.reshape(256, 16, 256, 16).permute(0, 2, 1, 3).reshape(-1, 256).contiguous()
+    d = x.square().mean(dim=1, keepdim=True).sqrt().half().float()
+    tab = torch.tensor(RIG["lut"], dtype=torch.float32, device=dev)
+    gains = make_gains(RIG["h"], RIG["step"], dev)
+
+    def step():
+        return viterbi_ub_cuda(x / d, tab, 2, 10, 359, gains, sub=16, tail_biting=True) * d
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    k0 = _lib.kernels_launched()
+
+    def many():
+        for _ in range(args.steps):
+            r = step()
+        return r
+    rec, dev_ms, clocks, _ = _timed(many, barrier, local)
+    launches = _lib.kernels_launched() - k0
+    mse = float((rec - x).square().mean().item())
+    e2e_ms = None
+    if not args.no_e2e:
+        hx = W.cpu().pin_memory()
+        out = torch.empty(4096, 4096, pin_memory=True)
+
+        def e2e():
+            for _ in range(args.steps):
+                Wd = hx.to(dev, non_blocking=True)
+                xt = Wd.reshape(256, 16, 256, 16).permute(0, 2, 1, 3).reshape(-1, 256).contiguous()
+                dd = xt.square().mean(dim=1, keepdim=True).sqrt().half().float()
+                r = viterbi_ub_cuda(xt / dd, tab, 2, 10, 359, gains, sub=16, tail_biting=True) * dd
+                out.copy_(r.reshape(256, 256, 16, 16).permute(0, 2, 1, 3).reshape(4096, 4096), non_blocking=True)
+        _, e2e_ms, _, _ = _timed(e2e, barrier, local)
+    dev_ms, e2e_max = _max_over_ranks(dist, dev, dev_ms, e2e_ms or 0.0)
+    if rank != 0:
+        return
+    total = 4096 * 4096 * args.steps * world
+    peak, sm_mhz = alu_peak_gacs()
+    ach = 4096 * 4096 * args.steps * 8192 / (dev_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": total / (dev_ms * 1e-3) / 1e6, "unit": METRIC, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0, 1), CPU generator)",
+        "config": {"workload": "gaussian_rig_4096x4096_tcq_k2_h2_tb", "tiles_per_step": 65536,
+                   "format": "K 2, nu 10, mask 359, 4 subsets, h 2 (step 0.3), sub 16, tail-biting, full first pass",
+                   "mse_per_weight": mse, "parallelism": f"dp{world} (one matrix per rank)",
+                   "l2": "inputs 64 MB + survivor streams 1 GB per step (above L2)"},
+        "roofline": {"bound": "alu", "kernel": "vit_fwd_kernel (stand-alone tail-biting Viterbi)",
+                     "achieved": ach, "peak": peak, "unit": "GACS/s", "frac": ach / peak, "traffic": None,
+                     "basis": "16.8 M weights x 8192 ACS (2 passes x 1024 states x 4 slots) per step / step time"},
+        "cpu_baseline": None,
+        "e2e": None if e2e_ms is None else {
+            "value": total / (e2e_max * 1e-3) / 1e6, "unit": METRIC, "h2d_bytes_per_step": 4096 * 4096 * 4,
+            "d2h_bytes_per_step": 4096 * 4096 * 4},
+        "gpu_launches": int(launches), "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--workload", default="llama3.2-3b",
+                    choices=["llama3.2-3b", "gaussian", "qwen3-8b", "qwen3-30b-a3b", "ple-rings"],
+                    help="BASELINE config: llama3.2-3b (config 2, the headline; a step is one decoder layer), "
+                         "gaussian (config 1), qwen3-8b (config 3, the whole model per step), qwen3-30b-a3b (config "
+                         "4, one MoE layer per step), ple-rings (config 5, the whole table per step)")
+    ap.add_argument("--ring-rows", type=int, default=262144, help="rows of the config-5 table")
     ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -512,6 +870,15 @@ def main():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
+
+    if args.workload != "llama3.2-3b":
+        run = {"gaussian": run_gaussian, "qwen3-8b": run_matrix_model, "qwen3-30b-a3b": run_matrix_model,
+               "ple-rings": run_rings}[args.workload]
+        run(args, rank, world, dev, dist, barrier, local)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     # inputs of the warm-up and timed layers, resident in HBM (each layer's H and W, ~0.7 GB, far above the 126 MB L2);
     # the warm-up quantizes --warmup layers untimed

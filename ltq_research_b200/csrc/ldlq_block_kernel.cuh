@@ -64,6 +64,17 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
+// Drops the L2 lines [p, p + bytes) without writing them back (discard.global.L2): for data that is dead, here survivor
+// words and merge winners after the traceback that consumed them.  Threads t0, t0 + ts, ... take one 128-byte line
+// each in turn; p and bytes are multiples of 128.  Without it, the dirty survivor lines of every pass would be
+// written to DRAM when evicted, although no one reads them again.
+__device__ __forceinline__ void discard_l2(const void* p, long long bytes, int t0, int ts)
+{
+    const char* c = static_cast<const char*>(p);
+    for (long long o = 128LL * t0; o < bytes; o += 128LL * ts)
+        asm volatile("discard.global.L2 [%0], 128;\n" ::"l"(c + o) : "memory");
+}
+
 __host__ __device__ inline int tb_coop_words(const VitParams& p)
 {
     return p.G * (p.sub / 4) * p.W4 * 32 + 128;
@@ -306,6 +317,14 @@ __global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) ldlq_block_kernel(const 
             __syncthreads();
             ldlq_tb<MP, MD>(pp, n, smem, q.fb_off, xr);
             __syncthreads();
+            // this pass's survivor words (its T / 4 groups in every slot's stream) and merge winners are dead: every
+            // copy the traceback made of them completed before the barrier above.  Each slot's stream starts on a
+            // 128-byte line (capA words = 64 W4 x 32), each merge-winner row is 512 bytes.
+            for (int g = 0; g < pp.G; g++)
+                discard_l2(pp.svA + ((size_t)n * pp.G + g) * (size_t)pp.capA, (long long)(pp.T / 4) * pp.W4 * 128, tid,
+                           nthr);
+            if (pp.G > 1)
+                discard_l2(pp.gsw + (size_t)n * pp.nsl * (NS / 8), (long long)(pp.T / pp.sub) * 512, tid, nthr);
         }
         for (int i = tid; i < 256; i += nthr) {
             const int r = i >> 4, c = i & 15;

@@ -108,8 +108,11 @@ def merge_row_shards(parts: Sequence[dict], align: int = 64, formats: Optional[S
     returns them under "ltq", on one device or on the host): d_row and e stacked; suh must be the same in every shard
     (the row-sharded refit makes it so).  Without `formats` the shards' packed data are concatenated, every shard
     starting on an `align`-byte boundary, slice rows and offsets moved accordingly.  With `formats` (the format of each
-    slice index, as given to quantize_matrices' ltq_formats), slices of one format on consecutive rows become one
-    slice, packed region by region, so that the result is laid out exactly as the whole matrix packed at once."""
+    slice index, as given to quantize_matrices' ltq_formats), a shard's last slice and the next shard's first slice
+    become one slice when they have the same format (the cut between shards fell inside one row slice of the
+    matrix), packed region by region; slices inside one shard stay as they are.  When every shard was quantized with
+    the matrix's row slices cut at the shard boundaries, the result is laid out exactly as the whole matrix packed at
+    once."""
     if not parts:
         raise ValueError("merge_row_shards: no shards")
     suh = parts[0]["suh"]
@@ -137,9 +140,10 @@ def merge_row_shards(parts: Sequence[dict], align: int = 64, formats: Optional[S
     row0 = 0
     for p in parts:
         flat = p["data"].reshape(-1).to(dev)
-        for r0, r1, fi, o in sorted(p["slices"], key=lambda x: x[0]):
+        for k, (r0, r1, fi, o) in enumerate(sorted(p["slices"], key=lambda x: x[0])):
             piece = (flat[o:o + _slice_nbytes(r1 - r0, K, formats[fi], align)], r1 - r0)
-            if runs and runs[-1][2] == fi and runs[-1][1] == r0 + row0:
+            # only a shard's first slice may continue the previous shard's last one
+            if k == 0 and runs and runs[-1][2] == fi and runs[-1][1] == r0 + row0:
                 runs[-1][1] = r1 + row0
                 runs[-1][3].append(piece)
             else:

@@ -218,3 +218,13 @@ def test_merge_row_shards_coalesces_to_whole_packing():
     whole = part([(0, 16, 0, i0, g0), (16, 96, 1, i1, g1)], 96)
     assert m["slices"] == whole["slices"]
     assert torch.equal(m["data"], whole["data"])
+    # two slices of one format inside a shard stay two slices (as the whole matrix packed with those row slices)
+    j0, h0 = codes(32, ofmts[0])
+    j1, h1 = codes(16, ofmts[0])
+    j2, h2 = codes(48, ofmts[0])
+    a = part([(0, 32, 0, j0, h0), (32, 48, 0, j1, h1)], 48)
+    b = part([(0, 48, 0, j2, h2)], 48)
+    m = merge_row_shards([a, b], formats=fmts)
+    whole = part([(0, 32, 0, j0, h0), (32, 96, 0, np.concatenate([j1, j2]), np.concatenate([h1, h2]))], 96)
+    assert m["slices"] == whole["slices"] == [[0, 32, 0, 0], [32, 96, 0, m["slices"][1][3]]]
+    assert torch.equal(m["data"], whole["data"])
