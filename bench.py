@@ -543,12 +543,18 @@ def run_matrix_model(args, rank, world, dev, dist, barrier, local):
     from ltq_research_b200.formats import MENU_TCQPQ, load_formats
     from ltq_research_b200.shard import assign, gather_ltq, nccl_row_reduce, row_ranges
     moe = args.workload == "qwen3-30b-a3b"
+    by_rows = moe and args.moe_shard == "rows"
     if moe:
         warm_m = [m for l in range(args.warmup) for m in moe_layer_matrices(1000 + l)]
         timed_m = [m for l in range(args.steps) for m in moe_layer_matrices(l)]
-        mine_w, mine_t = list(range(len(warm_m))), list(range(len(timed_m)))
-        rows = {M: row_ranges(M, world)[rank] for M in {m[1] for m in warm_m + timed_m}}
-        row_reduce = nccl_row_reduce() if world > 1 else None
+        if by_rows:
+            mine_w, mine_t = list(range(len(warm_m))), list(range(len(timed_m)))
+            rows = {M: row_ranges(M, world)[rank] for M in {m[1] for m in warm_m + timed_m}}
+            row_reduce = nccl_row_reduce() if world > 1 else None
+        else:
+            mine_w = assign([(M, K, sp) for _, M, K, sp, _ in warm_m], world)[rank]
+            mine_t = assign([(M, K, sp) for _, M, K, sp, _ in timed_m], world)[rank]
+            rows, row_reduce = None, None
         fmts = load_formats(["TCQ45X", "TCQ275X"], dev)
     else:
         allm = qwen3_8b_matrices()
@@ -614,7 +620,7 @@ def run_matrix_model(args, rank, world, dev, dist, barrier, local):
                 hosts[id(H)] = H.cpu().pin_memory()
             host.append((W.cpu().pin_memory(), hosts[id(H)], sp))
         h2d = sum(W.numel() * 2 + H.numel() * 4 for W, H, _ in host)
-        gid = [(i if not moe else (i * world + rank)) for i in mine_t]
+        gid = [(i * world + rank if by_rows else i) for i in mine_t]
 
         def e2e():
             r = quantize_matrices(host, damp=damp, n_streams=args.streams, ltq_formats=fmts, pack=False,
@@ -651,11 +657,14 @@ def run_matrix_model(args, rank, world, dev, dist, barrier, local):
         "steps": steps, "warmup": args.warmup, "ms_per_step": dev_ms / steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded; config-2 weight and Hessian distributions)",
-        "config": ({"workload": "qwen3-30b-a3b_moe_rowshard_tcq45x_attn_tcq275x_experts",
+        "config": ({"workload": "qwen3-30b-a3b_moe_" + ("rowshard" if by_rows else "by_matrix") +
+                                "_tcq45x_attn_tcq275x_experts",
                     "step": "one MoE layer: q 4096x2048, k/v 512x2048, o 2048x4096 at TCQ45X; 128 experts x "
                             "(gate_up 1536x2048, down 2048x768) at TCQ275X; 623 M weights",
                     "layers_timed": args.steps, "hessian_rows": "4096 (attention), 1024 per expert",
-                    "parallelism": f"rows of every matrix over {world} ranks, 5 NCCL all-reduces per matrix"}
+                    "parallelism": (f"rows of every matrix over {world} ranks, 5 NCCL all-reduces per matrix"
+                                    if by_rows else f"whole matrices over {world} ranks (longest first), no "
+                                    "data-path collective")}
                    if moe else
                    {"workload": "qwen3-8b_model_by_matrix_tcqpq_menu",
                     "step": "the whole model: 36 layers x (q/o 4096x4096, k/v 1024x4096, gate/up 12288x4096, down "
@@ -814,6 +823,9 @@ def main():
                          "gaussian (config 1), qwen3-8b (config 3, the whole model per step), qwen3-30b-a3b (config "
                          "4, one MoE layer per step), ple-rings (config 5, the whole table per step)")
     ap.add_argument("--ring-rows", type=int, default=262144, help="rows of the config-5 table")
+    ap.add_argument("--moe-shard", default="rows", choices=["rows", "matrices"],
+                    help="config 4: split every matrix's rows across the ranks (the config's row sharding), or give "
+                         "each rank whole matrices (experts and attention, longest first; no collective)")
     ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
