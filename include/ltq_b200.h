@@ -145,8 +145,23 @@ int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* X, long lon
  * are tensor-core GEMMs on the caller's side.
  */
 int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt6, float* X, long long ldx, int* info, void* stream);
+/*
+ * Tensor-core GEMM of the fast mode's fp32-accurate products (tcgen05.mma, accumulator in tensor memory, operands by
+ * TMA): C[M, N] = beta * C + alpha * A[M, Kd] B[N, Kd]^T with A, B bf16 (K contiguous, row strides lda / ldb) and C
+ * fp32 (row stride ldc).  Replaces the library GEMM (torch.addmm / torch.mm on cuBLAS) that ran the six-product bf16
+ * form of the LDLQ inter-block update W_work[:, c1:] -= ((w_blk - what) @ U_blk_inv) @ U[c0:c1, c1:]
+ * (src/liqk_v2.py:972-979).  Limits: N % 16 == 0, Kd a positive multiple of 64, lda and ldb multiples of 8, ldc of 4,
+ * A / B / C 16-byte aligned.  err (optional, device int): set to 1 if a pipeline wait ran out (the result is then
+ * not valid); the caller clears it.
+ */
+int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t* B, long long ldb, float* C, long long ldc,
+                     int M, int N, int Kd, float alpha, float beta, int* err, void* stream);
 size_t ltq_ldlq_bcat_elems(int K);
 int ltq_ldlq_bcat(const float* U, long long ldU, int K, uint16_t* bcat, void* stream);
+/* the same operands transposed for ltq_gemm_bf16_tn (K contiguous): block b's [K - 256 (b + 1), 1536] matrix whose row n
+ * is the six slots [u0 u1 u0 u2 u1 u0] of column 256 (b + 1) + n of U[256 b : 256 b + 256, :], at the same offsets
+ * (K >= 512; bcat 16-byte aligned). */
+int ltq_ldlq_bcat_t(const float* U, long long ldU, int K, uint16_t* bcat, void* stream);
 int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* G, long long ldG,
                    const float* Uinv, long long ldUi, int M, float* what, long long ld_what, uint16_t* d_h,
                    long long ld_dh, uint16_t* acat, void* stream);

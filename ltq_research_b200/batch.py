@@ -19,7 +19,7 @@ import torch
 
 from . import _lib
 from .formats import TCQ_CONFIG
-from .liqk_v2 import _quantize_matrix_steps
+from .liqk_v2 import _quantize_matrix_steps, check_gemm_errors
 
 Spec = Union[str, Sequence[Tuple[int, int, str]]]
 
@@ -181,6 +181,7 @@ def quantize_matrices(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor, Spec]], s
     for i, r in enumerate(out):
         _record(r, main)
     nd = torch.stack([torch.stack([r["num"], r["den"]]) for r in out]).cpu()
+    check_gemm_errors(dev)
     info = torch.stack([r["chol_info"].reshape(()) for r in out]).cpu()
     bad = (torch.stack([r["ltq"]["bad"].reshape(()) for r in out]).cpu() if ltq_formats is not None
            else torch.zeros(len(out), dtype=torch.int64))

@@ -1,0 +1,282 @@
+// Tensor-core GEMM for the quantizer's fp32-accurate products on B200 (sm_100a): tcgen05.mma with the accumulator in
+// tensor memory, operands brought to shared memory by TMA.
+//
+//     C[M, N] = beta * C + alpha * A[M, Kd] B[N, Kd]^T      (A, B bf16 with K contiguous; fp32 accumulation and C)
+//
+// Used for the LDLQ inter-block update W_work[:, c1:] -= acat @ bcat_b (src/liqk_v2.py:972-979 in its six-product
+// bf16 form: A = [e0 e0 e1 e0 e1 e2], B^T = the matching slots of U[c0:c1, c1:]) and the Cholesky panel / trailing
+// products (src/liqk_v2.py:1078) of the fast mode, where the bf16 split makes every operand K-major.
+//
+// One CTA per 128 x 256 tile of C, 128 threads:
+//   thread 0 (warp 0)  TMA producer: per 64-wide K chunk, A [128 x 64] and B [256 x 64] tiles into a 3-stage ring of
+//                      shared buffers (128-byte swizzle), completion counted in bytes on the stage's "full" mbarrier;
+//   thread 32 (warp 1) MMA issuer: four tcgen05.mma (M 128, N 256, K 16 each) per chunk into one 128-lane x 256-column
+//                      fp32 accumulator in tensor memory; tcgen05.commit frees the stage ("empty" mbarrier) once the
+//                      MMAs have read it, and signals the accumulator after the last chunk;
+//   all four warps     epilogue: warp w reads lanes 32 w .. 32 w + 31 (rows of the tile) with tcgen05.ld, 16 columns at a
+//                      time, and writes C = beta C + alpha acc (one fma per element) to global memory.
+// Every wait on an mbarrier is bounded: after GEMM_WAIT_LIMIT polls the thread records a timeout in *err (when given)
+// and leaves its loop; the CTA still meets at its final barrier and frees its tensor memory.  No cluster, no multicast:
+// every TMA load reads this GPU's own memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <atomic>
+#include "ltq_b200.h"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
+constexpr int A_BYTES = BM * BK * 2;            // 16 KB
+constexpr int B_BYTES = BN * BK * 2;            // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB, a multiple of the 1024-byte swizzle atom
+constexpr int TMEM_COLS = 256;
+constexpr uint32_t GEMM_WAIT_LIMIT = 1u << 26;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+
+struct GemmParams {
+    float* C;
+    long long ldc;
+    int M, N, Kd;
+    float alpha, beta;
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait for the phase with parity `parity`; false after GEMM_WAIT_LIMIT polls (the timeout is recorded)
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err)
+{
+    for (uint32_t i = 0; i < GEMM_WAIT_LIMIT; i++)
+        if (mbar_try_wait(b, parity)) return true;
+    if (err) atomicExch(err, 1);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// shared-memory matrix descriptor (tcgen05): K-major tile of rows x 64 bf16 with the 128-byte swizzle, as TMA writes it:
+// 8-row atoms of 1024 bytes one after the other (stride byte offset 1024), the second 16-byte column chunk adjacent
+// (leading byte offset 16), descriptor version 1, layout 2 (128-byte swizzle).  `addr` may step through the atom's
+// row in 32-byte units (one K = 16 slice of bf16), the hardware applying the swizzle to the computed address.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t addr)
+{
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12 = 1), both K-major
+// (bits 15, 16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(IDESC), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
+{
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                              const __grid_constant__ CUtensorMap tmB,
+                                                              const GemmParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* accum = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int nk = p.Kd / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {  // the whole warp allocates the accumulator's columns (the address lands in shared memory)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (threadIdx.x == 0) {  // TMA producer
+        int issued = 0;
+        for (int k = 0; k < nk; k++) {
+            const int s = k % STAGES;
+            if (k >= STAGES && !mbar_wait(&empty[s], ((k / STAGES) - 1) & 1, p.err)) break;
+            mbar_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_2d(smem + s * STAGE_BYTES, &tmA, k * BK, m0, &full[s]);
+            tma_load_2d(smem + s * STAGE_BYTES + A_BYTES, &tmB, k * BK, n0, &full[s]);
+            issued = k + 1;
+        }
+        // every copy this thread started has landed before the CTA can leave (a completed phase stays visible to
+        // its parity until the barrier completes the next one, which needs a new arrive from this thread)
+        for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; k++)
+            mbar_wait(&full[k % STAGES], (k / STAGES) & 1, p.err);
+    } else if (threadIdx.x == 32) {  // MMA issuer
+        for (int k = 0; k < nk; k++) {
+            const int s = k % STAGES;
+            if (!mbar_wait(&full[s], (k / STAGES) & 1, p.err)) break;
+            tc_fence_after();
+            const uint32_t a = smem_u32(smem + s * STAGE_BYTES), b = a + A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; kk++)
+                umma_bf16(tmem, sw128_kmajor_desc(a + 32 * kk), sw128_kmajor_desc(b + 32 * kk), (k | kk) != 0);
+            umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        umma_commit(accum);  // arrives when every MMA issued above has completed
+    }
+
+    // epilogue
+    const bool ok = mbar_wait(accum, 0, p.err);
+    __syncwarp();
+    tc_fence_after();
+    if (ok) {
+        const int row = m0 + 32 * warp + lane;
+        const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+        for (int c = 0; c < BN; c += 16) {
+            if (n0 + c >= p.N) break;  // warp-uniform: N is a multiple of 16
+            float v[16];
+            tmem_ld16(tl + c, v);
+            if (row < p.M) {
+                float* cp = p.C + (long long)row * p.ldc + n0 + c;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (p.beta != 0.f) {
+                        const float4 old = *reinterpret_cast<const float4*>(cp + 4 * q);
+                        o = make_float4(p.beta * old.x, p.beta * old.y, p.beta * old.z, p.beta * old.w);
+                    }
+                    o.x = __fmaf_rn(p.alpha, v[4 * q], o.x);
+                    o.y = __fmaf_rn(p.alpha, v[4 * q + 1], o.y);
+                    o.z = __fmaf_rn(p.alpha, v[4 * q + 2], o.z);
+                    o.w = __fmaf_rn(p.alpha, v[4 * q + 3], o.w);
+                    *reinterpret_cast<float4*>(cp + 4 * q) = o;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> fn{nullptr};
+    PFN_cuTensorMapEncodeTiled_v12000 f = fn.load(std::memory_order_acquire);
+    if (!f) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        f = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        fn.store(f, std::memory_order_release);
+    }
+    return f;
+}
+
+// 2-D tensor map of a row-major bf16 matrix [rows, cols] (row stride ld elements), box [box_rows, 64] with the
+// 128-byte swizzle; out-of-range rows and columns read as zero
+bool make_map(CUtensorMap* m, const void* base, int rows, int cols, long long ld, int box_rows)
+{
+    auto f = encode_fn();
+    if (!f) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t* B, long long ldb, float* C,
+                                long long ldc, int M, int N, int Kd, float alpha, float beta, int* err, void* stream)
+{
+    if (M < 0 || N < 0 || Kd < 0 || N % 16 || Kd % BK || !A || !B || !C || lda < Kd || ldb < Kd || ldc < N ||
+        (lda % 8) || (ldb % 8) || (ldc % 4) || ((uintptr_t)A & 15) || ((uintptr_t)B & 15) || ((uintptr_t)C & 15))
+        return -1;
+    if (M == 0 || N == 0) return 0;
+    if (Kd == 0) return -1;
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, A, M, Kd, lda, BM) || !make_map(&tb, B, N, Kd, ldb, BN)) return -1;
+    static std::atomic<int> attr_set[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+            cudaSuccess)
+            return -1;
+        attr_set[dev].store(1, std::memory_order_release);
+    }
+    GemmParams p{C, ldc, M, N, Kd, alpha, beta, err};
+    dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+    gemm_bf16_tn_kernel<<<grid, 128, SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, p);
+    return (int)cudaGetLastError();
+}

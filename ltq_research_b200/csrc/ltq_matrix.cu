@@ -232,6 +232,39 @@ __global__ void __launch_bounds__(256) ldlq_bcat_kernel(const float* __restrict_
     }
 }
 
+// The same operands transposed, for the tensor-core GEMM (both operands K-major): block b's [N_b, 1536] matrix with
+// row n = [u0 u1 u0 u2 u1 u0] of column c1 + n of U[256 b : 256 b + 256, :], i.e. out_b[n][256 s + i] = part_s(U[c0 + i][c1 + n]).
+// A 32 x 32 tile of U per CTA (32 x 8 threads): read along n (coalesced), split, transposed through shared memory,
+// written along i (64 bytes per slot and row).  blockIdx = (n tile, i tile, block b).
+__global__ void __launch_bounds__(256) ldlq_bcat_t_kernel(const float* __restrict__ U, long long ldU, int K,
+                                                          uint16_t* __restrict__ out)
+{
+    __shared__ uint16_t sp[3][32][34];  // [part][n][i]
+    const int b = blockIdx.z, c0 = 256 * b, c1 = c0 + 256, nb = K - c1;
+    const int n0 = 32 * blockIdx.x, i0 = 32 * blockIdx.y;
+    if (n0 >= nb) return;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const long long off = 1536LL * ((long long)b * K - 128LL * b * (b + 1));
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int i = ty + 8 * q;
+        uint16_t p0, p1, p2;
+        split3_bf16(U[(long long)(c0 + i0 + i) * ldU + c1 + n0 + tx], p0, p1, p2);
+        sp[0][tx][i] = p0;
+        sp[1][tx][i] = p1;
+        sp[2][tx][i] = p2;
+    }
+    __syncthreads();
+    constexpr int part_of_slot[6] = {0, 1, 0, 2, 1, 0};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int n = ty + 8 * q;
+        uint16_t* row = out + off + (long long)(n0 + n) * 1536 + i0 + tx;
+#pragma unroll
+        for (int sl = 0; sl < 6; sl++) row[256 * sl] = sp[part_of_slot[sl]][n][tx];
+    }
+}
+
 // after block [c0, c0 + 256): W_hat = d * G, d_h = fp16(d), e = w - W_hat (the reference's operations, same bits), and
 // for the update err = e @ Uinv (Uinv upper triangular: err[k] = sum_{i <= k} e[i] Uinv[i][k], i ascending, fma) split
 // into acat [M, 1536] = [e0 e0 e1 e0 e1 e2].  One CTA per 16 rows, thread k = column k.
@@ -618,6 +651,14 @@ extern "C" size_t ltq_ldlq_bcat_elems(int K)
     if (K < 256 || K % 256) return 0;
     const long long nb = K / 256 - 1;  // blocks with an update
     return (size_t)(1536LL * (nb * K - 128LL * nb * (nb + 1)));
+}
+
+extern "C" int ltq_ldlq_bcat_t(const float* U, long long ldU, int K, uint16_t* bcat, void* stream)
+{
+    if (K < 512 || K % 256 || ldU < K || !U || !bcat || ((uintptr_t)bcat & 15)) return -1;
+    const dim3 grid((K - 256) / 32, 8, K / 256 - 1);
+    ldlq_bcat_t_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(U, ldU, K, bcat);
+    return (int)cudaGetLastError();
 }
 
 extern "C" int ltq_ldlq_bcat(const float* U, long long ldU, int K, uint16_t* bcat, void* stream)

@@ -443,6 +443,30 @@ def _rows_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: torch.Tensor, d
     return _drive(_rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name, fused, gemm))
 
 
+_GEMM_ERR: Dict[str, torch.Tensor] = {}
+
+
+def gemm_error_flag(device) -> torch.Tensor:
+    """The device int that the tensor-core GEMM sets when one of its pipeline waits runs out (one per device, shared by
+    all streams; cleared by check_gemm_errors)."""
+    key = str(torch.device(device))
+    t = _GEMM_ERR.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        torch.cuda.current_stream(device).synchronize()
+        _GEMM_ERR[key] = t
+    return t
+
+
+def check_gemm_errors(device):
+    """Raises if a tensor-core GEMM on `device` reported a timed-out pipeline wait since the last check (a host
+    synchronisation: call it where the caller synchronises anyway)."""
+    t = _GEMM_ERR.get(str(torch.device(device)))
+    if t is not None and int(t.item()) != 0:
+        t.zero_()
+        raise RuntimeError("ltq_gemm_bf16_tn: a pipeline wait ran out; the LDLQ update of this call is not valid")
+
+
 def _scale_fit_reference(W_rot: torch.Tensor, cfg: dict):
     """The row-scale fit as the reference computes it with torch (src/liqk_v2.py:938-946): block RMS, fp16 geometric
     mean per row, 5-bit exponents; returns (d_row fp32 [M], e int8 [M, K/256], d_rb fp32 [M, K/256])."""
@@ -504,8 +528,10 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
         # tensor-core GEMM W_work[:, c1:] -= acat @ bcat_b
         brun = _BlockRunner(spec_name, M, device)
         dwc = diag_w.float().contiguous()
-        bcat = torch.empty(max(int(L.ltq_ldlq_bcat_elems(K)), 1), dtype=torch.bfloat16, device=device)
-        _check(L.ltq_ldlq_bcat(ptr(Uc), Uc.stride(0), K, ptr(bcat), st), "ltq_ldlq_bcat")
+        bcat = torch.empty(max(int(L.ltq_ldlq_bcat_elems(K)), 8), dtype=torch.bfloat16, device=device)
+        if nblocks > 1:  # every block's right operand, K-major for the tensor-core GEMM
+            _check(L.ltq_ldlq_bcat_t(ptr(Uc), Uc.stride(0), K, ptr(bcat), st), "ltq_ldlq_bcat_t")
+        gerr = gemm_error_flag(device)
         acat = torch.empty((M, 6 * QK_K), dtype=torch.bfloat16, device=device)
         U_blks_inv = U_blks_inv.contiguous()  # row-major blocks (a batched triangular solve may return column-major)
         off = 0
@@ -519,10 +545,11 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
                                     ptr(W_hat_rot) + 4 * c0, W_hat_rot.stride(0), ptr(d_full) + 2 * ibl,
                                     d_full.stride(0), None if last else ptr(acat), st), "ltq_ldlq_inter")
             if not last:
+                # W_work[:, c1:] -= acat @ bcat_b^T on the tensor cores (ltq_gemm_bf16_tn, tcgen05)
                 nb = K - c1
-                Wv = W_work[:, c1:]
-                torch.addmm(Wv, acat, bcat[off:off + 6 * QK_K * nb].view(6 * QK_K, nb), out_dtype=torch.float32,
-                            beta=1, alpha=-1, out=Wv)
+                _check(L.ltq_gemm_bf16_tn(ptr(acat), 6 * QK_K, ptr(bcat) + 2 * off, 6 * QK_K, ptr(W_work) + 4 * c1,
+                                          W_work.stride(0), M, nb, 6 * QK_K, -1.0, 1.0, ptr(gerr), st),
+                       "ltq_gemm_bf16_tn")
                 off += 6 * QK_K * nb
             yield
         return d_full, W_hat_rot, group
