@@ -156,15 +156,31 @@ int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt6, float* X, lo
  */
 int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t* B, long long ldb, float* C, long long ldc,
                      int M, int N, int Kd, float alpha, float beta, int* err, void* stream);
+/*
+ * The same product in the six-product form from compact three-part operands A3 = [a0 a1 a2] [M, 3 Kp] and
+ * B3 = [b0 b1 b2] [N, 3 Kp] (x = x0 + x1 + x2 the three-way bf16 split of an fp32 operand):
+ *     C = beta C + alpha (a0 b0^T + a0 b1^T + a1 b0^T + a0 b2^T + a1 b1^T + a2 b0^T),
+ * each A part of a K chunk loaded once for the three B parts it meets — half the operand bytes of the concatenated form
+ * [a0 a0 a1 a0 a1 a2] [b0 b1 b0 b2 b1 b0]^T.  Limits as ltq_gemm_bf16_tn with Kp a positive multiple of 64 and
+ * lda, ldb >= 3 Kp.  This is the LDLQ inter-block update's GEMM (A3 from ltq_ldlq_inter3, B3 from ltq_ldlq_bcat_t).
+ */
+int ltq_gemm_bf16x6_tn(const uint16_t* A3, long long lda, const uint16_t* B3, long long ldb, float* C, long long ldc,
+                       int M, int N, int Kp, float alpha, float beta, int* err, void* stream);
 size_t ltq_ldlq_bcat_elems(int K);
 int ltq_ldlq_bcat(const float* U, long long ldU, int K, uint16_t* bcat, void* stream);
-/* the same operands transposed for ltq_gemm_bf16_tn (K contiguous): block b's [K - 256 (b + 1), 1536] matrix whose row n
- * is the six slots [u0 u1 u0 u2 u1 u0] of column 256 (b + 1) + n of U[256 b : 256 b + 256, :], at the same offsets
- * (K >= 512; bcat 16-byte aligned). */
+/* the right operands in the compact three-part form of ltq_gemm_bf16x6_tn (K contiguous): block b's
+ * [K - 256 (b + 1), 768] matrix whose row n is [u0 u1 u2], the three-way split of column 256 (b + 1) + n of
+ * U[256 b : 256 b + 256, :], at element offset 768 * sum_{b' < b} (K - 256 (b' + 1)), ltq_ldlq_bcat_elems(K) / 2 elements
+ * in all (K >= 512; bcat 16-byte aligned). */
 int ltq_ldlq_bcat_t(const float* U, long long ldU, int K, uint16_t* bcat, void* stream);
 int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* G, long long ldG,
                    const float* Uinv, long long ldUi, int M, float* what, long long ld_what, uint16_t* d_h,
                    long long ld_dh, uint16_t* acat, void* stream);
+/* ltq_ldlq_inter with err's split in the compact form acat3 [M, 768] = [e0 e1 e2] (row stride 768) for
+ * ltq_gemm_bf16x6_tn. */
+int ltq_ldlq_inter3(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* G,
+                    long long ldG, const float* Uinv, long long ldUi, int M, float* what, long long ld_what,
+                    uint16_t* d_h, long long ld_dh, uint16_t* acat3, void* stream);
 int ltq_ldlq_block(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* dw,
                    const float* U, long long ldU, const float* Uinv, long long ldUi, float* G, long long ldG,
                    int16_t* idx, uint8_t* gi, long long ldP, int M, const float* tab, const float* gains, int K, int m,

@@ -14,7 +14,8 @@
 //                      fp32 accumulator in tensor memory; tcgen05.commit frees the stage ("empty" mbarrier) once the
 //                      MMAs have read it, and signals the accumulator after the last chunk;
 //   all four warps     epilogue: warp w reads lanes 32 w .. 32 w + 31 (rows of the tile) with tcgen05.ld, 16 columns at a
-//                      time, and writes C = beta C + alpha acc (one fma per element) to global memory.
+//                      time, stages them row-major in the freed pipeline buffers and writes C = beta C + alpha acc (one
+//                      fma per element) a whole row segment per warp instruction.
 // Every wait on an mbarrier is bounded: after GEMM_WAIT_LIMIT polls the thread records a timeout in *err (when given)
 // and leaves its loop; the CTA still meets at its final barrier and frees its tensor memory.  No cluster, no multicast:
 // every TMA load reads this GPU's own memory.
@@ -27,13 +28,21 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
+#ifndef LTQ_GEMM_BN
+#define LTQ_GEMM_BN 256
+#endif
+#ifndef LTQ_GEMM_STAGES
+#define LTQ_GEMM_STAGES 2
+#endif
+constexpr int BM = 128, BN = LTQ_GEMM_BN, BK = 64, STAGES = LTQ_GEMM_STAGES;
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
 constexpr int B_BYTES = BN * BK * 2;            // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB, a multiple of the 1024-byte swizzle atom
-constexpr int TMEM_COLS = 256;
+// two stages (97 KB of shared memory) let two CTAs share an SM, which measured faster than three stages at one CTA
+constexpr int TMEM_COLS = BN;  // a power of two >= 32
 constexpr uint32_t GEMM_WAIT_LIMIT = 1u << 26;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+static_assert(4 * 32 * ((BN < 128 ? BN : 128) + 4) * 4 <= STAGES * STAGE_BYTES, "epilogue staging exceeds the buffers");
 
 struct GemmParams {
     float* C;
@@ -125,6 +134,53 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// Epilogue, in halves of 128 columns: each warp moves its 32 rows x 16 columns at a time from tensor memory (thread =
+// row) into a row-major shared tile (the pipeline's buffers are free once the accumulator is complete), then writes C
+// row by row, a whole 512-byte row segment per warp instruction (coalesced read-modify-write), C = beta C + alpha acc.
+__device__ __forceinline__ void epilogue(const GemmParams& p, uint64_t* accum, uint32_t tmem, uint8_t* smem, int m0,
+                                         int n0, int warp, int lane)
+{
+    const bool ok = mbar_wait(accum, 0, p.err);
+    __syncwarp();
+    tc_fence_after();
+    if (!ok) return;
+    constexpr int HALF = BN < 128 ? BN : 128, LDS = HALF + 4;
+    float* st = reinterpret_cast<float*>(smem) + warp * 32 * LDS;
+    const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+    for (int h = 0; h < BN; h += HALF) {
+        if (n0 + h >= p.N) break;  // warp-uniform
+        for (int c = 0; c < HALF; c += 16) {
+            float v[16];
+            tmem_ld16(tl + h + c, v);
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                *reinterpret_cast<float4*>(st + lane * LDS + c + 4 * q) =
+                    make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+        __syncwarp();
+        const int col = n0 + h + 4 * lane;
+        for (int r = 0; r < 32; r++) {
+            const int row = m0 + 32 * warp + r;
+            if (row >= p.M) break;
+            if (col < p.N) {
+                const float4 a = *reinterpret_cast<const float4*>(st + r * LDS + 4 * lane);
+                float* cp = p.C + (long long)row * p.ldc + col;
+                float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (p.beta != 0.f) {
+                    const float4 old = *reinterpret_cast<const float4*>(cp);
+                    o = make_float4(p.beta * old.x, p.beta * old.y, p.beta * old.z, p.beta * old.w);
+                }
+                o.x = __fmaf_rn(p.alpha, a.x, o.x);
+                o.y = __fmaf_rn(p.alpha, a.y, o.y);
+                o.z = __fmaf_rn(p.alpha, a.z, o.z);
+                o.w = __fmaf_rn(p.alpha, a.w, o.w);
+                *reinterpret_cast<float4*>(cp) = o;
+            }
+        }
+        __syncwarp();
+    }
+}
+
 __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA,
                                                               const __grid_constant__ CUtensorMap tmB,
                                                               const GemmParams p)
@@ -140,6 +196,8 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_const
     const int nk = p.Kd / BK;
 
     if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmB) : "memory");
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
@@ -186,35 +244,115 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_const
         umma_commit(accum);  // arrives when every MMA issued above has completed
     }
 
-    // epilogue
-    const bool ok = mbar_wait(accum, 0, p.err);
-    __syncwarp();
-    tc_fence_after();
-    if (ok) {
-        const int row = m0 + 32 * warp + lane;
-        const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
-        for (int c = 0; c < BN; c += 16) {
-            if (n0 + c >= p.N) break;  // warp-uniform: N is a multiple of 16
-            float v[16];
-            tmem_ld16(tl + c, v);
-            if (row < p.M) {
-                float* cp = p.C + (long long)row * p.ldc + n0 + c;
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (p.beta != 0.f) {
-                        const float4 old = *reinterpret_cast<const float4*>(cp + 4 * q);
-                        o = make_float4(p.beta * old.x, p.beta * old.y, p.beta * old.z, p.beta * old.w);
-                    }
-                    o.x = __fmaf_rn(p.alpha, v[4 * q], o.x);
-                    o.y = __fmaf_rn(p.alpha, v[4 * q + 1], o.y);
-                    o.z = __fmaf_rn(p.alpha, v[4 * q + 2], o.z);
-                    o.w = __fmaf_rn(p.alpha, v[4 * q + 3], o.w);
-                    *reinterpret_cast<float4*>(cp + 4 * q) = o;
-                }
-            }
-        }
+    epilogue(p, accum, tmem, smem, m0, n0, warp, lane);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
     }
+}
+
+// The six-product form of an fp32-accurate product from compact three-part operands:
+//     C = beta C + alpha (a0 b0^T + a0 b1^T + a1 b0^T + a0 b2^T + a1 b1^T + a2 b0^T)
+// with A3 = [a0 a1 a2] [M, 3 Kp] and B3 = [b0 b1 b2] [N, 3 Kp] (bf16, K contiguous; x = x0 + x1 + x2 the three-way split
+// of an fp32 operand).  Per 64-wide chunk j of Kp: the three A parts of the chunk stay in one of two A buffers
+// (3 x 16 KB) while the B parts stream through three 32 KB stages (stage q holds b_q): b0 meets a0, a1, a2; b1 meets a0,
+// a1; b2 meets a0 — the same 96 MMAs per 128 x 256 tile as the concatenated form, from half the operand bytes.
+constexpr int A3_BYTES = 3 * A_BYTES;
+constexpr int SMEM6_BYTES = 2 * A3_BYTES + 3 * B_BYTES + 1024 + 256;
+static_assert(4 * 32 * ((BN < 128 ? BN : 128) + 4) * 4 <= 2 * A3_BYTES + 3 * B_BYTES, "epilogue staging");
+
+__global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                const __grid_constant__ CUtensorMap tmB,
+                                                                const GemmParams p, const int Kp)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sa = smem;                   // 2 A buffers of 3 parts
+    uint8_t* sb = smem + 2 * A3_BYTES;    // 3 B stages (stage q = part q)
+    uint64_t* afull = reinterpret_cast<uint64_t*>(sb + 3 * B_BYTES);
+    uint64_t* aempty = afull + 2;
+    uint64_t* bfull = aempty + 2;
+    uint64_t* bempty = bfull + 3;
+    uint64_t* accum = bempty + 3;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int nk = Kp / BK;
+
+    if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmB) : "memory");
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&afull[i], 1);
+            mbar_init(&aempty[i], 1);
+        }
+        for (int i = 0; i < 3; i++) {
+            mbar_init(&bfull[i], 1);
+            mbar_init(&bempty[i], 1);
+        }
+        mbar_init(accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (threadIdx.x == 0) {  // TMA producer: per chunk j, the A triple, then b0, b1, b2
+        int ja = 0, jb = 0;  // chunks whose A / B loads were issued
+        for (int j = 0; j < nk; j++) {
+            const int a = j & 1;
+            if (j >= 2 && !mbar_wait(&aempty[a], ((j >> 1) - 1) & 1, p.err)) break;
+            mbar_expect_tx(&afull[a], A3_BYTES);
+            for (int pt = 0; pt < 3; pt++)
+                tma_load_2d(sa + a * A3_BYTES + pt * A_BYTES, &tmA, pt * Kp + j * BK, m0, &afull[a]);
+            ja = j + 1;
+            bool ok = true;
+            for (int q = 0; q < 3 && ok; q++) {
+                if (j >= 1 && !mbar_wait(&bempty[q], (j - 1) & 1, p.err)) { ok = false; break; }
+                mbar_expect_tx(&bfull[q], B_BYTES);
+                tma_load_2d(sb + q * B_BYTES, &tmB, q * Kp + j * BK, n0, &bfull[q]);
+            }
+            if (!ok) break;
+            jb = j + 1;
+        }
+        // every copy started has landed before the CTA can leave
+        for (int j = ja > 2 ? ja - 2 : 0; j < ja; j++) mbar_wait(&afull[j & 1], (j >> 1) & 1, p.err);
+        if (jb > 0)
+            for (int q = 0; q < 3; q++) mbar_wait(&bfull[q], (jb - 1) & 1, p.err);
+    } else if (threadIdx.x == 32) {  // MMA issuer
+        bool ok = true, first = true;
+        for (int j = 0; j < nk && ok; j++) {
+            const int a = j & 1;
+            if (!mbar_wait(&afull[a], (j >> 1) & 1, p.err)) break;
+            const uint32_t abase = smem_u32(sa + a * A3_BYTES);
+            for (int q = 0; q < 3; q++) {
+                if (!mbar_wait(&bfull[q], j & 1, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t bq = smem_u32(sb + q * B_BYTES);
+                for (int pt = 0; pt < 3 - q; pt++) {  // b0: a0 a1 a2; b1: a0 a1; b2: a0
+                    const uint32_t ap = abase + pt * A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; kk++) {
+                        umma_bf16(tmem, sw128_kmajor_desc(ap + 32 * kk), sw128_kmajor_desc(bq + 32 * kk), first ? 0u : 1u);
+                        first = false;
+                    }
+                }
+                umma_commit(&bempty[q]);
+            }
+            if (ok) umma_commit(&aempty[a]);
+        }
+        umma_commit(accum);
+    }
+    epilogue(p, accum, tmem, smem, m0, n0, warp, lane);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -278,5 +416,30 @@ extern "C" int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t
     GemmParams p{C, ldc, M, N, Kd, alpha, beta, err};
     dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
     gemm_bf16_tn_kernel<<<grid, 128, SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, p);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_gemm_bf16x6_tn(const uint16_t* A3, long long lda, const uint16_t* B3, long long ldb, float* C,
+                                  long long ldc, int M, int N, int Kp, float alpha, float beta, int* err, void* stream)
+{
+    if (M < 0 || N < 0 || Kp <= 0 || N % 16 || Kp % BK || !A3 || !B3 || !C || lda < 3LL * Kp || ldb < 3LL * Kp ||
+        ldc < N || (lda % 8) || (ldb % 8) || (ldc % 4) || ((uintptr_t)A3 & 15) || ((uintptr_t)B3 & 15) ||
+        ((uintptr_t)C & 15))
+        return -1;
+    if (M == 0 || N == 0) return 0;
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, A3, M, 3 * Kp, lda, BM) || !make_map(&tb, B3, N, 3 * Kp, ldb, BN)) return -1;
+    static std::atomic<int> attr_set[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(gemm_bf16x6_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM6_BYTES) !=
+            cudaSuccess)
+            return -1;
+        attr_set[dev].store(1, std::memory_order_release);
+    }
+    GemmParams p{C, ldc, M, N, Kp, alpha, beta, err};
+    dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+    gemm_bf16x6_tn_kernel<<<grid, 128, SMEM6_BYTES, (cudaStream_t)stream>>>(ta, tb, p, Kp);
     return (int)cudaGetLastError();
 }

@@ -232,19 +232,20 @@ __global__ void __launch_bounds__(256) ldlq_bcat_kernel(const float* __restrict_
     }
 }
 
-// The same operands transposed, for the tensor-core GEMM (both operands K-major): block b's [N_b, 1536] matrix with
-// row n = [u0 u1 u0 u2 u1 u0] of column c1 + n of U[256 b : 256 b + 256, :], i.e. out_b[n][256 s + i] = part_s(U[c0 + i][c1 + n]).
-// A 32 x 32 tile of U per CTA (32 x 8 threads): read along n (coalesced), split, transposed through shared memory,
-// written along i (64 bytes per slot and row).  blockIdx = (n tile, i tile, block b).
-__global__ void __launch_bounds__(256) ldlq_bcat_t_kernel(const float* __restrict__ U, long long ldU, int K,
-                                                          uint16_t* __restrict__ out)
+// The right operands of every block's update in the compact three-part form of the tensor-core GEMM
+// (ltq_gemm_bf16x6_tn, both operands K-major): block b's [N_b, 768] matrix with row n = [u0 u1 u2], the three-way split
+// of column c1 + n of U[256 b : 256 b + 256, :], i.e. out_b[n][256 p + i] = part_p(U[c0 + i][c1 + n]), at element offset
+// 768 * sum_{b' < b} N_b'.  A 32 x 32 tile of U per CTA (32 x 8 threads): read along n (coalesced), split, transposed
+// through shared memory, written along i (64 bytes per part and row).  blockIdx = (n tile, i tile, block b).
+__global__ void __launch_bounds__(256) ldlq_bcat3_t_kernel(const float* __restrict__ U, long long ldU, int K,
+                                                           uint16_t* __restrict__ out)
 {
     __shared__ uint16_t sp[3][32][34];  // [part][n][i]
     const int b = blockIdx.z, c0 = 256 * b, c1 = c0 + 256, nb = K - c1;
     const int n0 = 32 * blockIdx.x, i0 = 32 * blockIdx.y;
     if (n0 >= nb) return;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const long long off = 1536LL * ((long long)b * K - 128LL * b * (b + 1));
+    const long long off = 768LL * ((long long)b * K - 128LL * b * (b + 1));
 #pragma unroll
     for (int q = 0; q < 4; q++) {
         const int i = ty + 8 * q;
@@ -255,19 +256,19 @@ __global__ void __launch_bounds__(256) ldlq_bcat_t_kernel(const float* __restric
         sp[2][tx][i] = p2;
     }
     __syncthreads();
-    constexpr int part_of_slot[6] = {0, 1, 0, 2, 1, 0};
 #pragma unroll
     for (int q = 0; q < 4; q++) {
         const int n = ty + 8 * q;
-        uint16_t* row = out + off + (long long)(n0 + n) * 1536 + i0 + tx;
+        uint16_t* row = out + off + (long long)(n0 + n) * 768 + i0 + tx;
 #pragma unroll
-        for (int sl = 0; sl < 6; sl++) row[256 * sl] = sp[part_of_slot[sl]][n][tx];
+        for (int pt = 0; pt < 3; pt++) row[256 * pt] = sp[pt][n][tx];
     }
 }
 
 // after block [c0, c0 + 256): W_hat = d * G, d_h = fp16(d), e = w - W_hat (the reference's operations, same bits), and
 // for the update err = e @ Uinv (Uinv upper triangular: err[k] = sum_{i <= k} e[i] Uinv[i][k], i ascending, fma) split
 // into acat [M, 1536] = [e0 e0 e1 e0 e1 e2].  One CTA per 16 rows, thread k = column k.
+template <bool COMPACT>
 __global__ void __launch_bounds__(256) ldlq_inter_kernel(const float* __restrict__ w, long long ld_w,
                                                          const float* __restrict__ d_rb, long long ld_d,
                                                          const float* __restrict__ G, long long ldG,
@@ -321,8 +322,13 @@ __global__ void __launch_bounds__(256) ldlq_inter_kernel(const float* __restrict
     for (int r = 0; r < 16; r++) {
         uint16_t p0, p1, p2;
         split3_bf16(acc[r], p0, p1, p2);
-        uint16_t* a = acat + (r0 + r) * 1536 + k;
-        a[0] = p0; a[256] = p0; a[512] = p1; a[768] = p0; a[1024] = p1; a[1280] = p2;
+        if constexpr (COMPACT) {  // [e0 e1 e2], row stride 768
+            uint16_t* a = acat + (r0 + r) * 768 + k;
+            a[0] = p0; a[256] = p1; a[512] = p2;
+        } else {  // the six slots [e0 e0 e1 e0 e1 e2], row stride 1536
+            uint16_t* a = acat + (r0 + r) * 1536 + k;
+            a[0] = p0; a[256] = p0; a[512] = p1; a[768] = p0; a[1024] = p1; a[1280] = p2;
+        }
     }
 }
 
@@ -657,7 +663,7 @@ extern "C" int ltq_ldlq_bcat_t(const float* U, long long ldU, int K, uint16_t* b
 {
     if (K < 512 || K % 256 || ldU < K || !U || !bcat || ((uintptr_t)bcat & 15)) return -1;
     const dim3 grid((K - 256) / 32, 8, K / 256 - 1);
-    ldlq_bcat_t_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(U, ldU, K, bcat);
+    ldlq_bcat3_t_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(U, ldU, K, bcat);
     return (int)cudaGetLastError();
 }
 
@@ -678,8 +684,20 @@ extern "C" int ltq_ldlq_inter(const float* w_blk, long long ld_w, const float* d
     if (M < 0 || M % 16 || !w_blk || !d_rb || !G || !what || (acat && (!Uinv || ((uintptr_t)Uinv & 15) || ldUi % 4)))
         return -1;
     if (M == 0) return 0;
-    ldlq_inter_kernel<<<M / 16, 256, 0, (cudaStream_t)stream>>>(w_blk, ld_w, d_rb, ld_d, G, ldG, Uinv, ldUi, what,
-                                                               ld_what, d_h, ld_dh, acat);
+    ldlq_inter_kernel<false><<<M / 16, 256, 0, (cudaStream_t)stream>>>(w_blk, ld_w, d_rb, ld_d, G, ldG, Uinv, ldUi,
+                                                                      what, ld_what, d_h, ld_dh, acat);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_ldlq_inter3(const float* w_blk, long long ld_w, const float* d_rb, long long ld_d, const float* G,
+                               long long ldG, const float* Uinv, long long ldUi, int M, float* what, long long ld_what,
+                               uint16_t* d_h, long long ld_dh, uint16_t* acat3, void* stream)
+{
+    if (M < 0 || M % 16 || !w_blk || !d_rb || !G || !what || (acat3 && (!Uinv || ((uintptr_t)Uinv & 15) || ldUi % 4)))
+        return -1;
+    if (M == 0) return 0;
+    ldlq_inter_kernel<true><<<M / 16, 256, 0, (cudaStream_t)stream>>>(w_blk, ld_w, d_rb, ld_d, G, ldG, Uinv, ldUi,
+                                                                     what, ld_what, d_h, ld_dh, acat3);
     return (int)cudaGetLastError();
 }
 

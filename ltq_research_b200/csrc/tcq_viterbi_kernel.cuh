@@ -557,20 +557,41 @@ static __device__ __forceinline__ void build_err_u(float* myerr, const float* s_
 {
     constexpr int NV = NL / 2, EW = NL * NP;
     __syncwarp();
+    if constexpr (UC > 0) {
+        // EW divides 32, so every entry of this lane has the same (label, class) pair: its table values and its NV
+        // destination offsets are loaded / computed once (the stores below could alias s_tab for the compiler, which
+        // then reloaded the table for every entry); the arithmetic per entry is unchanged
+        const int lb = (lane % EW) / NP, pc = lane % NP;
+        constexpr int NU = MD ? UC / 2 : UC;
+        float tv[NU];
+#pragma unroll
+        for (int k = 0; k < NU; k++) tv[k] = s_tab[lb * UC + (MD ? pc + 2 * k : k)];
+        int doff[NV];
+#pragma unroll
+        for (int P = 0; P < NV; P++) doff[P] = P * EW + (lb ^ (P << 1)) * NP + pc;
+        for (int tt = lane / EW; tt < sub; tt += 32 / EW) {
+            const int t = t0 + tt;
+            const float x = s_x[t];
+            float e = BIG;
+#pragma unroll
+            for (int k = 0; k < NU; k++) {
+                const float d = __fmaf_rn(-gain, tv[k], x);
+                e = fminf(e, __fmul_rn(d, d));
+            }
+            e = __fmul_rn(e, s_w[t]);
+            float* dst = myerr + (size_t)tt * NV * EW;
+#pragma unroll
+            for (int P = 0; P < NV; P++) dst[doff[P]] = e;
+        }
+        __syncwarp();
+        return;
+    }
     for (int it = lane; it < sub * NL * NP; it += 32) {
         const int tt = it / (NL * NP), lb = (it / NP) % NL, pc = it % NP;
         const int t = t0 + tt;
         const float x = s_x[t];
         float e;
-        if constexpr (UC > 0) {
-            const float* tl = s_tab + lb * UC + (MD ? pc : 0);
-            e = BIG;
-#pragma unroll
-            for (int u = 0; u < UC; u += MD ? 2 : 1) {
-                const float d = __fmaf_rn(-gain, tl[u], x);
-                e = fminf(e, __fmul_rn(d, d));
-            }
-        } else {
+        {
             const bool hi = !MD && mix > 0 && ((t / mix) & 1);
             if (MD) e = branch_err(x, gain, s_tab + lb * U, pc, 2, U);
             else if (hi) e = branch_err(x, gainhi, s_tabhi + lb * U_hi, 0, 1, U_hi);

@@ -528,11 +528,13 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
         # tensor-core GEMM W_work[:, c1:] -= acat @ bcat_b
         brun = _BlockRunner(spec_name, M, device)
         dwc = diag_w.float().contiguous()
-        bcat = torch.empty(max(int(L.ltq_ldlq_bcat_elems(K)), 8), dtype=torch.bfloat16, device=device)
-        if nblocks > 1:  # every block's right operand, K-major for the tensor-core GEMM
+        # every block's right operand [u0 u1 u2] (K-major), built once per matrix; each block's left operand
+        # [e0 e1 e2] of err = (w_blk - what) @ U_blk^-1; the update is the six-product tensor-core GEMM of the two
+        bcat = torch.empty(max(int(L.ltq_ldlq_bcat_elems(K)) // 2, 8), dtype=torch.bfloat16, device=device)
+        if nblocks > 1:
             _check(L.ltq_ldlq_bcat_t(ptr(Uc), Uc.stride(0), K, ptr(bcat), st), "ltq_ldlq_bcat_t")
         gerr = gemm_error_flag(device)
-        acat = torch.empty((M, 6 * QK_K), dtype=torch.bfloat16, device=device)
+        acat = torch.empty((M, 3 * QK_K), dtype=torch.bfloat16, device=device)
         U_blks_inv = U_blks_inv.contiguous()  # row-major blocks (a batched triangular solve may return column-major)
         off = 0
         for ibl in range(nblocks):
@@ -540,17 +542,17 @@ def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool =
             U_blk_inv = U_blks_inv[ibl]
             brun.run(W_work, c0, d_rb_all, ibl, dwc, Uc, U_blk_inv, G, idx, gi)
             last = c1 >= K
-            _check(L.ltq_ldlq_inter(ptr(W_work) + 4 * c0, W_work.stride(0), ptr(d_rb_all) + 4 * ibl, d_rb_all.stride(0),
+            _check(L.ltq_ldlq_inter3(ptr(W_work) + 4 * c0, W_work.stride(0), ptr(d_rb_all) + 4 * ibl, d_rb_all.stride(0),
                                     ptr(G) + 4 * c0, G.stride(0), ptr(U_blk_inv), U_blk_inv.stride(0), M,
                                     ptr(W_hat_rot) + 4 * c0, W_hat_rot.stride(0), ptr(d_full) + 2 * ibl,
                                     d_full.stride(0), None if last else ptr(acat), st), "ltq_ldlq_inter")
             if not last:
-                # W_work[:, c1:] -= acat @ bcat_b^T on the tensor cores (ltq_gemm_bf16_tn, tcgen05)
+                # W_work[:, c1:] -= six-product(acat, bcat_b) on the tensor cores (ltq_gemm_bf16x6_tn, tcgen05)
                 nb = K - c1
-                _check(L.ltq_gemm_bf16_tn(ptr(acat), 6 * QK_K, ptr(bcat) + 2 * off, 6 * QK_K, ptr(W_work) + 4 * c1,
-                                          W_work.stride(0), M, nb, 6 * QK_K, -1.0, 1.0, ptr(gerr), st),
-                       "ltq_gemm_bf16_tn")
-                off += 6 * QK_K * nb
+                _check(L.ltq_gemm_bf16x6_tn(ptr(acat), 3 * QK_K, ptr(bcat) + 2 * off, 3 * QK_K, ptr(W_work) + 4 * c1,
+                                            W_work.stride(0), M, nb, QK_K, -1.0, 1.0, ptr(gerr), st),
+                       "ltq_gemm_bf16x6_tn")
+                off += 3 * QK_K * nb
             yield
         return d_full, W_hat_rot, group
 

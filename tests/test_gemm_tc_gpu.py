@@ -1,14 +1,15 @@
-"""GPU: the tensor-core GEMM (ltq_gemm_bf16_tn: tcgen05.mma, TMA, tensor-memory accumulator) and the K-major operands of
-the LDLQ inter-block update (ltq_ldlq_bcat_t).
+"""GPU: the tensor-core GEMMs (ltq_gemm_bf16_tn and the six-product ltq_gemm_bf16x6_tn: tcgen05.mma, TMA, tensor-memory
+accumulator) and the compact K-major operands of the LDLQ inter-block update (ltq_ldlq_bcat_t, ltq_ldlq_inter3).
 
 * Small-integer operands make every product and every partial sum exact in fp32, so C must equal the integer reference
   exactly: any error in the shared-memory descriptors, the swizzle, the K stepping, the tensor-memory read-back or the
   edge handling shows up as a mismatch.  Ragged M, N not a multiple of the 256-wide tile, padded row strides, a strided
   C view, beta 0 / 1 / 0.5, alpha -1 / 1.
 * Real-valued operands: within the fp32 accumulation bound |C - C64| <= (Kd + 2) u (|alpha| |A||B|^T + |beta C|).
-* ltq_ldlq_bcat_t is ltq_ldlq_bcat's operand transposed, block by block, bit for bit; the inter-block update through
-  the tensor-core GEMM agrees with the same six-product form through torch (cuBLAS) within the fp32 bound of the
-  six-product sum.
+* The six-product kernel from three-part operands equals the concatenated six-slot product exactly on integers.
+* ltq_ldlq_bcat_t / ltq_ldlq_inter3 hold the three parts of ltq_ldlq_bcat's / ltq_ldlq_inter's six slots (transposed
+  for the right operand), bit for bit; the inter-block update through the six-product tensor-core GEMM agrees with the
+  same six-product form through torch (cuBLAS) within the fp32 bound of the 1536-term sum.
 """
 import pytest
 import torch
@@ -71,6 +72,39 @@ def test_gemm_rejects_bad_arguments(cuda_dev):
     assert _gemm(A, A, C, 1.0, 0.0, M=0) == 0            # empty: nothing launched
 
 
+def _gemm6(A3, B3, C, alpha, beta, Kp, err=None):
+    from ltq_research_b200 import _lib
+    return _lib.lib().ltq_gemm_bf16x6_tn(A3.data_ptr(), A3.stride(0), B3.data_ptr(), B3.stride(0), C.data_ptr(),
+                                         C.stride(0), A3.shape[0], B3.shape[0], Kp, alpha, beta,
+                                         None if err is None else err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+
+
+def _six(X3, Kp, order):
+    """The concatenated six-slot operand of three parts: left [x0 x0 x1 x0 x1 x2], right [x0 x1 x0 x2 x1 x0]."""
+    p = [X3[:, i * Kp:(i + 1) * Kp] for i in range(3)]
+    idx = (0, 1, 0, 2, 1, 0) if order else (0, 0, 1, 0, 1, 2)
+    return torch.cat([p[i] for i in idx], dim=1).contiguous()
+
+
+@pytest.mark.parametrize("M,N,Kp", [(16, 16, 64), (1040, 272, 256), (300, 2816, 256), (2048, 512, 128)])
+def test_gemm6_exact_on_small_integers(cuda_dev, M, N, Kp):
+    g = torch.Generator(device=cuda_dev).manual_seed(M + 3 * N + Kp)
+    A3 = torch.randint(-3, 4, (M, 3 * Kp), generator=g, device=cuda_dev).to(torch.bfloat16)
+    B3 = torch.randint(-3, 4, (N, 3 * Kp + 8), generator=g, device=cuda_dev).to(torch.bfloat16)[:, :3 * Kp]
+    C0 = torch.randint(-1000, 1000, (M, N), generator=g, device=cuda_dev).float()
+    a = [A3[:, i * Kp:(i + 1) * Kp].double() for i in range(3)]
+    b = [B3[:, i * Kp:(i + 1) * Kp].double() for i in range(3)]
+    six = a[0] @ b[0].T + a[0] @ b[1].T + a[1] @ b[0].T + a[0] @ b[2].T + a[1] @ b[1].T + a[2] @ b[0].T
+    err = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    C = C0.clone()
+    assert _gemm6(A3, B3, C, -1.0, 1.0, Kp, err) == 0
+    C2 = C0.clone()
+    assert _gemm(_six(A3, Kp, 0), _six(B3, Kp, 1), C2, -1.0, 1.0) == 0
+    torch.cuda.synchronize()
+    assert int(err) == 0
+    assert torch.equal(C.double(), C0.double() - six) and torch.equal(C, C2)
+
+
 @pytest.mark.parametrize("K", [512, 1280, 3072])
 def test_bcat_t_is_bcat_transposed(cuda_dev, K):
     from ltq_research_b200 import _lib
@@ -79,41 +113,71 @@ def test_bcat_t_is_bcat_transposed(cuda_dev, K):
     U = torch.triu(torch.randn(K, K, generator=g, device=cuda_dev))
     n = int(L.ltq_ldlq_bcat_elems(K))
     a = torch.empty(n, dtype=torch.int16, device=cuda_dev)
-    b = torch.empty(n, dtype=torch.int16, device=cuda_dev)
+    b = torch.empty(n // 2, dtype=torch.int16, device=cuda_dev)
     st = torch.cuda.current_stream().cuda_stream
     assert L.ltq_ldlq_bcat(U.data_ptr(), K, K, a.data_ptr(), st) == 0
     assert L.ltq_ldlq_bcat_t(U.data_ptr(), K, K, b.data_ptr(), st) == 0
     torch.cuda.synchronize()
-    off = 0
+    off6 = off3 = 0
     for blk in range(K // 256 - 1):
         nb = K - 256 * (blk + 1)
-        assert torch.equal(a[off:off + 1536 * nb].view(1536, nb).T, b[off:off + 1536 * nb].view(nb, 1536)), blk
-        off += 1536 * nb
+        six = a[off6:off6 + 1536 * nb].view(1536, nb)
+        three = b[off3:off3 + 768 * nb].view(nb, 768)
+        for part, slot in ((0, 0), (1, 1), (2, 3)):  # the right slots [u0 u1 u0 u2 u1 u0]
+            assert torch.equal(six[256 * slot:256 * slot + 256].T, three[:, 256 * part:256 * part + 256]), (blk, part)
+        off6 += 1536 * nb
+        off3 += 768 * nb
+
+
+def test_inter3_is_inter_compact(cuda_dev):
+    from ltq_research_b200 import _lib
+    L = _lib.lib()
+    g = torch.Generator(device=cuda_dev).manual_seed(8)
+    M = 64
+    w = torch.randn(M, 256, generator=g, device=cuda_dev)
+    d = torch.rand(M, 1, generator=g, device=cuda_dev) + 0.5
+    G = torch.randn(M, 256, generator=g, device=cuda_dev)
+    Ui = torch.triu(torch.randn(256, 256, generator=g, device=cuda_dev)) / 8 + torch.eye(256, device=cuda_dev)
+    st = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for fn, width in ((L.ltq_ldlq_inter, 1536), (L.ltq_ldlq_inter3, 768)):
+        what = torch.empty(M, 256, device=cuda_dev)
+        dh = torch.empty(M, 1, dtype=torch.int16, device=cuda_dev)
+        ac = torch.empty(M, width, dtype=torch.int16, device=cuda_dev)
+        assert fn(w.data_ptr(), 256, d.data_ptr(), 1, G.data_ptr(), 256, Ui.data_ptr(), 256, M, what.data_ptr(), 256,
+                  dh.data_ptr(), 1, ac.data_ptr(), st) == 0
+        outs.append((what, dh, ac))
+    torch.cuda.synchronize()
+    (w6, d6, a6), (w3, d3, a3) = outs
+    assert torch.equal(w6, w3) and torch.equal(d6, d3)
+    for part, slot in ((0, 0), (1, 2), (2, 5)):  # the left slots [e0 e0 e1 e0 e1 e2]
+        assert torch.equal(a6[:, 256 * slot:256 * slot + 256], a3[:, 256 * part:256 * part + 256]), part
 
 
 def test_inter_block_update_tensor_core_vs_library(cuda_dev):
-    """W[:, c1:] -= acat @ bcat_b for one block: the tcgen05 GEMM against torch's GEMM of the same bf16 operands,
-    both within the fp32 bound of the 1536-term sum."""
+    """W[:, c1:] -= six-product(acat3, bcat3_b) for one block: the tcgen05 six-product GEMM against torch's GEMM of the
+    concatenated six-slot operands, both within the fp32 bound of the 1536-term sum."""
     from ltq_research_b200 import _lib
     L = _lib.lib()
     g = torch.Generator(device=cuda_dev).manual_seed(5)
     M, K = 1024, 1024
     U = torch.triu(torch.randn(K, K, generator=g, device=cuda_dev)) / 16
-    n = int(L.ltq_ldlq_bcat_elems(K))
+    n = int(L.ltq_ldlq_bcat_elems(K)) // 2
     bt = torch.empty(n, dtype=torch.bfloat16, device=cuda_dev)
     st = torch.cuda.current_stream().cuda_stream
     assert L.ltq_ldlq_bcat_t(U.data_ptr(), K, K, bt.data_ptr(), st) == 0
-    acat = torch.randn(M, 1536, generator=g, device=cuda_dev).to(torch.bfloat16)
+    acat3 = torch.randn(M, 768, generator=g, device=cuda_dev).to(torch.bfloat16)
     W = torch.randn(M, K, generator=g, device=cuda_dev)
     nb = K - 256
-    Bt = bt[:1536 * nb].view(nb, 1536)
+    B3 = bt[:768 * nb].view(nb, 768)
     W1 = W.clone()
-    assert _gemm(acat, Bt, W1[:, 256:], -1.0, 1.0) == 0
+    assert _gemm6(acat3, B3, W1[:, 256:], -1.0, 1.0, 256) == 0
+    A6, B6 = _six(acat3, 256, 0), _six(B3, 256, 1)
     W2 = W.clone()
-    torch.addmm(W2[:, 256:], acat, Bt.T, out_dtype=torch.float32, beta=1, alpha=-1, out=W2[:, 256:])
+    torch.addmm(W2[:, 256:], A6, B6.T, out_dtype=torch.float32, beta=1, alpha=-1, out=W2[:, 256:])
     torch.cuda.synchronize()
-    ref = W[:, 256:].double() - acat.double() @ Bt.double().T
-    bound = (1536 + 2) * U32 * (acat.double().abs() @ Bt.double().abs().T + W[:, 256:].double().abs())
+    ref = W[:, 256:].double() - A6.double() @ B6.double().T
+    bound = (1536 + 2) * U32 * (A6.double().abs() @ B6.double().abs().T + W[:, 256:].double().abs())
     for got in (W1, W2):
         assert torch.equal(got[:, :256], W[:, :256])
         assert ((got[:, 256:].double() - ref).abs() <= bound).all()
