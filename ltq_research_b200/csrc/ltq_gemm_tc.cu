@@ -134,6 +134,61 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// Epilogue for beta = 0 or 1 without reading C: per warp, 32 rows x 32 columns at a time go from tensor memory (thread
+// = row) to a 4 KB shared buffer in the 128-byte-swizzled layout of a {32 x 32} fp32 box (row r's 16-byte chunk k at
+// chunk k ^ (r & 7): conflict-free 16-byte stores), then one lane has TMA store the box into C (beta 0) or add it to C
+// in L2 (beta 1, cp.reduce.async.bulk.tensor .add: C + alpha acc in one rounding).  Two buffers per warp alternate;
+// rows >= M and columns >= N of a box are clipped by the tensor map.  Deterministic: one CTA owns each element.
+__device__ __forceinline__ void tma_store_box(const CUtensorMap* map, const void* src, int x, int y, bool reduce)
+{
+    if (reduce)
+        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(map),
+                     "r"(smem_u32(src)), "r"(x), "r"(y)
+                     : "memory");
+    else
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(map),
+                     "r"(smem_u32(src)), "r"(x), "r"(y)
+                     : "memory");
+    asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensorMap* tmC, bool reduce, uint64_t* accum,
+                                             uint32_t tmem, uint8_t* smem, int m0, int n0, int warp, int lane)
+{
+    const bool ok = mbar_wait(accum, 0, p.err);
+    __syncwarp();
+    tc_fence_after();
+    if (!ok) return;
+    uint8_t* wbuf = smem + warp * 8192;
+    const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+    int nbox = 0;
+    for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= p.N) break;  // warp-uniform
+        float v[16], w[16];
+        tmem_ld16(tl + c, v);
+        tmem_ld16(tl + c + 16, w);
+        uint8_t* buf = wbuf + (nbox & 1) * 4096;
+        if (nbox >= 2) {  // the box stored from this buffer two boxes ago has been read out of shared memory
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
+            __syncwarp();
+        }
+        uint8_t* row = buf + lane * 128;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            *reinterpret_cast<float4*>(row + ((q ^ (lane & 7)) << 4)) =
+                make_float4(p.alpha * v[4 * q], p.alpha * v[4 * q + 1], p.alpha * v[4 * q + 2], p.alpha * v[4 * q + 3]);
+            *reinterpret_cast<float4*>(row + (((q + 4) ^ (lane & 7)) << 4)) =
+                make_float4(p.alpha * w[4 * q], p.alpha * w[4 * q + 1], p.alpha * w[4 * q + 2], p.alpha * w[4 * q + 3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // the writes, visible to the TMA engine
+        __syncwarp();
+        if (lane == 0) tma_store_box(tmC, buf, n0 + c, m0 + 32 * warp, reduce);
+        nbox++;
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+    __syncwarp();
+}
+
 // Epilogue, in halves of 128 columns: each warp moves its 32 rows x 16 columns at a time from tensor memory (thread =
 // row) into a row-major shared tile (the pipeline's buffers are free once the accumulator is complete), then writes C
 // row by row, a whole 512-byte row segment per warp instruction (coalesced read-modify-write), C = beta C + alpha acc.
@@ -183,7 +238,8 @@ __device__ __forceinline__ void epilogue(const GemmParams& p, uint64_t* accum, u
 
 __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA,
                                                               const __grid_constant__ CUtensorMap tmB,
-                                                              const GemmParams p)
+                                                              const __grid_constant__ CUtensorMap tmC,
+                                                              const GemmParams p, const int cmode)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -198,6 +254,7 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_const
     if (threadIdx.x == 0) {
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmA) : "memory");
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmB) : "memory");
+        if (cmode) asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmC) : "memory");
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
@@ -216,7 +273,11 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_const
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (threadIdx.x == 0) {  // TMA producer
+    // roles: lane 0 of warp 0 feeds the pipeline, lane 0 of warp 1 issues the MMAs; their warps' other lanes wait at
+    // the warp's own barrier (not on an mbarrier: a spinning sibling path would be serialised with the role's path and
+    // delay it), then every warp runs the epilogue
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
         int issued = 0;
         for (int k = 0; k < nk; k++) {
             const int s = k % STAGES;
@@ -230,7 +291,10 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_const
         // its parity until the barrier completes the next one, which needs a new arrive from this thread)
         for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; k++)
             mbar_wait(&full[k % STAGES], (k / STAGES) & 1, p.err);
-    } else if (threadIdx.x == 32) {  // MMA issuer
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
         for (int k = 0; k < nk; k++) {
             const int s = k % STAGES;
             if (!mbar_wait(&full[s], (k / STAGES) & 1, p.err)) break;
@@ -242,9 +306,12 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_const
             umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
         umma_commit(accum);  // arrives when every MMA issued above has completed
+        }
+        __syncwarp();
     }
 
-    epilogue(p, accum, tmem, smem, m0, n0, warp, lane);
+    if (cmode == 0) epilogue(p, accum, tmem, smem, m0, n0, warp, lane);
+    else epilogue_tma(p, &tmC, cmode == 2, accum, tmem, smem, m0, n0, warp, lane);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -265,7 +332,8 @@ static_assert(4 * 32 * ((BN < 128 ? BN : 128) + 4) * 4 <= 2 * A3_BYTES + 3 * B_B
 
 __global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                 const __grid_constant__ CUtensorMap tmB,
-                                                                const GemmParams p, const int Kp)
+                                                                const __grid_constant__ CUtensorMap tmC,
+                                                                const GemmParams p, const int cmode, const int Kp)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -284,6 +352,7 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_con
     if (threadIdx.x == 0) {
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmA) : "memory");
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmB) : "memory");
+        if (cmode) asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmC) : "memory");
         for (int i = 0; i < 2; i++) {
             mbar_init(&afull[i], 1);
             mbar_init(&aempty[i], 1);
@@ -306,7 +375,8 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (threadIdx.x == 0) {  // TMA producer: per chunk j, the A triple, then b0, b1, b2
+    if (warp == 0) {  // roles as in gemm_bf16_tn_kernel: lane 0 of warp 0 / warp 1, the siblings at __syncwarp
+        if (lane == 0) {  // TMA producer: per chunk j, the A triple, then b0, b1, b2
         int ja = 0, jb = 0;  // chunks whose A / B loads were issued
         for (int j = 0; j < nk; j++) {
             const int a = j & 1;
@@ -328,7 +398,10 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_con
         for (int j = ja > 2 ? ja - 2 : 0; j < ja; j++) mbar_wait(&afull[j & 1], (j >> 1) & 1, p.err);
         if (jb > 0)
             for (int q = 0; q < 3; q++) mbar_wait(&bfull[q], (jb - 1) & 1, p.err);
-    } else if (threadIdx.x == 32) {  // MMA issuer
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
         bool ok = true, first = true;
         for (int j = 0; j < nk && ok; j++) {
             const int a = j & 1;
@@ -351,8 +424,11 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_con
             if (ok) umma_commit(&aempty[a]);
         }
         umma_commit(accum);
+        }
+        __syncwarp();
     }
-    epilogue(p, accum, tmem, smem, m0, n0, warp, lane);
+    if (cmode == 0) epilogue(p, accum, tmem, smem, m0, n0, warp, lane);
+    else epilogue_tma(p, &tmC, cmode == 2, accum, tmem, smem, m0, n0, warp, lane);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -376,6 +452,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     }
     return f;
 }
+
+// 2-D tensor map of the fp32 output C [rows, cols] (row stride ld elements) for the epilogue's {32 x 32} boxes, 128-byte
+// swizzle
+bool make_map_c(CUtensorMap* m, const float* base, int rows, int cols, long long ld)
+{
+    auto f = encode_fn();
+    if (!f) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// epilogue mode: 1 TMA store (beta 0), 2 TMA reduce-add (beta 1), 0 read-modify-write (any other beta)
+int c_mode(float beta) { return beta == 0.f ? 1 : (beta == 1.f ? 2 : 0); }
 
 // 2-D tensor map of a row-major bf16 matrix [rows, cols] (row stride ld elements), box [box_rows, 64] with the
 // 128-byte swizzle; out-of-range rows and columns read as zero
@@ -413,9 +507,12 @@ extern "C" int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t
             return -1;
         attr_set[dev].store(1, std::memory_order_release);
     }
+    const int cm = c_mode(beta);
+    CUtensorMap tc{};
+    if (cm && !make_map_c(&tc, C, M, N, ldc)) return -1;
     GemmParams p{C, ldc, M, N, Kd, alpha, beta, err};
     dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
-    gemm_bf16_tn_kernel<<<grid, 128, SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, p);
+    gemm_bf16_tn_kernel<<<grid, 128, SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, tc, p, cm);
     return (int)cudaGetLastError();
 }
 
@@ -438,8 +535,11 @@ extern "C" int ltq_gemm_bf16x6_tn(const uint16_t* A3, long long lda, const uint1
             return -1;
         attr_set[dev].store(1, std::memory_order_release);
     }
+    const int cm = c_mode(beta);
+    CUtensorMap tc{};
+    if (cm && !make_map_c(&tc, C, M, N, ldc)) return -1;
     GemmParams p{C, ldc, M, N, Kp, alpha, beta, err};
     dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
-    gemm_bf16x6_tn_kernel<<<grid, 128, SMEM6_BYTES, (cudaStream_t)stream>>>(ta, tb, p, Kp);
+    gemm_bf16x6_tn_kernel<<<grid, 128, SMEM6_BYTES, (cudaStream_t)stream>>>(ta, tb, tc, p, cm, Kp);
     return (int)cudaGetLastError();
 }
