@@ -139,12 +139,12 @@ int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* X, long lon
  * Blocked Cholesky of the damped Hessian (src/liqk_v2.py:1078 torch.linalg.cholesky of flip(H_reg); :1163 the refit
  * system's solve), the diagonal step: the 256 x 256 block at (c0, c0) of A (row-major fp32, row stride ld, lower
  * triangle read, trailing updates of the earlier panels already applied) is factored in place (L, zeros above its
- * diagonal) and its factor inverted; xt6 [1536][256] (bf16) receives the six-slot right operand of L_blk^-T for the
- * panel product below the block, and X (optional, row stride ldx) the inverse itself at (c0, c0).  The first pivot
- * that is not positive sets *info = c0 + j + 1 when *info is 0 (LAPACK's convention).  The panel and trailing updates
- * are tensor-core GEMMs on the caller's side.
+ * diagonal) and its factor inverted; xt3 [256][768] (bf16) receives the compact right operand of the panel product
+ * below the block for ltq_gemm_bf16x3p_tn (row n = the three-way bf16 split [x0 x1 x2] of row n of X = L_blk^-1), and X
+ * (optional, row stride ldx) the inverse itself at (c0, c0).  The first pivot that is not positive sets
+ * *info = c0 + j + 1 when *info is 0 (LAPACK's convention).  The panel and trailing updates are tensor-core GEMMs.
  */
-int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt6, float* X, long long ldx, int* info, void* stream);
+int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt3, float* X, long long ldx, int* info, void* stream);
 /*
  * Tensor-core GEMM of the fast mode's fp32-accurate products (tcgen05.mma, accumulator in tensor memory, operands by
  * TMA): C[M, N] = beta * C + alpha * A[M, Kd] B[N, Kd]^T with A, B bf16 (K contiguous, row strides lda / ldb) and C
@@ -166,6 +166,26 @@ int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t* B, long l
  */
 int ltq_gemm_bf16x6_tn(const uint16_t* A3, long long lda, const uint16_t* B3, long long ldb, float* C, long long ldc,
                        int M, int N, int Kp, float alpha, float beta, int* err, void* stream);
+/*
+ * The general part-operand form, batched: for z < batch (A3 + z abs, B3 + z bbs, C + z cbs, elements),
+ *     C_z = beta C_z + alpha sum_{p + q < nq} a_p b_q^T,
+ * nq = 3 the six products above, nq = 2 the three a0 b0 + a1 b0 + a0 b1 (A3 / B3 then need only their first 2 Kp
+ * columns).  The fast mode's products with H, the refit's Gram matrix, the Cholesky panel and trailing updates and the
+ * triangular-inverse merges (src/liqk_v2.py:1074-1088, :1139-1180) run on it.  Limits as ltq_gemm_bf16x6_tn;
+ * batch <= 65535; batched strides multiples of 8 (A, B) / 4 (C) elements.  beta 0 and 1 write C by TMA store /
+ * reduce-add (no read of C; one rounding of beta C + alpha acc), other beta by a read-modify-write.
+ */
+int ltq_gemm_bf16x3p_tn(const uint16_t* A3, long long lda, long long abs, const uint16_t* B3, long long ldb,
+                        long long bbs, float* C, long long ldc, long long cbs, int M, int N, int Kp, int nq, int batch,
+                        float alpha, float beta, int* err, void* stream);
+/*
+ * The compact part operand of `batch` fp32 matrices x_z = x + z xbs (rows x cols, row stride ld): trans 0 writes
+ * out_z[r][p Kp + c] = part_p(s x_z[r][c]) (Kp >= cols), trans 1 writes out_z[c][p Kp + r] = part_p(s x_z[r][c])
+ * (Kp >= rows), zero-padded up to Kp (a multiple of 32); s = -1 when neg.  part_p: x0 = bf16(x), x1 = bf16(x - x0),
+ * x2 = bf16(x - x0 - x1).  out row stride ld_out >= 3 Kp (multiple of 4), batch stride obs; 8-byte aligned.
+ */
+int ltq_bf16x3_split(const float* x, long long ld, long long xbs, int rows, int cols, int batch, int trans, int neg,
+                     int Kp, uint16_t* out, long long ld_out, long long obs, void* stream);
 size_t ltq_ldlq_bcat_elems(int K);
 int ltq_ldlq_bcat(const float* U, long long ldU, int K, uint16_t* bcat, void* stream);
 /* the right operands in the compact three-part form of ltq_gemm_bf16x6_tn (K contiguous): block b's

@@ -46,7 +46,7 @@ static_assert(4 * 32 * ((BN < 128 ? BN : 128) + 4) * 4 <= STAGES * STAGE_BYTES, 
 
 struct GemmParams {
     float* C;
-    long long ldc;
+    long long ldc, cbs;  // row stride, batch stride (elements)
     int M, N, Kd;
     float alpha, beta;
     int* err;
@@ -79,6 +79,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err
         if (mbar_try_wait(b, parity)) return true;
     if (err) atomicExch(err, 1);
     return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
@@ -139,15 +148,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
 // chunk k ^ (r & 7): conflict-free 16-byte stores), then one lane has TMA store the box into C (beta 0) or add it to C
 // in L2 (beta 1, cp.reduce.async.bulk.tensor .add: C + alpha acc in one rounding).  Two buffers per warp alternate;
 // rows >= M and columns >= N of a box are clipped by the tensor map.  Deterministic: one CTA owns each element.
-__device__ __forceinline__ void tma_store_box(const CUtensorMap* map, const void* src, int x, int y, bool reduce)
+__device__ __forceinline__ void tma_store_box(const CUtensorMap* map, const void* src, int x, int y, int z, bool reduce)
 {
     if (reduce)
-        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(map),
-                     "r"(smem_u32(src)), "r"(x), "r"(y)
+        asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];\n" ::"l"(
+                         map),
+                     "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                      : "memory");
     else
-        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(map),
-                     "r"(smem_u32(src)), "r"(x), "r"(y)
+        asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];\n" ::"l"(map),
+                     "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                      : "memory");
     asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
 }
@@ -182,7 +192,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmParams& p, const CUtensor
         }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // the writes, visible to the TMA engine
         __syncwarp();
-        if (lane == 0) tma_store_box(tmC, buf, n0 + c, m0 + 32 * warp, reduce);
+        if (lane == 0) tma_store_box(tmC, buf, n0 + c, m0 + 32 * warp, blockIdx.z, reduce);
         nbox++;
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
@@ -219,7 +229,7 @@ __device__ __forceinline__ void epilogue(const GemmParams& p, uint64_t* accum, u
             if (row >= p.M) break;
             if (col < p.N) {
                 const float4 a = *reinterpret_cast<const float4*>(st + r * LDS + 4 * lane);
-                float* cp = p.C + (long long)row * p.ldc + col;
+                float* cp = p.C + (long long)blockIdx.z * p.cbs + (long long)row * p.ldc + col;
                 float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (p.beta != 0.f) {
                     const float4 old = *reinterpret_cast<const float4*>(cp);
@@ -320,25 +330,28 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_tn_kernel(const __grid_const
     }
 }
 
-// The six-product form of an fp32-accurate product from compact three-part operands:
-//     C = beta C + alpha (a0 b0^T + a0 b1^T + a1 b0^T + a0 b2^T + a1 b1^T + a2 b0^T)
-// with A3 = [a0 a1 a2] [M, 3 Kp] and B3 = [b0 b1 b2] [N, 3 Kp] (bf16, K contiguous; x = x0 + x1 + x2 the three-way split
-// of an fp32 operand).  Per 64-wide chunk j of Kp: the three A parts of the chunk stay in one of two A buffers
-// (3 x 16 KB) while the B parts stream through three 32 KB stages (stage q holds b_q): b0 meets a0, a1, a2; b1 meets a0,
-// a1; b2 meets a0 — the same 96 MMAs per 128 x 256 tile as the concatenated form, from half the operand bytes.
+// Products of split fp32 operands from compact part operands: A3 = [a0 a1 a2] [M, 3 Kp] and B3 = [b0 b1 b2] [N, 3 Kp]
+// (bf16, K contiguous; x = x0 + x1 + x2 the three-way split of an fp32 matrix), batched over blockIdx.z:
+//     C = beta C + alpha sum_{p + q < nq} a_p b_q^T
+// nq = 3: the six products a0 b0 + a1 b0 + a2 b0 + a0 b1 + a1 b1 + a0 b2 (an fp32-accurate product);
+// nq = 2: the three products a0 b0 + a1 b0 + a0 b1 (a product whose own size makes fp32 rounding of its terms moot).
+// Per 64-wide chunk j of Kp: the A parts of the chunk stay in one of two A buffers (3 x 16 KB) while the B parts stream
+// through three 32 KB stages (stage q holds b_q): b0 meets a0 .. a_{nq-1}, b1 meets a0 .. a_{nq-2}, ... — each A part
+// of a chunk loaded once for every B part it meets, half the operand bytes of the concatenated six-slot form.
 constexpr int A3_BYTES = 3 * A_BYTES;
 constexpr int SMEM6_BYTES = 2 * A3_BYTES + 3 * B_BYTES + 1024 + 256;
 static_assert(4 * 32 * ((BN < 128 ? BN : 128) + 4) * 4 <= 2 * A3_BYTES + 3 * B_BYTES, "epilogue staging");
 
-__global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                                const __grid_constant__ CUtensorMap tmB,
-                                                                const __grid_constant__ CUtensorMap tmC,
-                                                                const GemmParams p, const int cmode, const int Kp)
+__global__ void __launch_bounds__(128, 1) gemm_bf16x3p_tn_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                 const __grid_constant__ CUtensorMap tmB,
+                                                                 const __grid_constant__ CUtensorMap tmC,
+                                                                 const GemmParams p, const int cmode, const int Kp,
+                                                                 const int nq)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t* sa = smem;                   // 2 A buffers of 3 parts
-    uint8_t* sb = smem + 2 * A3_BYTES;    // 3 B stages (stage q = part q)
+    uint8_t* sa = smem;                   // 2 A buffers of nq parts
+    uint8_t* sb = smem + 2 * A3_BYTES;    // B stages (stage q = part q)
     uint64_t* afull = reinterpret_cast<uint64_t*>(sb + 3 * B_BYTES);
     uint64_t* aempty = afull + 2;
     uint64_t* bfull = aempty + 2;
@@ -346,7 +359,7 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_con
     uint64_t* accum = bempty + 3;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN, z = blockIdx.z;
     const int nk = Kp / BK;
 
     if (threadIdx.x == 0) {
@@ -375,55 +388,64 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16x6_tn_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {  // roles as in gemm_bf16_tn_kernel: lane 0 of warp 0 / warp 1, the siblings at __syncwarp
-        if (lane == 0) {  // TMA producer: per chunk j, the A triple, then b0, b1, b2
-        int ja = 0, jb = 0;  // chunks whose A / B loads were issued
-        for (int j = 0; j < nk; j++) {
-            const int a = j & 1;
-            if (j >= 2 && !mbar_wait(&aempty[a], ((j >> 1) - 1) & 1, p.err)) break;
-            mbar_expect_tx(&afull[a], A3_BYTES);
-            for (int pt = 0; pt < 3; pt++)
-                tma_load_2d(sa + a * A3_BYTES + pt * A_BYTES, &tmA, pt * Kp + j * BK, m0, &afull[a]);
-            ja = j + 1;
-            bool ok = true;
-            for (int q = 0; q < 3 && ok; q++) {
-                if (j >= 1 && !mbar_wait(&bempty[q], (j - 1) & 1, p.err)) { ok = false; break; }
-                mbar_expect_tx(&bfull[q], B_BYTES);
-                tma_load_2d(sb + q * B_BYTES, &tmB, q * Kp + j * BK, n0, &bfull[q]);
+    // roles as in gemm_bf16_tn_kernel: lane 0 of warp 0 loads, lane 0 of warp 1 issues the MMAs, their siblings wait at
+    // __syncwarp, then every warp runs the epilogue
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer: per chunk j, the A parts, then b0 .. b_{nq-1}
+            int ja = 0, jb = 0;  // chunks whose A / B loads were all issued
+            for (int j = 0; j < nk; j++) {
+                const int a = j & 1;
+                if (j >= 2 && !mbar_wait(&aempty[a], ((j >> 1) - 1) & 1, p.err)) break;
+                mbar_expect_tx(&afull[a], nq * A_BYTES);
+                for (int pt = 0; pt < nq; pt++)
+                    tma_load_3d(sa + a * A3_BYTES + pt * A_BYTES, &tmA, pt * Kp + j * BK, m0, z, &afull[a]);
+                ja = j + 1;
+                bool ok = true;
+                for (int q = 0; q < nq; q++) {
+                    if (j >= 1 && !mbar_wait(&bempty[q], (j - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&bfull[q], B_BYTES);
+                    tma_load_3d(sb + q * B_BYTES, &tmB, q * Kp + j * BK, n0, z, &bfull[q]);
+                }
+                if (!ok) break;
+                jb = j + 1;
             }
-            if (!ok) break;
-            jb = j + 1;
-        }
-        // every copy started has landed before the CTA can leave
-        for (int j = ja > 2 ? ja - 2 : 0; j < ja; j++) mbar_wait(&afull[j & 1], (j >> 1) & 1, p.err);
-        if (jb > 0)
-            for (int q = 0; q < 3; q++) mbar_wait(&bfull[q], (jb - 1) & 1, p.err);
+            // every copy started has landed before the CTA can leave
+            for (int j = ja > 2 ? ja - 2 : 0; j < ja; j++) mbar_wait(&afull[j & 1], (j >> 1) & 1, p.err);
+            if (jb > 0)
+                for (int q = 0; q < nq; q++) mbar_wait(&bfull[q], (jb - 1) & 1, p.err);
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
-        bool ok = true, first = true;
-        for (int j = 0; j < nk && ok; j++) {
-            const int a = j & 1;
-            if (!mbar_wait(&afull[a], (j >> 1) & 1, p.err)) break;
-            const uint32_t abase = smem_u32(sa + a * A3_BYTES);
-            for (int q = 0; q < 3; q++) {
-                if (!mbar_wait(&bfull[q], j & 1, p.err)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t bq = smem_u32(sb + q * B_BYTES);
-                for (int pt = 0; pt < 3 - q; pt++) {  // b0: a0 a1 a2; b1: a0 a1; b2: a0
-                    const uint32_t ap = abase + pt * A_BYTES;
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; kk++) {
-                        umma_bf16(tmem, sw128_kmajor_desc(ap + 32 * kk), sw128_kmajor_desc(bq + 32 * kk), first ? 0u : 1u);
-                        first = false;
+            bool ok = true, first = true;
+            for (int j = 0; j < nk && ok; j++) {
+                const int a = j & 1;
+                if (!mbar_wait(&afull[a], (j >> 1) & 1, p.err)) break;
+                const uint32_t abase = smem_u32(sa + a * A3_BYTES);
+                for (int q = 0; q < nq; q++) {
+                    if (!mbar_wait(&bfull[q], j & 1, p.err)) {
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    const uint32_t bq = smem_u32(sb + q * B_BYTES);
+                    for (int pt = 0; pt < nq - q; pt++) {
+                        const uint32_t ap = abase + pt * A_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; kk++) {
+                            umma_bf16(tmem, sw128_kmajor_desc(ap + 32 * kk), sw128_kmajor_desc(bq + 32 * kk),
+                                      first ? 0u : 1u);
+                            first = false;
+                        }
+                    }
+                    umma_commit(&bempty[q]);
                 }
-                umma_commit(&bempty[q]);
+                if (ok) umma_commit(&aempty[a]);
             }
-            if (ok) umma_commit(&aempty[a]);
-        }
-        umma_commit(accum);
+            umma_commit(accum);
         }
         __syncwarp();
     }
@@ -453,17 +475,33 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return f;
 }
 
-// 2-D tensor map of the fp32 output C [rows, cols] (row stride ld elements) for the epilogue's {32 x 32} boxes, 128-byte
-// swizzle
-bool make_map_c(CUtensorMap* m, const float* base, int rows, int cols, long long ld)
+// 3-D tensor map of the fp32 output C [batch][rows, cols] (row stride ld, batch stride bs elements) for the epilogue's
+// {32 x 32 x 1} boxes, 128-byte swizzle
+bool make_map_c(CUtensorMap* m, const float* base, int rows, int cols, long long ld, int batch, long long bs)
 {
     auto f = encode_fn();
     if (!f) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-    cuuint32_t box[2] = {32, 32};
-    cuuint32_t estr[2] = {1, 1};
-    return f(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(batch > 1 ? bs : ld * rows) * 4};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 3-D tensor map of a bf16 operand [batch][rows, cols] (row stride ld, batch stride bs elements), box
+// [1][box_rows][64], 128-byte swizzle; out-of-range rows and columns read as zero
+bool make_map3(CUtensorMap* m, const void* base, int rows, int cols, long long ld, int batch, long long bs,
+               int box_rows)
+{
+    auto f = encode_fn();
+    if (!f) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)(batch > 1 ? bs : ld * rows) * 2};
+    cuuint32_t box[3] = {BK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -509,37 +547,46 @@ extern "C" int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t
     }
     const int cm = c_mode(beta);
     CUtensorMap tc{};
-    if (cm && !make_map_c(&tc, C, M, N, ldc)) return -1;
-    GemmParams p{C, ldc, M, N, Kd, alpha, beta, err};
+    if (cm && !make_map_c(&tc, C, M, N, ldc, 1, 0)) return -1;
+    GemmParams p{C, ldc, 0, M, N, Kd, alpha, beta, err};
     dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
     gemm_bf16_tn_kernel<<<grid, 128, SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, tc, p, cm);
     return (int)cudaGetLastError();
 }
 
-extern "C" int ltq_gemm_bf16x6_tn(const uint16_t* A3, long long lda, const uint16_t* B3, long long ldb, float* C,
-                                  long long ldc, int M, int N, int Kp, float alpha, float beta, int* err, void* stream)
+extern "C" int ltq_gemm_bf16x3p_tn(const uint16_t* A3, long long lda, long long abs_, const uint16_t* B3,
+                                   long long ldb, long long bbs, float* C, long long ldc, long long cbs, int M, int N,
+                                   int Kp, int nq, int batch, float alpha, float beta, int* err, void* stream)
 {
-    if (M < 0 || N < 0 || Kp <= 0 || N % 16 || Kp % BK || !A3 || !B3 || !C || lda < 3LL * Kp || ldb < 3LL * Kp ||
-        ldc < N || (lda % 8) || (ldb % 8) || (ldc % 4) || ((uintptr_t)A3 & 15) || ((uintptr_t)B3 & 15) ||
-        ((uintptr_t)C & 15))
+    if (M < 0 || N < 0 || Kp <= 0 || N % 16 || Kp % BK || (nq != 2 && nq != 3) || batch < 1 || batch > 65535 || !A3 ||
+        !B3 || !C || lda < 1LL * nq * Kp || ldb < 1LL * nq * Kp || ldc < N || (lda % 8) || (ldb % 8) || (ldc % 4) ||
+        ((uintptr_t)A3 & 15) || ((uintptr_t)B3 & 15) || ((uintptr_t)C & 15) ||
+        (batch > 1 && (abs_ % 8 || bbs % 8 || cbs % 4 || abs_ < lda * M || bbs < ldb * N || cbs < ldc * M)))
         return -1;
     if (M == 0 || N == 0) return 0;
     CUtensorMap ta, tb;
-    if (!make_map(&ta, A3, M, 3 * Kp, lda, BM) || !make_map(&tb, B3, N, 3 * Kp, ldb, BN)) return -1;
+    if (!make_map3(&ta, A3, M, nq * Kp, lda, batch, abs_, BM) || !make_map3(&tb, B3, N, nq * Kp, ldb, batch, bbs, BN))
+        return -1;
     static std::atomic<int> attr_set[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
     if (!attr_set[dev].load(std::memory_order_acquire)) {
-        if (cudaFuncSetAttribute(gemm_bf16x6_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM6_BYTES) !=
+        if (cudaFuncSetAttribute(gemm_bf16x3p_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM6_BYTES) !=
             cudaSuccess)
             return -1;
         attr_set[dev].store(1, std::memory_order_release);
     }
     const int cm = c_mode(beta);
     CUtensorMap tc{};
-    if (cm && !make_map_c(&tc, C, M, N, ldc)) return -1;
-    GemmParams p{C, ldc, M, N, Kp, alpha, beta, err};
-    dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
-    gemm_bf16x6_tn_kernel<<<grid, 128, SMEM6_BYTES, (cudaStream_t)stream>>>(ta, tb, tc, p, cm, Kp);
+    if (cm && !make_map_c(&tc, C, M, N, ldc, batch, cbs)) return -1;
+    GemmParams p{C, ldc, cbs, M, N, Kp, alpha, beta, err};
+    dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, batch);
+    gemm_bf16x3p_tn_kernel<<<grid, 128, SMEM6_BYTES, (cudaStream_t)stream>>>(ta, tb, tc, p, cm, Kp, nq);
     return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_gemm_bf16x6_tn(const uint16_t* A3, long long lda, const uint16_t* B3, long long ldb, float* C,
+                                  long long ldc, int M, int N, int Kp, float alpha, float beta, int* err, void* stream)
+{
+    return ltq_gemm_bf16x3p_tn(A3, lda, 0, B3, ldb, 0, C, ldc, 0, M, N, Kp, 3, 1, alpha, beta, err, stream);
 }

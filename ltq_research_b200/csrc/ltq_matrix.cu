@@ -362,6 +362,67 @@ __global__ void __launch_bounds__(256) bf16x6_split_kernel(const float* __restri
     }
 }
 
+// Compact three-part operand of the tensor-core GEMM (ltq_gemm_bf16x3p_tn) for `batch` fp32 matrices x_z = x + z xbs
+// (rows x cols, row stride ld), parts along the columns at stride Kp, zero-padded to Kp:
+//   trans 0: out_z[r][p Kp + c] = part_p(s x_z[r][c])   (r < rows; c < Kp, 0 for c >= cols)
+//   trans 1: out_z[c][p Kp + r] = part_p(s x_z[r][c])   (c < cols; r < Kp, 0 for r >= rows)
+// with s = -1 when neg (exact) else 1, part_p the three-way bf16 split.  trans 0: one thread per 4 columns of a row;
+// trans 1: 32 x 32 tiles through shared memory (reads along c, writes along r).
+__global__ void __launch_bounds__(256) bf16x3_split_kernel(const float* __restrict__ x, long long ld, long long xbs,
+                                                           int rows, int cols, int neg, int Kp,
+                                                           uint16_t* __restrict__ out, long long ld_out, long long obs)
+{
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int c4 = Kp >> 2;
+    if (t >= (long long)rows * c4) return;
+    x += (long long)blockIdx.y * xbs;
+    out += (long long)blockIdx.y * obs;
+    const int r = (int)(t / c4), c = 4 * (int)(t - (long long)r * c4);
+    const float sg = neg ? -1.f : 1.f;
+    uint16_t p[3][4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float v = c + k < cols ? sg * x[(long long)r * ld + c + k] : 0.f;
+        split3_bf16(v, p[0][k], p[1][k], p[2][k]);
+    }
+#pragma unroll
+    for (int q = 0; q < 3; q++)
+        *reinterpret_cast<uint2*>(out + (long long)r * ld_out + (long long)q * Kp + c) =
+            make_uint2((uint32_t)p[q][0] | ((uint32_t)p[q][1] << 16), (uint32_t)p[q][2] | ((uint32_t)p[q][3] << 16));
+}
+
+__global__ void __launch_bounds__(256) bf16x3_split_t_kernel(const float* __restrict__ x, long long ld, long long xbs,
+                                                             int rows, int cols, int neg, int Kp,
+                                                             uint16_t* __restrict__ out, long long ld_out,
+                                                             long long obs)
+{
+    __shared__ uint16_t sp[3][32][34];  // [part][c][r]
+    const int c0 = 32 * blockIdx.x, r0 = 32 * blockIdx.y;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    x += (long long)blockIdx.z * xbs;
+    out += (long long)blockIdx.z * obs;
+    const float sg = neg ? -1.f : 1.f;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int r = r0 + ty + 8 * q, c = c0 + tx;
+        const float v = (r < rows && c < cols) ? sg * x[(long long)r * ld + c] : 0.f;
+        uint16_t p0, p1, p2;
+        split3_bf16(v, p0, p1, p2);
+        sp[0][tx][ty + 8 * q] = p0;
+        sp[1][tx][ty + 8 * q] = p1;
+        sp[2][tx][ty + 8 * q] = p2;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int c = c0 + ty + 8 * q;
+        if (c >= cols) continue;
+        uint16_t* row = out + (long long)c * ld_out + r0 + tx;
+#pragma unroll
+        for (int pt = 0; pt < 3; pt++) row[(long long)pt * Kp] = sp[pt][ty + 8 * q][tx];
+    }
+}
+
 // inverse of the 256 x 256 lower-triangular diagonal block b of L (row-major, row stride ldL) into the diagonal block of
 // X (row stride ldX; the block's upper part written as 0), by forward substitution: thread t owns column j = 128 h + t
 // (h = blockIdx.y), x_i = (delta_ij - sum_{k < i} L_ik x_k) / L_ii for i >= j, the sum in ascending k; the column lives
@@ -400,8 +461,8 @@ __global__ void __launch_bounds__(128) trtri256_lower_kernel(const float* __rest
 //     shared memory, column-major with every column starting at its tile row (32-byte aligned: 132 KB);
 //   phase 2, Y = L~^-1 by Gauss-Jordan on the identity: at pivot j the owners of tile row j/8 broadcast row j of Y and
 //     every tile below it and left of it takes y_ik -= L~_ij y_jk (rows i > j); then X = L^-1 = D^-1/2 Y;
-//   outputs: L in A's block (zeros above the diagonal); xt6 [1536][256] (bf16) = the six-slot right operand
-//     [x0; x1; x0; x2; x1; x0] of X^T (the panel below the block is A_21 X^T; every element written); X itself in the
+//   outputs: L in A's block (zeros above the diagonal); xt3 [256][768] (bf16) = the compact right operand of the panel
+//     product A_21 X^T for ltq_gemm_bf16x3p_tn, row n = [x0 x1 x2] of row n of X (every element written); X itself in the
 //     block at (c0, c0) of Xo (row stride ldx) when Xo is given; *info = c0 + j + 1 for the first pivot that is not
 //     positive (or NaN) when *info was 0 (LAPACK's convention).
 constexpr int LT_FLOATS = 33792;  // sum over columns of 256 - 8 * (j / 8)
@@ -412,7 +473,7 @@ __device__ __forceinline__ int lt_col(int j)
 }
 
 __global__ void __launch_bounds__(544, 1) chol256_tiled_kernel(float* __restrict__ A, long long ld, int c0,
-                                                               uint16_t* __restrict__ xt6, float* __restrict__ Xo,
+                                                               uint16_t* __restrict__ xt3, float* __restrict__ Xo,
                                                                long long ldx, int* __restrict__ info)
 {
     extern __shared__ __align__(16) float smem[];
@@ -577,26 +638,26 @@ __global__ void __launch_bounds__(544, 1) chol256_tiled_kernel(float* __restrict
             *reinterpret_cast<float4*>(dst + 4) = make_float4(a[r][4], a[r][5], a[r][6], a[r][7]);
         }
     }
+    // the compact right operand of the panel product A21 X^T: row n of xt3 = [x0 x1 x2] of row n of X, i.e. this
+    // thread's 8 x 8 tile in rows 8 bi + r, columns 8 bk .. 8 bk + 7 of each part (and the zero tile above the diagonal)
 #pragma unroll
-    for (int cc = 0; cc < 8; cc++) {
-        uint32_t w[3][4];  // the three bf16 parts of column cc's 8 values, two to a word
+    for (int r = 0; r < 8; r++) {
+        uint32_t w[3][4];  // the three bf16 parts of row r's 8 values, two to a word
 #pragma unroll
-        for (int r = 0; r < 8; r += 2) {
+        for (int cc = 0; cc < 8; cc += 2) {
             uint16_t p0, p1, p2, q0, q1, q2;
             split3_bf16(a[r][cc], p0, p1, p2);
-            split3_bf16(a[r + 1][cc], q0, q1, q2);
-            w[0][r / 2] = p0 | (uint32_t)q0 << 16;
-            w[1][r / 2] = p1 | (uint32_t)q1 << 16;
-            w[2][r / 2] = p2 | (uint32_t)q2 << 16;
+            split3_bf16(a[r][cc + 1], q0, q1, q2);
+            w[0][cc / 2] = p0 | (uint32_t)q0 << 16;
+            w[1][cc / 2] = p1 | (uint32_t)q1 << 16;
+            w[2][cc / 2] = p2 | (uint32_t)q2 << 16;
         }
-        constexpr int slot_part[6] = {0, 1, 0, 2, 1, 0};
 #pragma unroll
-        for (int sl = 0; sl < 6; sl++) {
-            const int q = slot_part[sl];
-            *reinterpret_cast<uint4*>(xt6 + (long long)(256 * sl + 8 * bk + cc) * 256 + 8 * bi) =
+        for (int q = 0; q < 3; q++) {
+            *reinterpret_cast<uint4*>(xt3 + (long long)(8 * bi + r) * 768 + 256 * q + 8 * bk) =
                 make_uint4(w[q][0], w[q][1], w[q][2], w[q][3]);
             if (bi != bk)
-                *reinterpret_cast<uint4*>(xt6 + (long long)(256 * sl + 8 * bi + cc) * 256 + 8 * bk) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(xt3 + (long long)(8 * bk + r) * 768 + 256 * q + 8 * bi) = make_uint4(0, 0, 0, 0);
         }
     }
 }
@@ -701,6 +762,27 @@ extern "C" int ltq_ldlq_inter3(const float* w_blk, long long ld_w, const float* 
     return (int)cudaGetLastError();
 }
 
+extern "C" int ltq_bf16x3_split(const float* x, long long ld, long long xbs, int rows, int cols, int batch, int trans,
+                                int neg, int Kp, uint16_t* out, long long ld_out, long long obs, void* stream)
+{
+    if (rows < 0 || cols < 0 || batch < 1 || batch > 65535 || (trans != 0 && trans != 1) || Kp < 0 || Kp % 32 ||
+        !x || !out || ld < cols || ld_out < 3LL * Kp || ld_out % 4 || ((uintptr_t)out & 7) ||
+        (trans ? Kp < rows : Kp < cols))
+        return -1;
+    const int orows = trans ? cols : rows;
+    if (orows == 0 || Kp == 0) return 0;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!trans) {
+        const long long threads = (long long)rows * (Kp / 4);
+        bf16x3_split_kernel<<<dim3((unsigned)((threads + 255) / 256), batch), 256, 0, st>>>(x, ld, xbs, rows, cols,
+                                                                                         neg, Kp, out, ld_out, obs);
+    } else {
+        bf16x3_split_t_kernel<<<dim3((cols + 31) / 32, Kp / 32, batch), 256, 0, st>>>(x, ld, xbs, rows, cols, neg,
+                                                                                       Kp, out, ld_out, obs);
+    }
+    return (int)cudaGetLastError();
+}
+
 extern "C" int ltq_bf16x6_split_batched(const float* x, long long ld, long long xbs, int rows, int cols, int batch,
                                         int order, int side, int neg, uint16_t* out, long long ld_out, long long obs,
                                         void* stream)
@@ -740,11 +822,11 @@ extern "C" int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* 
     return (int)cudaGetLastError();
 }
 
-extern "C" int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt6, float* X, long long ldx, int* info,
+extern "C" int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt3, float* X, long long ldx, int* info,
                                 void* stream)
 {
-    if (!A || !xt6 || !info || c0 < 0 || ld < c0 + 256LL || (X && ldx < c0 + 256LL)) return -1;
-    if (c0 % 4 || ld % 4 || (X && ldx % 4) || ((uintptr_t)A & 15) || ((uintptr_t)xt6 & 15) || ((uintptr_t)X & 15)) return -1;
+    if (!A || !xt3 || !info || c0 < 0 || ld < c0 + 256LL || (X && ldx < c0 + 256LL)) return -1;
+    if (c0 % 4 || ld % 4 || (X && ldx % 4) || ((uintptr_t)A & 15) || ((uintptr_t)xt3 & 15) || ((uintptr_t)X & 15)) return -1;
     static std::atomic<int> attr_done[64];
     constexpr int smem = (LT_FLOATS + 768) * 4;
     int dev = 0;
@@ -754,6 +836,6 @@ extern "C" int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt6, f
         if (e != cudaSuccess) return (int)e;
         attr_done[dev].store(1, std::memory_order_release);
     }
-    chol256_tiled_kernel<<<1, 544, smem, (cudaStream_t)stream>>>(A, ld, c0, xt6, X, ldx, info);
+    chol256_tiled_kernel<<<1, 544, smem, (cudaStream_t)stream>>>(A, ld, c0, xt3, X, ldx, info);
     return (int)cudaGetLastError();
 }

@@ -25,7 +25,7 @@ from typing import List, Optional, Tuple
 
 import torch
 
-from . import _lib
+from . import _lib, tcgemm
 from ._lib import ptr
 
 QK = 256
@@ -123,15 +123,10 @@ def _merge(Lr: torch.Tensor, X: torch.Tensor, a0: int, ba: int, bc: int, batch: 
     XA = X.as_strided((batch, ba, ba), (bs, K, 1), X.storage_offset() + a0 * K + a0)
     XC = X.as_strided((batch, bc, bc), (bs, K, 1), X.storage_offset() + c0 * K + c0)
     X21 = X.as_strided((batch, bc, ba), (bs, K, 1), X.storage_offset() + c0 * K + a0)
-    # T = L21 X_A  [bc, ba]
-    left = _split6(L21, bs, bc, ba, batch, 0, 0, False, K)
-    right = _split6(XA, bs, ba, ba, batch, 1, 1, False, K)
-    T = torch.bmm(left, right, out_dtype=torch.float32)
-    del left, right
-    # X21 = (-X_C) T  [bc, ba]
-    left = _split6(XC, bs, bc, bc, batch, 0, 0, True, K)
-    right = _split6(T, T.stride(0), bc, ba, batch, 1, 1, False, T.stride(1))
-    X21.copy_(torch.bmm(left, right, out_dtype=torch.float32))
+    # T = L21 X_A  [bc, ba], then X21 = (-X_C) T written in place: batched six-product tensor-core GEMMs
+    T = torch.empty((batch, bc, ba), dtype=torch.float32, device=X.device)
+    tcgemm.gemm3(tcgemm.split3(L21, Kp=ba), tcgemm.split3(XA, trans=True, Kp=ba), T, ba)
+    tcgemm.gemm3(tcgemm.split3(XC, neg=True, Kp=bc), tcgemm.split3(T, trans=True, Kp=bc), X21, bc)
 
 
 def cholesky_lower(A: torch.Tensor, inverse: bool = False, overwrite: bool = False
@@ -148,31 +143,28 @@ def cholesky_lower(A: torch.Tensor, inverse: bool = False, overwrite: bool = Fal
         A = A.contiguous().clone() if A.is_contiguous() else A.contiguous()
     info = torch.zeros(1, dtype=torch.int32, device=dev)
     X = torch.zeros_like(A) if inverse else None
-    xt6 = torch.empty((6 * QK, QK), dtype=torch.bfloat16, device=dev)
+    xt3 = torch.empty((QK, 3 * QK), dtype=torch.bfloat16, device=dev)  # the leaf's compact operand of L11^-1
     st = _stream(dev)
     L_ = _lib.lib()
     nb = K // QK
     for p in range(nb):
         c0, c1 = QK * p, QK * (p + 1)
-        _check(L_.ltq_chol256_diag(ptr(A), K, c0, ptr(xt6), ptr(X) if X is not None else None, K, ptr(info), st),
+        _check(L_.ltq_chol256_diag(ptr(A), K, c0, ptr(xt3), ptr(X) if X is not None else None, K, ptr(info), st),
                "ltq_chol256_diag")
         if c1 == K:
             break
         m = K - c1
         A21 = A[c1:, c0:c1]
-        # L21 = A21 L11^-T written over A21 (beta = 0: the old values are not read)
-        torch.addmm(A21, _split6(A21, 0, m, QK, 1, 0, 0, False, K)[0], xt6, beta=0, out_dtype=torch.float32, out=A21)
-        left = _split6(A21, 0, m, QK, 1, 0, 0, False, K)[0]     # [m, 1536], slots [x0 x0 x1 x0 x1 x2]
-        right = _split6(A21, 0, m, QK, 1, 1, 0, False, K)[0].T  # [1536, m], slots [x0 x1 x0 x2 x1 x0] of L21^T
+        # L21 = A21 L11^-T written over A21 (beta = 0: the old values are not read; the operand is split first)
+        tcgemm.gemm3(tcgemm.split3(A21, Kp=QK), xt3, A21, QK)
+        parts = tcgemm.split3(A21, Kp=QK)  # [m, 768]: L21 = [l0 l1 l2], both operands of L21 L21^T
         A22 = A[c1:, c1:]
         h = QK * (m // QK // 2) if m >= 4 * QK else m
         # A22 -= L21 L21^T on the lower triangle's cover: the leading h x h square, then the rows below it in full
-        C = A22[:h, :h]
-        torch.addmm(C, left[:h], right[:, :h], beta=1, alpha=-1, out_dtype=torch.float32, out=C)
+        tcgemm.gemm3(parts[:h], parts[:h], A22[:h, :h], QK, alpha=-1.0, beta=1.0)
         if h < m:
-            C = A22[h:]
-            torch.addmm(C, left[h:], right, beta=1, alpha=-1, out_dtype=torch.float32, out=C)
-        del left, right
+            tcgemm.gemm3(parts[h:], parts, A22[h:], QK, alpha=-1.0, beta=1.0)
+        del parts
     A.tril_()
     if inverse:
         tri_inv_lower(A, X)

@@ -21,7 +21,7 @@ from typing import Dict, List, Optional, Tuple
 
 import torch
 
-from . import _lib
+from . import _lib, tcgemm
 from ._lib import ptr
 from .hessian import cholesky_lower
 from .formats import LIQK_V2_SPECS, QK_K, SUBBLOCK_SIZE, TCQ_CONFIG  # noqa: F401
@@ -127,11 +127,13 @@ def _gram_lower6(x: torch.Tensor) -> torch.Tensor:
 
 
 def _mm(a: torch.Tensor, b: torch.Tensor, gemm: str) -> torch.Tensor:
-    """a @ b for fp32 [M, K] x [K, N] in the given mode."""
+    """a @ b for fp32 [M, K] x [K, N] in the given mode: torch's fp32 matmul, or the six-product tensor-core GEMM."""
     if gemm == "fp32":
         return a @ b
     if gemm != "bf16x6":
         raise ValueError(f"gemm mode {gemm!r}: expected one of {GEMM_MODES}")
+    if b.shape[1] % 16 == 0:
+        return tcgemm.mm(a, b)
     return _mm6(_left6(a), _right6(b))
 
 
@@ -717,10 +719,11 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
         def times_h(A):
             return A @ H_f32
     else:
-        Hb = _right6(H_f32)  # the split of H, shared by every product with H
+        Kp = tcgemm._pad(K)
+        Hb3 = tcgemm.split3(H_f32, trans=True, Kp=Kp)  # the split of H (as the right operand), shared by every product
 
         def times_h(A):
-            return _mm6(_left6(A), Hb)
+            return tcgemm.times(A, Hb3, Kp)
     U_base = fwht_inplace(W_hat_rot.clone(), block_size=QK_K)
     W_hat_eff = U_base * suh.unsqueeze(0)
     c_pack = torch.ones((M,), dtype=torch.float32, device=W.device)
@@ -741,7 +744,7 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     if gemm == "fp32":
         A_in = U_w.T @ U_scaled
     elif row_weights is None:  # U_w is U_scaled: a Gram matrix, needed on its lower triangle only (Cholesky below)
-        A_in = _gram_lower6(U_scaled)
+        A_in = tcgemm.gram_lower(U_scaled, QK_K * (K // QK_K // 2) if K >= 4 * QK_K else K)
     else:
         A_in = _mm(U_w.T, U_scaled, gemm)
     b_in = (U_w * HW).sum(dim=0)
@@ -791,11 +794,9 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
             HQ = times_h(W_pk)
         else:
             # the packed reconstruction differs from W_hat_eff only by the fp16 roundings of the row scale and suh:
-            # HQ takes the product of that small change, in the three-product bf16 form (the first three slots of
-            # each six-slot operand: relative error ~2^-16 of the change, far below fp32 rounding of HQ itself)
-            dl = _left6(W_pk - W_hat_eff)
-            HQ = torch.addmm(HQ, dl[:, :3 * K], Hb[:3 * K], out_dtype=torch.float32)
-            del dl
+            # HQ takes the product of that small change, in the three-product bf16 form (a0 b0 + a1 b0 + a0 b1:
+            # relative error ~2^-16 of the change, far below fp32 rounding of HQ itself)
+            HQ = tcgemm.gemm3(tcgemm.split3(W_pk - W_hat_eff, Kp=Kp), Hb3, HQ, Kp, beta=1.0, nq=2)
         W_hat_eff = W_pk
         pack = {"row_slices": row_slices, "idx": pm["idx"], "gi": pm["gi"], "G": pm["G"], "d_row": d_row_p,
                 "e": pm["e"], "suh": suh_p}

@@ -181,3 +181,73 @@ def test_inter_block_update_tensor_core_vs_library(cuda_dev):
     for got in (W1, W2):
         assert torch.equal(got[:, :256], W[:, :256])
         assert ((got[:, 256:].double() - ref).abs() <= bound).all()
+
+
+def _parts(x):
+    """The three-way bf16 split in torch (each difference exact in fp32)."""
+    x0 = x.to(torch.bfloat16)
+    r = x - x0.float()
+    x1 = r.to(torch.bfloat16)
+    x2 = (r - x1.float()).to(torch.bfloat16)
+    return x0, x1, x2
+
+
+@pytest.mark.parametrize("trans,neg", [(False, False), (True, False), (False, True), (True, True)])
+def test_split3_layout(cuda_dev, trans, neg):
+    from ltq_research_b200.tcgemm import split3
+    g = torch.Generator(device=cuda_dev).manual_seed(4)
+    big = torch.randn(3, 50, 120, generator=g, device=cuda_dev) * 7
+    x = big[:, 3:43, 8:108]  # batch 3 of [40, 100], strided
+    Kp = 128
+    got = split3(x, trans=trans, neg=neg, Kp=Kp)
+    src = -x if neg else x
+    src = src.transpose(1, 2) if trans else src
+    k = src.shape[2]
+    want = torch.zeros(3, src.shape[1], 3 * Kp, dtype=torch.bfloat16, device=cuda_dev)
+    for p, part in enumerate(_parts(src.contiguous())):
+        want[:, :, p * Kp:p * Kp + k] = part
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+@pytest.mark.parametrize("nq", [2, 3])
+def test_gemm3_batched_exact(cuda_dev, nq):
+    """Batched part GEMM on small integers into strided C views: beta 0 (TMA store), 1 (TMA reduce-add), 0.5
+    (read-modify-write), exactly the integer sum of the nq (nq + 1) / 2 products."""
+    from ltq_research_b200.tcgemm import gemm3
+    g = torch.Generator(device=cuda_dev).manual_seed(10 + nq)
+    batch, M, N, Kp = 3, 200, 272, 128
+    A3 = torch.randint(-3, 4, (batch, M, 3 * Kp), generator=g, device=cuda_dev).to(torch.bfloat16)
+    B3 = torch.randint(-3, 4, (batch, N, 3 * Kp), generator=g, device=cuda_dev).to(torch.bfloat16)
+    a = [A3[:, :, i * Kp:(i + 1) * Kp].double() for i in range(3)]
+    b = [B3[:, :, i * Kp:(i + 1) * Kp].double() for i in range(3)]
+    prod = sum(a[p] @ b[q].transpose(1, 2) for p in range(3) for q in range(3) if p + q < nq)
+    for beta in (0.0, 1.0, 0.5):
+        big = torch.randint(-100, 100, (batch, M + 8, N + 32), generator=g, device=cuda_dev).float()
+        C = big[:, 4:4 + M, 16:16 + N]
+        want = beta * C.double() - prod
+        guard = big.clone()
+        gemm3(A3, B3, C, Kp, alpha=-1.0, beta=beta, nq=nq)
+        torch.cuda.synchronize()
+        assert torch.equal(C.double(), want), beta
+        mask = torch.ones_like(big, dtype=torch.bool)
+        mask[:, 4:4 + M, 16:16 + N] = False
+        assert torch.equal(big[mask], guard[mask]), beta
+
+
+def test_mm_and_gram_within_fp32_bound(cuda_dev):
+    from ltq_research_b200.tcgemm import gram_lower, mm
+    g = torch.Generator(device=cuda_dev).manual_seed(12)
+    a = torch.randn(300, 1000, generator=g, device=cuda_dev)
+    b = torch.randn(1000, 512, generator=g, device=cuda_dev) * torch.exp(torch.randn(1, 512, generator=g, device=cuda_dev))
+    got = mm(a, b)
+    ref = a.double() @ b.double()
+    bound = (1000 + 2) * U32 * (a.double().abs() @ b.double().abs())
+    torch.cuda.synchronize()
+    assert ((got.double() - ref).abs() <= bound).all()
+    x = torch.randn(1000, 1024, generator=g, device=cuda_dev)
+    C = gram_lower(x, 512)
+    ref = x.double().T @ x.double()
+    bound = (1000 + 2) * U32 * (x.double().abs().T @ x.double().abs())
+    low = torch.tril(torch.ones(1024, 1024, dtype=torch.bool, device=cuda_dev))
+    torch.cuda.synchronize()
+    assert ((C.double() - ref).abs() <= bound)[low].all()
