@@ -364,8 +364,9 @@ def aux_measurements(dev, fmts) -> dict:
     return out
 
 
-def hbm_kernels(dev, f) -> dict:
-    """Bandwidth of the path's HBM-bound kernels (see aux_measurements)."""
+def hbm_kernels(dev, f, reps: int = 10, timed: bool = True) -> dict:
+    """Bandwidth of the path's HBM-bound kernels (see aux_measurements).  timed=False: each kernel `reps` times,
+    untimed (the profiling run of --profile-hbm)."""
     from ltq_research_b200 import _lib
     from ltq_research_b200.liqk_v2 import fwht_rows_scaled
     from ltq_research_b200.ltq_file import decode_slice_device, pack_slice_device
@@ -389,7 +390,6 @@ def hbm_kernels(dev, f) -> dict:
     st = torch.cuda.current_stream(dev).cuda_stream
     L = _lib.lib()
     tb = data.numel()
-    reps = 10
     kernels = {
         "fwht256": (lambda: fwht_rows_scaled(W, s, mode=1, out=Wr), 8 * n),
         "scale_fit": (lambda: L.ltq_scale_fit(W.data_ptr(), K, R, K, 1.1, 0.25, 5, None, d_row.data_ptr(),
@@ -398,6 +398,12 @@ def hbm_kernels(dev, f) -> dict:
         "decode_verify": (lambda: decode_slice_device(buf, R, K, f, ref=ref, mismatches=bad), tb + 4 * n),
     }
     out = {"shape": [R, K], "format": f.name, "peak_gbs": peak}
+    if not timed:
+        for name, (fn, nbytes) in kernels.items():
+            for _ in range(reps):
+                fn()
+        torch.cuda.synchronize()
+        return out
     for name, (fn, nbytes) in kernels.items():
         ms = _event_ms(lambda: [fn() for _ in range(reps)]) / reps
         gbs = nbytes / ms / 1e6
@@ -838,6 +844,9 @@ def main():
     ap.add_argument("--profile-viterbi", default=None, metavar="FORMAT",
                     help="three stand-alone two-pass Viterbi calls (ltq_viterbi_tb) of FORMAT over the --rows / 16 "
                          "tiles of one sub-block, for ncu captures of vit_fwd_kernel")
+    ap.add_argument("--profile-hbm", action="store_true",
+                    help="the HBM-bound kernels (FWHT-256, scale fit, pack, verify decode) on a 16384 x 4096 matrix, "
+                         "three launches each, untimed, for ncu captures")
     ap.add_argument("--aux", action="store_true",
                     help="time the secondary paths instead of the layer step (one JSON line): the decode GEMV from "
                          "packed tiles, ring quantization (config 5's path) and the DP-profile table kernel")
@@ -869,6 +878,10 @@ def main():
 
     if args.aux:
         print(json.dumps(aux_measurements(dev, fmts)), flush=True)
+        return
+    if args.profile_hbm:
+        hbm_kernels(dev, fmts["TCQ3X"], reps=3, timed=False)
+        print("profile run: HBM-bound kernels on 16384 x 4096, 3 launches each", flush=True)
         return
     if args.profile_viterbi:
         r = Lq._TcqRunner(args.profile_viterbi, args.rows, dev)

@@ -38,8 +38,21 @@ def test_pack_and_decode_match_reference_all_formats(cuda_dev):
         wide_g = torch.zeros((R + 32, K), dtype=torch.uint8, device=cuda_dev)
         wide_i[16:16 + R], wide_g[16:16 + R] = idx, gi
         assert pack_slice_device(wide_i[16:16 + R], wide_g[16:16 + R], f).cpu().numpy().tobytes() == raw, n
+        # every byte of the slice is written (padding included): an output buffer full of 0xAB gives the same bytes
+        dirty = torch.full((len(raw) + 128,), 0xAB, dtype=torch.uint8, device=cuda_dev)
+        assert pack_slice_device(idx, gi, f, out=dirty).cpu().numpy().tobytes() == raw, n
+        assert bool((dirty[len(raw):] == 0xAB).all()), n
         vals = decode_slice(raw, R, K, f, cuda_dev).cpu().numpy()
         assert np.array_equal(vals.view(np.uint32), z[f"{n}/vals"].view(np.uint32)), n
+        # rows that are not 16-byte aligned (scalar stores / loads) decode and verify the same values
+        from ltq_research_b200.ltq_file import decode_slice_device
+        buf = dirty[: len(raw)]
+        wide = torch.zeros((R, K + 1), dtype=torch.float32, device=cuda_dev)
+        decode_slice_device(buf, R, K, f, out=wide[:, 1:])
+        assert np.array_equal(wide[:, 1:].cpu().numpy().view(np.uint32), z[f"{n}/vals"].view(np.uint32)), n
+        bad = torch.zeros(1, dtype=torch.int64, device=cuda_dev)
+        decode_slice_device(buf, R, K, f, ref=wide[:, 1:], mismatches=bad)
+        assert int(bad) == 0, n
 
 
 def test_pack_kernel_validation(cuda_dev):
