@@ -314,6 +314,31 @@ def _event_ms(fn, reps: int = 5) -> float:
     return statistics.median(ms)
 
 
+def gemm_ldlq_compare(dev) -> dict:
+    """tcgen05 six-product GEMM vs cuBLAS on the six-slot form, microseconds per call (see aux_measurements)."""
+    from ltq_research_b200 import _lib
+    L = _lib.lib()
+    st = torch.cuda.current_stream(dev).cuda_stream
+
+    def med_us(fn):
+        return _event_ms(lambda: [fn() for _ in range(5)], reps=10) / 5 * 1e3
+
+    g = torch.Generator(device=dev).manual_seed(9)
+    res = {}
+    for M, N in ((1024, 256), (3072, 2816), (8192, 2816), (8192, 7936)):
+        A3 = torch.randn(M, 768, device=dev, generator=g).to(torch.bfloat16)
+        B3 = torch.randn(N, 768, device=dev, generator=g).to(torch.bfloat16)
+        A6 = torch.cat([A3[:, 256 * i:256 * i + 256] for i in (0, 0, 1, 0, 1, 2)], 1).contiguous()
+        B6 = torch.cat([B3[:, 256 * i:256 * i + 256] for i in (0, 1, 0, 2, 1, 0)], 1).contiguous()
+        C = torch.randn(M, N, device=dev, generator=g)
+        tc = med_us(lambda: L.ltq_gemm_bf16x6_tn(A3.data_ptr(), 768, B3.data_ptr(), 768, C.data_ptr(), N, M, N, 256,
+                                                  -1.0, 1.0, None, st))
+        cb = med_us(lambda: torch.addmm(C, A6, B6.T, beta=1, alpha=-1, out_dtype=torch.float32, out=C))
+        res[f"{M}x{N}"] = {"tcgen05_us": round(tc, 1), "cublas_us": round(cb, 1),
+                           "tcgen05_tflops": round(2 * M * N * 1536 / (tc * 1e-6) / 1e12, 1)}
+    return res
+
+
 def aux_measurements(dev, fmts) -> dict:
     """The secondary paths on one GPU:
     * decode GEMV: y = W x from the packed tiles of a gate-shaped 8192 x 3072 TCQ3X matrix: the kernel alone
@@ -326,7 +351,11 @@ def aux_measurements(dev, fmts) -> dict:
     * the HBM-bound kernels of the path on a 16384 x 4096 matrix (268 MB in fp32, above the 126 MB L2), 10 back-to-back
       calls each, algorithmic bytes / s against MEASURED_PEAKS hbm_gbs: FWHT-256 with the column scale (fp32 in and
       out, 8 B / weight), the row-scale fit (4 B read), the .ltq pack of TCQ3X codes (idx + gi read, 3 B, tile bytes
-      written) and the on-device verify decode (tile bytes + the fp32 reference values read)."""
+      written) and the on-device verify decode (tile bytes + the fp32 reference values read);
+    * the LDLQ inter-block update's GEMM (W[:, c1:] -= acat @ bcat, K = 256 split in three bf16 parts, six products) at
+      four (rows, columns) shapes: the tcgen05 kernel (ltq_gemm_bf16x6_tn on compact part operands) against cuBLAS
+      (torch.addmm with fp32 output) on the K-concatenated six-slot operands of the same product, medians of 10 x 5
+      back-to-back calls."""
     from ltq_research_b200.batch import quantize_matrices
     from ltq_research_b200.ltq_file import matvec, matvec_slice_device, rotate_input
     from ltq_research_b200.rings import quantize_rings
@@ -354,6 +383,7 @@ def aux_measurements(dev, fmts) -> dict:
     n = T.numel()
     out["rings"] = {"table": [2048, 2560], "format": "TCQ4X:rot", "ms": ms, "mvalues_per_s": n / ms / 1e3,
                     "gacs_per_s": n * 2 * 1024 * 4 * 3 / ms / 1e6}
+    out["gemm_ldlq"] = gemm_ldlq_compare(dev)
     S = 1 << 20
     xs = torch.randn(S, 16, device=dev)
     dh = torch.rand(S, 16, device=dev) + 0.1

@@ -8,14 +8,16 @@
 // products (src/liqk_v2.py:1078) of the fast mode, where the bf16 split makes every operand K-major.
 //
 // One CTA per 128 x 256 tile of C, 128 threads:
-//   thread 0 (warp 0)  TMA producer: per 64-wide K chunk, A [128 x 64] and B [256 x 64] tiles into a 3-stage ring of
+//   thread 0 (warp 0)  TMA producer: per 64-wide K chunk, A [128 x 64] and B [256 x 64] tiles into a ring of STAGES
 //                      shared buffers (128-byte swizzle), completion counted in bytes on the stage's "full" mbarrier;
 //   thread 32 (warp 1) MMA issuer: four tcgen05.mma (M 128, N 256, K 16 each) per chunk into one 128-lane x 256-column
 //                      fp32 accumulator in tensor memory; tcgen05.commit frees the stage ("empty" mbarrier) once the
 //                      MMAs have read it, and signals the accumulator after the last chunk;
-//   all four warps     epilogue: warp w reads lanes 32 w .. 32 w + 31 (rows of the tile) with tcgen05.ld, 16 columns at a
-//                      time, stages them row-major in the freed pipeline buffers and writes C = beta C + alpha acc (one
-//                      fma per element) a whole row segment per warp instruction.
+//                      the other lanes of warps 0 and 1 wait at __syncwarp, so the two role threads issue alone;
+//   all four warps     epilogue: warp w reads lanes 32 w .. 32 w + 31 (rows of the tile) with tcgen05.ld; for beta 0 / 1
+//                      32 x 32 boxes go through swizzled shared buffers to a TMA store (beta 0) or a TMA reduce-add
+//                      into C (beta 1), so C is never read by the SMs; any other beta reads and writes C row by row.
+// gemm_bf16x3p_tn_kernel (below) is the same pipeline over compact three-part operands, batched over blockIdx.z.
 // Every wait on an mbarrier is bounded: after GEMM_WAIT_LIMIT polls the thread records a timeout in *err (when given)
 // and leaves its loop; the CTA still meets at its final barrier and frees its tensor memory.  No cluster, no multicast:
 // every TMA load reads this GPU's own memory.
