@@ -2,7 +2,7 @@
 
 Mirrors lumen-inference/ltq-research:
   * ``TCQ_CONFIG`` / ``TCQ_X_SCALE`` for the tail-biting (.ltq) formats — src/liqk_v2.py:818-840 (tables from
-    results/tcq_x_tables.json, n_cand = 4 when h > 2);
+    results/tcq_x_tables.json, n_cand = 4 when h > 2) — and the earlier formats of src/liqk_v2.py:786-821;
   * ``LIQK_V2_SPECS`` bit accounting of those formats — src/liqk_v2.py:862-869;
   * ``SETS`` format menus (``TCQPQ`` = the 19-format menu) — src/equal_bpw.py:58-75;
   * ``LtqFormat`` / ``load_formats`` — src/ltq_format.py:21-66.
@@ -41,6 +41,26 @@ for _name, _t in _DATA["formats"].items():
                          "m_extra": tuple(_t["m_extra"]), "row_scale": True, "tb": True,
                          **({"n_cand": 4} if _t["h"] > 2 else {})}
     TCQ_X_SCALE[_name] = _t["scale"]
+# The earlier formats (src/liqk_v2.py:786-821), not tail-biting and not written to .ltq files: TCQ2 / TCQ3 / TCQ4 take a
+# scale per (row, 256-block) refitted over two passes; the R formats one scale per row with 5-bit block exponents and the
+# trellis state carried from each tile to the next tile of the same rows (one pass); TCQ25R / TCQ35R alternate tile rows
+# between the tables of their "lo" and "hi" formats (each premultiplied by its own scale).
+LEGACY_FORMATS: list = list(_DATA["legacy"])
+for _name, _t in _DATA["legacy"].items():
+    _c = {k: _t[k] for k in ("K", "nu", "m", "h", "scale")}
+    if _t["row_scale"]:
+        _c["row_scale"] = True
+    if _t["carry"]:
+        _c["carry"] = True
+    if _t["n_cand"]:
+        _c["n_cand"] = _t["n_cand"]
+    if "K_hi" in _t:
+        _c.update({"K_hi": _t["K_hi"], "lo": _t["lo"], "hi": _t["hi"]})
+    else:
+        _c.update({"step": _t["step"], "lut": list(_t["lut"])})
+    TCQ_CONFIG[_name] = _c
+# the tail-biting (.ltq) formats
+LTQ_FORMATS: list = [n for n, c in TCQ_CONFIG.items() if c.get("tb")]
 # config-1 Gaussian rig format (results/universal_gaussian.json "tcq_K2_h2": K = 2, 4 subsets, h = 2)
 GAUSSIAN_RIG_K2H2: dict = dict(_DATA["formats"]["_config1_tcq_K2_h2"])
 
@@ -59,11 +79,20 @@ class LiqkV2Spec:
         return (self.block_bytes * 8.0) / QK_K
 
 
+def _block_bits(c: dict) -> float:
+    """Bits per 256 weights (src/liqk_v2.py:862-867): row-scale formats pay K (+ 1/2 for half-integer rows, minus the
+    parity mode's saving) per weight, h per sub-block, 5 for the block exponent and 2 for the row scale's share; the
+    block-scale formats pay the initial state (nu), a 16-bit scale and h per tile row."""
+    if c.get("row_scale"):
+        return (QK_K * (c["K"] + 0.5 * ("K_hi" in c) - {0: 0.0, 1: 0.5, 2: 0.25, 3: 0.75}[int(c.get("pp", 0))])
+                + QK_K // c.get("sub", SUBBLOCK_SIZE) * c["h"] + 5 + 2)
+    return QK_K * c["K"] + c["nu"] + 16 + 16 * c["h"]
+
+
 LIQK_V2_SPECS: Dict[str, LiqkV2Spec] = {}
 for _name, _cfg in TCQ_CONFIG.items():
-    _bits = (QK_K * (_cfg["K"] - {0: 0.0, 1: 0.5, 2: 0.25, 3: 0.75}[int(_cfg.get("pp", 0))])
-             + QK_K // _cfg.get("sub", SUBBLOCK_SIZE) * _cfg["h"] + 5 + 2)
-    LIQK_V2_SPECS[_name] = LiqkV2Spec(_name, float(_cfg["K"]), 1 << (_cfg["K"] + 1), 1 << _cfg["h"], _bits / 8)
+    LIQK_V2_SPECS[_name] = LiqkV2Spec(_name, float(_cfg["K"]), 1 << (_cfg["K"] + 1), 1 << _cfg["h"],
+                                      _block_bits(_cfg) / 8)
 
 
 @dataclass(frozen=True)

@@ -10,7 +10,9 @@ Mirrors lumen-inference/ltq-research src/liqk_v2.py (same names, arguments, retu
 Two modes for the linear algebra (GEMM_MODES): "fp32" runs the reference's torch operations (cuBLAS fp32, cuSOLVER's
 Cholesky and solves) bit for bit; "bf16x6", the batch driver's default, runs the products as fp32-accurate six-product
 bf16 GEMMs on the tensor cores and the factorisations through hessian.cholesky_lower / tri_inv_lower.
-Only the tail-biting row-scale formats of TCQ_CONFIG (the .ltq formats) are handled; the reference's other quantizers
+The TCQ formats of TCQ_CONFIG are handled: the tail-biting row-scale (.ltq) formats on the fused path above, the
+earlier non-tail-biting ones (block-scale TCQ2 / 3 / 4, the carry R formats, half-integer TCQ25R / TCQ35R; no .ltq
+encoding) through the per-sub-block Viterbi with the reference's torch updates; the reference's other quantizers
 (.liqk v2 banks, E8) are out of this path.  Everything runs on CUDA; there is no CPU path.
 """
 from __future__ import annotations
@@ -481,13 +483,112 @@ def _scale_fit_reference(W_rot: torch.Tensor, cfg: dict):
     return d_row, e_rb.to(torch.int8), d_rb.contiguous()
 
 
+def _legacy_tables(cfg: dict, device) -> tuple:
+    """(table, gains, extra Viterbi arguments) of an earlier format (src/liqk_v2.py:885-895): a half-integer format
+    runs its "lo" format's table on even tile rows and its "hi" format's table on odd ones, each premultiplied by its
+    own scale (its d carries no scale factor)."""
+    if "K_hi" not in cfg:
+        return (torch.tensor(cfg["lut"], dtype=torch.float32, device=device), make_gains(cfg["h"], cfg["step"], device),
+                {})
+    lo, hi = TCQ_CONFIG[cfg["lo"]], TCQ_CONFIG[cfg["hi"]]
+    tab = torch.tensor(lo["lut"], dtype=torch.float32, device=device) * lo["scale"]
+    extra = {"small_hi": torch.tensor(hi["lut"], dtype=torch.float32, device=device) * hi["scale"],
+             "gains_hi": make_gains(hi["h"], hi["step"], device), "mix": SUBBLOCK_SIZE}
+    return tab, make_gains(lo["h"], lo["step"], device), extra
+
+
+def _rows_legacy_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, n_pass: int = 2):
+    """The earlier (non-tail-biting) formats through the LDLQ loop of src/liqk_v2.py:948-1021, one Viterbi call per
+    16-column sub-block of all rows (tiles of 16 rows x 16 columns, t = 16 r + c), with the reference's torch operations
+    for the feedback and block updates (these formats are not on the fast path):
+      * R formats (row_scale): d(row, block) from the row-scale fit; the end state of each tile starts the next tile of
+        the same rows (carry), across sub-blocks and blocks;
+      * TCQ2 / TCQ3 / TCQ4: a scale per (row, block) from the block's rms, refitted over n_pass passes against the
+        block's Cholesky-weighted error, the best of (current, refit) kept per row.
+    A generator like _rows_ldlq_steps (yields after each block); returns (d_full, W_hat_rot, None): nothing to pack."""
+    from .tcq_proto import viterbi_ub_cuda
+    cfg = TCQ_CONFIG[spec_name]
+    device = W_rot.device
+    tab, gains, extra = _legacy_tables(cfg, device)
+    M, K = W_rot.shape
+    assert M % 16 == 0, "TCQ: number of rows must be divisible by 16"
+    nt, nblocks = M // 16, K // QK_K
+    n_cand = int(os.environ.get("TCQ_NCAND", cfg.get("n_cand", 0)))
+    W_work = W_rot.float().clone()
+    W_hat_rot = torch.empty_like(W_work)
+    d_full = torch.empty((M, nblocks), dtype=torch.float16, device=device)
+    state = [None]  # the tiles' end states, carried to the next sub-block (R formats)
+
+    def tiles_of(xs, dw):  # xs [M, 16] already divided by d, dw [16]: the reconstruction [M, 16]
+        t = xs.reshape(nt, 16 * SUBBLOCK_SIZE)
+        w = dw.repeat(16)
+        if cfg.get("carry"):
+            rec, state[0] = viterbi_ub_cuda(t, tab, cfg["K"], cfg["nu"], cfg["m"], gains, sub=SUBBLOCK_SIZE, wts=w,
+                                            init_state=state[0], return_end_state=True, n_cand=n_cand, **extra)
+        else:
+            rec = viterbi_ub_cuda(t, tab, cfg["K"], cfg["nu"], cfg["m"], gains, sub=SUBBLOCK_SIZE, wts=w,
+                                  n_cand=n_cand)
+        return rec.view(M, SUBBLOCK_SIZE)
+
+    def sweep(w_blk, d, U_blk, U_blk_inv, dw_blk):  # one LDLQ pass over a block's 16 sub-blocks at scale d [M]
+        work = w_blk.clone()
+        G = torch.empty((M, QK_K), dtype=torch.float32, device=device)
+        inv_d = 1.0 / d.unsqueeze(1)
+        for ib in range(NUM_SUBBLOCKS):
+            s0, s1 = ib * SUBBLOCK_SIZE, (ib + 1) * SUBBLOCK_SIZE
+            w_sub = work[:, s0:s1]
+            g = tiles_of(w_sub * inv_d, dw_blk[s0:s1])
+            G[:, s0:s1] = g
+            if s1 < QK_K:
+                e = (w_sub - d.unsqueeze(1) * g) @ U_blk_inv[s0:s1, s0:s1]
+                work[:, s1:] -= e @ U_blk[s0:s1, s1:]
+        return G
+
+    if cfg.get("row_scale"):
+        _, _, d_rb_all = _scale_fit_reference(W_work, cfg)
+    for ibl in range(nblocks):
+        c0, c1 = ibl * QK_K, (ibl + 1) * QK_K
+        w_blk = W_work[:, c0:c1].clone()
+        U_blk, U_blk_inv, dw_blk = U[c0:c1, c0:c1], U_blks_inv[ibl], diag_w[c0:c1]
+        if cfg.get("row_scale"):
+            d_best = d_rb_all[:, ibl].clamp(min=1e-8)
+            what = d_best.unsqueeze(1) * sweep(w_blk, d_best, U_blk, U_blk_inv, dw_blk)
+        else:
+            A = w_blk @ U_blk_inv
+            d = (w_blk.square().mean(dim=1).sqrt() * cfg.get("scale", 1.0)).to(torch.float16).to(torch.float32)
+            d = d.clamp(min=1e-8)
+            loss_best = torch.full((M,), float("inf"), device=device)
+            d_best, what = d.clone(), torch.zeros((M, QK_K), dtype=torch.float32, device=device)
+            for _ in range(n_pass):
+                G = sweep(w_blk, d, U_blk, U_blk_inv, dw_blk)
+                B = G @ U_blk_inv
+                num, den = (A * B).sum(dim=1), (B * B).sum(dim=1).clamp(min=1e-12)
+                d_fit = torch.where(den > 0, num / den, d).to(torch.float16).to(torch.float32).clamp(min=1e-8)
+                for d_try in (d, d_fit):  # keep the scale with the lower block loss, per row (ties keep the first)
+                    loss = (A - d_try.unsqueeze(1) * B).square().sum(dim=1)
+                    better = loss < loss_best
+                    loss_best = torch.where(better, loss, loss_best)
+                    d_best = torch.where(better, d_try, d_best)
+                    what = torch.where(better.unsqueeze(1), d_try.unsqueeze(1) * G, what)
+                d = d_fit
+        W_hat_rot[:, c0:c1] = what
+        d_full[:, ibl] = d_best.to(torch.float16)
+        if c1 < K:
+            W_work[:, c1:] -= ((w_blk - what) @ U_blk_inv) @ U[c0:c1, c1:]
+        yield
+    return d_full, W_hat_rot, None
+
+
 def _rows_ldlq_steps(W_rot, U, U_blks_inv, diag_w, spec_name: str, fused: bool = True, gemm: str = "fp32",
                      U_parts: Optional[tuple] = None):
     """_rows_ldlq as a generator that yields after each 256-column block's launches (for interleaved issue).
-    U_parts: the bf16 split of U when the caller already has it (bf16x6 mode)."""
+    U_parts: the bf16 split of U when the caller already has it (bf16x6 mode).  The earlier, non-tail-biting formats
+    go through _rows_legacy_steps."""
     cfg = TCQ_CONFIG[spec_name]
-    if not (cfg.get("row_scale") and cfg.get("tb")):
-        raise ValueError(f"{spec_name}: only the tail-biting row-scale (.ltq) TCQ formats are on this path")
+    if not cfg.get("tb"):
+        return (yield from _rows_legacy_steps(W_rot, U, U_blks_inv, diag_w, spec_name))
+    if not cfg.get("row_scale"):
+        raise ValueError(f"{spec_name}: the tail-biting TCQ formats are row-scale formats")
     device = W_rot.device
     L = _lib.lib()
     st = _stream(device)
@@ -607,6 +708,8 @@ def _quantize_rows_tcq_ldlq(W_rot: torch.Tensor, U: torch.Tensor, U_blks_inv: to
     """Block16-LDLQ with TCQ tiles, row-scale formats (src/liqk_v2.py:872-1021): returns (d_full fp16 [M, K/256],
     W_hat_rot [M, K]); with PACK set, appends the group's codes to PACK["groups"].  fused: one ltq_ldlq_block launch per
     256-column block; otherwise a gather, a two-pass Viterbi and a feedback launch per 16-column sub-block (same bits)."""
+    if PACK is not None and not (TCQ_CONFIG[spec_name].get("tb") and TCQ_CONFIG[spec_name].get("row_scale")):
+        raise ValueError(f"{spec_name}: only formats with tail-biting and d_row are written to .ltq")
     d_full, W_hat_rot, group = _rows_ldlq(W_rot, U, U_blks_inv, diag_w, spec_name, fused)
     if PACK is not None:
         PACK["groups"].append(group)
@@ -646,7 +749,9 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     specs_used = [spec_or_row_specs] if isinstance(spec_or_row_specs, str) else [sp for _, _, sp in spec_or_row_specs]
     for sp in specs_used:
         if sp not in TCQ_CONFIG:
-            raise ValueError(f"{sp}: not a TCQ (.ltq) format; this path quantizes the TCQ formats only")
+            raise ValueError(f"{sp}: not a TCQ format; this path quantizes the TCQ formats only")
+        if want_pack and not TCQ_CONFIG[sp].get("tb"):
+            raise ValueError(f"{sp}: only formats with tail-biting and d_row are written to .ltq")
     damp *= float(os.environ.get("TCQ_DAMP_MULT", "10"))
 
     W_rot, H_rot, suh = compute_optimal_suh(W, H_f32, seed=seed, row_weights=row_weights, row_reduce=row_reduce)

@@ -9,9 +9,10 @@ run it.  Fixtures written next to this file:
 * ltq_file_slices.npz   — `pack_slice` / `decode_slice` (src/ltq_file.py:79-148) for a few formats.
 * fwht.npz              — `fwht_inplace` (src/iqk_format.py:153-170) and `make_rademacher_signs` (:173-179).
 * formats.json          — the TCQPQ menu parameters as the reference's TCQ_CONFIG builds them (src/liqk_v2.py:834-840)
-                          with the gain tables evaluated by torch on CPU (the format stores its gain table explicitly).
+                          with the gain tables evaluated by torch on CPU (the format stores its gain table explicitly),
+                          and the earlier non-tail-biting formats (src/liqk_v2.py:786-821) under "legacy".
 
-    PYTHONDONTWRITEBYTECODE=1 TCQ_NO_COMPILE=1 python tests/golden/make_golden.py
+    PYTHONDONTWRITEBYTECODE=1 TCQ_NO_COMPILE=1 python tests/golden/make_golden.py [--formats-only]
 """
 from __future__ import annotations
 
@@ -64,8 +65,23 @@ def formats_json():
                                  "lut": [float(v) for v in np.asarray(u["tab"], np.float32)],
                                  "gains_cpu": [float(v) for v in make_gains(2, u["step"], "cpu").numpy()],
                                  "in_tcqpq": False, "gap": float(u["gap"])}
+    # the earlier (non-tail-biting) formats: per-block scale with a refit (TCQ2 / TCQ3 / TCQ4), one scale per row with
+    # the trellis state carried from tile to tile (the R formats), half-integer rows (TCQ25R / TCQ35R: tables of the
+    # "lo" / "hi" formats premultiplied by their scales).  Quantized by the driver; not written to .ltq files.
+    legacy = {}
+    for name, c in lv2.TCQ_CONFIG.items():
+        if c.get("tb"):
+            continue
+        e = {"K": c["K"], "nu": c["nu"], "m": c["m"], "h": c["h"], "scale": float(c.get("scale", 1.0)),
+             "row_scale": bool(c.get("row_scale", False)), "carry": bool(c.get("carry", False)),
+             "n_cand": int(c.get("n_cand", 0)), "bits": float(lv2.LIQK_V2_SPECS[name].block_bytes * 8)}
+        if "K_hi" in c:
+            e.update({"K_hi": c["K_hi"], "lo": c["lo"], "hi": c["hi"]})
+        else:
+            e.update({"step": float(c["step"]), "lut": [float(v) for v in np.asarray(c["lut"], np.float32)]})
+        legacy[name] = e
     doc = {"menu_TCQPQ": menu, "sets": {k: v for k, v in SETS.items() if v is not None and k.startswith("TCQ")},
-           "formats": out}
+           "formats": out, "legacy": legacy}
     (OUT / "formats.json").write_text(json.dumps(doc, indent=1))
     pkg = OUT.parent.parent / "ltq_research_b200" / "data"
     pkg.mkdir(exist_ok=True)
@@ -185,6 +201,8 @@ def fwht_cases():
 
 if __name__ == "__main__":
     formats_json()
+    if "--formats-only" in sys.argv:
+        raise SystemExit(0)
     torch_viterbi_cases()
     ltq_format_cases()
     ltq_file_cases()

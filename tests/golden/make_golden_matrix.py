@@ -4,7 +4,9 @@ formats, PACK mode) run from the reference tree on CPU, with its CUDA-only viter
 configs (bf16 Student-t(5) * 0.02 weights with 0.5 % outlier input channels x 20, H = X^T X of log-normal-scaled
 Gaussian activations).
 
-    PYTHONDONTWRITEBYTECODE=1 TCQ_NO_COMPILE=1 python tests/golden/make_golden_matrix.py
+    PYTHONDONTWRITEBYTECODE=1 TCQ_NO_COMPILE=1 python tests/golden/make_golden_matrix.py [--legacy]
+
+--legacy: the earlier non-tail-biting formats (LEGACY_CASES) -> matrix_quant_legacy.npz.
 """
 from __future__ import annotations
 
@@ -26,7 +28,7 @@ import torch  # noqa: E402
 import src.liqk_v2 as lv2  # noqa: E402
 import src.tcq_proto as tp  # noqa: E402
 from oracle import oracle as O  # noqa: E402
-from tests.golden.matrix_inputs import CASES, synth  # noqa: E402
+from tests.golden.matrix_inputs import CASES, LEGACY_CASES, synth  # noqa: E402
 
 
 def oracle_viterbi_ub_cuda(x, small, K, nu, m, gains=None, **kw):
@@ -86,5 +88,46 @@ def main():
     print((OUT / "matrix_quant.npz").stat().st_size, "bytes")
 
 
+def legacy_main():
+    """The earlier formats (no PACK mode in the reference for them): per case the row groups' d_full and W_hat_rot
+    before the refits (recorded at _quantize_rows_tcq_ldlq), and the returned d, suh and rel_loss ->
+    matrix_quant_legacy.npz."""
+    tp.viterbi_ub_cuda = oracle_viterbi_ub_cuda
+    orig_rows = lv2._quantize_rows_tcq_ldlq
+    rec = []
+
+    def rows_hook(W_rot, *a, **k):
+        d_sub, wh = orig_rows(W_rot, *a, **k)
+        rec.append((d_sub.clone(), wh.clone()))
+        return d_sub, wh
+    lv2._quantize_rows_tcq_ldlq = rows_hook
+    arrays, meta = {}, []
+    for name, M, K, spec, seed in LEGACY_CASES:
+        W, H = synth(M, K, seed)
+        rec.clear()
+        specs = [(0, M, spec)] if isinstance(spec, str) else spec
+        by = {}
+        for r0, r1, sp in specs:
+            by.setdefault(sp, []).append(torch.arange(r0, r1))
+        d0 = torch.zeros((M, K // 256), dtype=torch.float16)
+        wh0 = torch.zeros((M, K))
+        q, w_hat, rel = lv2.quantize_matrix_liqk_v2(W, H, spec, seed=1337, damp=0.02)
+        for rows, (d_sub, wh) in zip([torch.cat(v) for v in by.values()], rec):
+            d0[rows], wh0[rows] = d_sub, wh
+        arrays[f"{name}/d0"] = d0.view(torch.int16).numpy()
+        arrays[f"{name}/w_hat_rot0"] = wh0.numpy()
+        arrays[f"{name}/d"] = q["d"].view(torch.int16).numpy()
+        arrays[f"{name}/suh"] = q["suh"].view(torch.int16).numpy()
+        meta.append({"name": name, "M": M, "K": K, "spec": spec, "rel_loss": rel})
+        print(name, "rel_loss", rel, flush=True)
+    lv2._quantize_rows_tcq_ldlq = orig_rows
+    arrays["meta"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
+    np.savez_compressed(OUT / "matrix_quant_legacy.npz", **arrays)
+    print((OUT / "matrix_quant_legacy.npz").stat().st_size, "bytes")
+
+
 if __name__ == "__main__":
-    main()
+    if "--legacy" in sys.argv:
+        legacy_main()
+    else:
+        main()

@@ -32,8 +32,8 @@ SHAPES = [(32, 256), (16, 256), (16, 512)]
 def main():
     arrays, meta = {}, []
     rng = np.random.default_rng(20261201)
-    for i, (name, c) in enumerate(sorted(TCQ_CONFIG.items())):
-        if int(c.get("pp", 0)) > 2 or not c.get("row_scale"):
+    for i, (name, c) in enumerate(sorted((n, c) for n, c in TCQ_CONFIG.items() if c.get("tb"))):
+        if int(c.get("pp", 0)) > 2:
             continue
         masks = (c["m"],) + tuple(c.get("m_extra", ()))
         gains = make_gains(c["h"], c["step"], "cpu").numpy().astype(np.float32)

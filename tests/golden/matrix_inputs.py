@@ -15,6 +15,17 @@ CASES = [
 ]
 
 
+# the earlier, non-tail-biting formats (no .ltq encoding): carry R formats, half-integer rows, gain candidates, the
+# block-scale refit, and two of them in one matrix
+LEGACY_CASES = [
+    ("m32k512_TCQ3R", 32, 512, "TCQ3R", 11),
+    ("m32k512_TCQ25R", 32, 512, "TCQ25R", 12),
+    ("m32k512_TCQ4RH3", 32, 512, "TCQ4RH3", 13),
+    ("m32k512_TCQ3", 32, 512, "TCQ3", 14),
+    ("m64k512_TCQ2R_TCQ4", 64, 512, [(0, 32, "TCQ2R"), (32, 64, "TCQ4")], 15),
+]
+
+
 def synth(M: int, K: int, seed: int, device="cpu"):
     """(W bf16 [M, K], H fp32 [K, K]) from a generator on `device` (the values depend on the device's generator)."""
     g = torch.Generator(device=device).manual_seed(seed)

@@ -175,7 +175,7 @@ def test_pack_slices_all_formats_match_reference():
     of TCQ_CONFIG (tests/golden/pack_slices.npz, made by tests/golden/make_golden_pack.py)."""
     z = np.load(GOLDEN / "pack_slices.npz")
     meta = json.loads(bytes(z["meta"]).decode())
-    assert len(meta) == 35  # every TCQ_CONFIG format but the three EQ ones, which have no .ltq encoding
+    assert len(meta) == 35  # every tail-biting format but the three EQ ones, which have no .ltq encoding
     for m in meta:
         n = m["name"]
         fmt = _ltq_fmt(n, z[f"{n}/gains"])
@@ -183,3 +183,25 @@ def test_pack_slices_all_formats_match_reference():
         assert np.array_equal(np.frombuffer(raw, np.uint8), z[f"{n}/bytes"]), n
         dec = O.decode_slice(raw, m["R"], m["K"], fmt)
         assert np.array_equal(dec.view(np.uint32), z[f"{n}/vals"].view(np.uint32)), n
+
+
+def test_legacy_formats_table():
+    """The earlier, non-tail-biting formats (src/liqk_v2.py:786-821) load with the reference's constants and bit counts
+    (tests/golden/formats.json "legacy", written from the reference's TCQ_CONFIG / LIQK_V2_SPECS), and stay out of the
+    .ltq format list."""
+    import json
+    from pathlib import Path
+    from ltq_research_b200.formats import LEGACY_FORMATS, LIQK_V2_SPECS, LTQ_FORMATS, TCQ_CONFIG
+    doc = json.loads((Path(__file__).resolve().parent / "golden" / "formats.json").read_text())
+    assert sorted(LEGACY_FORMATS) == sorted(doc["legacy"]) == sorted(
+        ["TCQ2", "TCQ3", "TCQ4", "TCQ2R", "TCQ3R", "TCQ4R", "TCQ3RH", "TCQ4RH", "TCQ4RH3", "TCQ25R", "TCQ35R"])
+    assert not set(LEGACY_FORMATS) & set(LTQ_FORMATS) and len(LTQ_FORMATS) == 38
+    for name, t in doc["legacy"].items():
+        c = TCQ_CONFIG[name]
+        assert not c.get("tb") and bool(c.get("row_scale")) == t["row_scale"] and bool(c.get("carry")) == t["carry"]
+        assert LIQK_V2_SPECS[name].block_bytes * 8 == t["bits"], name
+        if "K_hi" in t:
+            assert (c["lo"], c["hi"], c["K_hi"]) == (t["lo"], t["hi"], t["K_hi"])
+        else:
+            assert c["lut"] == t["lut"] and c["step"] == t["step"]
+    assert TCQ_CONFIG["TCQ4RH3"]["n_cand"] == 4 and TCQ_CONFIG["TCQ3R"]["carry"] and "row_scale" not in TCQ_CONFIG["TCQ3"]

@@ -164,7 +164,7 @@ def test_slice_region_sizes_match_library():
     from ltq_research_b200 import _lib
     from ltq_research_b200.formats import TCQ_CONFIG
     from ltq_research_b200.shard import _slice_nbytes
-    names = [n for n, c in TCQ_CONFIG.items() if int(c.get("pp", 0)) != 3]
+    names = [n for n, c in TCQ_CONFIG.items() if c.get("tb") and int(c.get("pp", 0)) != 3]
     fmts, _ = _pack_fmts(names)
     for f in fmts:
         for R, K in ((16, 256), (48, 512), (96, 768), (208, 3072)):
