@@ -163,10 +163,10 @@ class _CpuViterbi:
     step's schedule needs CPU_PASSES passes per weight, so its rate is the pass rate / CPU_PASSES.  Without the
     reference install, the oracle's C restatement runs the GPU step's own TCQ3X two-pass tail-biting schedule."""
 
-    def __init__(self):
+    def __init__(self, port: bool = False):
         self.threads = _cpu_threads()
         from oracle.refroot import import_reference, reference_root
-        root = reference_root()
+        root = None if port else reference_root()
         if root is not None:
             import_reference(root)
             os.environ["TCQ_NO_COMPILE"] = "1"  # its torch.compile step cannot build on these hosts (no Python headers)
@@ -206,9 +206,11 @@ class _CpuViterbi:
         return weights / seconds / 1e6 * self.per_weight_passes / CPU_PASSES
 
 
-def cpu_baseline_sample(seconds: float = 15.0) -> dict:
-    """The CPU leg on rank 0 at N = 1: CPU_TILES tiles per call, calls until `seconds` have passed."""
-    cv = _CpuViterbi()
+def cpu_baseline_sample(seconds: float = 15.0, port: bool = False, port_seconds: float = 8.0) -> dict:
+    """The CPU leg on rank 0 at N = 1: CPU_TILES tiles per call, calls until `seconds` have passed.  When it ran the
+    reference's torch viterbi_ub, the oracle's C port is timed as well (`port_seconds`) and reported under "port", a
+    second, labelled number."""
+    cv = _CpuViterbi(port)
     x, w = _cpu_tiles(CPU_TILES * 4)
     cv.run(x[:CPU_TILES], w)  # untimed first call
     done, calls, t0 = 0, 0, time.perf_counter()
@@ -218,9 +220,13 @@ def cpu_baseline_sample(seconds: float = 15.0) -> dict:
         done += CPU_TILES * 256
         calls += 1
     el = time.perf_counter() - t0
-    return {"value": cv.rate(done, el), "unit": METRIC, "cores": cv.threads, "kind": cv.kind,
-            "sample": f"{calls} calls of {CPU_TILES} tiles of 256 in {el:.1f} s: {cv.desc}; the Viterbi search only "
-                      f"(the LDLQ / refit linear algebra of the GPU step is not timed on the CPU)"}
+    out = {"value": cv.rate(done, el), "unit": METRIC, "cores": cv.threads, "kind": cv.kind,
+           "sample": f"{calls} calls of {CPU_TILES} tiles of 256 in {el:.1f} s: {cv.desc}; the Viterbi search only "
+                     f"(the LDLQ / refit linear algebra of the GPU step is not timed on the CPU)"}
+    if cv.kind == "reference" and port_seconds > 0:
+        pt = cpu_baseline_sample(port_seconds, port=True, port_seconds=0)
+        out["port"] = {k: pt[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    return out
 
 
 def run_reference(args, rank: int, world: int):

@@ -18,7 +18,7 @@ long long sv_words(int T, int pp)  // words per (tile, gain slot), one lane row 
 int gsel_planes(int G) { return G <= 2 ? 1 : (G <= 4 ? 2 : 4); }
 
 // The reference's validation table (src/cuda/tcq_viterbi.cu:748-751 and the dispatch limits :720-763) plus this
-// implementation's limits (S = 1024, nl <= 16).  The reference's TCQ_BLOCK switch only picks its thread-block shape.
+// implementation's limit S = 1024 (the reference also runs S = 256 with 4 subsets).  The reference's TCQ_BLOCK switch only picks its thread-block shape.
 static bool valid(int N, int T, int S, int U, int G, int Gfull, bool cand, int sub, int U_hi, int mix, int nl, int ld,
                   int pp)
 {
@@ -31,7 +31,7 @@ static bool valid(int N, int T, int S, int U, int G, int Gfull, bool cand, int s
         nl * U_hi > 4 * MAXU)
         return false;
     if (!(G == 1 || G == 2 || G == 3 || G == 4 || G == 8)) return false;
-    if (S != 1024 || nl > 16 || U < 1 || U_hi < 1) return false;
+    if (S != 1024 || nl > 32 || U < 1 || U_hi < 1) return false;
     if (cand && G > Gfull) return false;
     return true;
 }
@@ -125,7 +125,7 @@ extern "C" int ltq_viterbi_tb(const float* x, const float* w, int w_stride, cons
                               int mix, int pp, int tb_passes, int tb_cand1, int tb_window, void* workspace,
                               size_t workspace_bytes, void* stream)
 {
-    if (nu != 10 || K < 1 || K > 8 || n_extra < 0 || n_extra > 2 || tb_passes < 2 || tb_window < 0 ||
+    if (nu != 10 || K < 1 || K > 8 || n_extra < 0 || n_extra > 3 || tb_passes < 2 || tb_window < 0 ||
         (n_extra > 0 && !m_extra))
         return -1;
     const int S = 1 << nu, U = 1 << (K - 1), nl = 4 << n_extra, h = T / 2;
@@ -157,7 +157,8 @@ extern "C" int ltq_viterbi_tb(const float* x, const float* w, int w_stride, cons
     p.x = x; p.w = w; p.tab = tab; p.gains = gains; p.tab_hi = tab_hi; p.gains_hi = gains_hi;
     p.rec = rec; p.best = best; p.gsw = gsw;
     p.N = N; p.U = U; p.Gfull = Gfull; p.sub = sub; p.U_hi = U_hi; p.mix = mix; p.ld = T; p.ldw = w_stride;
-    p.m = m; p.m2 = n_extra > 0 ? m_extra[0] : 0; p.m3 = n_extra > 1 ? m_extra[1] : 0; p.m4 = 0; p.nl = nl;
+    p.m = m; p.m2 = n_extra > 0 ? m_extra[0] : 0; p.m3 = n_extra > 1 ? m_extra[1] : 0;
+    p.m4 = n_extra > 2 ? m_extra[2] : 0; p.nl = nl;
     p.svA = sv; p.svB = sv; p.capA = sv_words(T, pp); p.capB = 0;
 
     // pass 1: free start, the path state before sample h (src/tcq_proto.py:594-599)

@@ -83,11 +83,14 @@ __host__ __device__ constexpr int cpar(unsigned v)
     return (int)(v & 1u);
 }
 
-// A branch-error row of one trellis step: NL labels x NP parity classes, permuted for this lane's label variant.
+// A branch-error row of one trellis step: NL labels x NP parity classes.  Compile-time masks: permuted for this lane's
+// label variant and held in registers (r).  Run-time masks: one unpermuted row per step in shared memory (ptr), the
+// lane part pl of the label applied per butterfly.
 template <int EW>
 struct ERow {
     float r[EW];
     const float* ptr;
+    int pl;
 };
 
 // Compile-time masks: label bits of every register are constants after unrolling.
@@ -160,7 +163,10 @@ struct FwdSmem {
 __host__ __device__ inline FwdSmem fwd_smem(int T, int G, int Gfull, int sub, int NL, int NP, int U, int U_hi)
 {
     FwdSmem L;
-    const int NV = NL / 2, EW = NL * NP;
+    // branch-error rows: NL / 2 label variants per step for the compiled-in mask sets (NL <= 16); one row per step for
+    // run-time masks, the only kind with NL = 32 (sized for the variants below that, which the run-time kernels leave
+    // partly unused)
+    const int NV = NL >= 32 ? 1 : NL / 2, EW = NL * NP;
     int o = 0;
     L.x = o; o = al16(o + 4 * T);
     L.w = o; o = al16(o + 4 * T);
@@ -232,9 +238,10 @@ __device__ __forceinline__ float branch_err(float x, float g, const float* tl, i
 }
 
 template <class MP, int EW>
-__device__ __forceinline__ void load_row(ERow<EW>& e, const float* row)
+__device__ __forceinline__ void load_row(ERow<EW>& e, const float* row, int pl = 0)
 {
     e.ptr = row;
+    e.pl = pl;
     if (!MP::RT) {
 #pragma unroll
         for (int k = 0; k < EW; k += 4) {
@@ -267,7 +274,7 @@ __device__ __forceinline__ float errv(const MP& mp, const ERow<EW>& E)
         constexpr int i = ((MP::template qc<J, RA>() << 1) | C) * NPc + P;
         return E.r[i];
     } else {
-        const int i = ((mp.template q<J, RA>() << 1) | C) * NPc + P;
+        const int i = (((mp.template q<J, RA>() ^ E.pl) << 1) | C) * NPc + P;
         return E.ptr[i];
     }
 }
@@ -550,14 +557,14 @@ static __device__ __forceinline__ void merge_any(int G, const float* s_dp, float
 // parity class, w * min_u (x - g tab[u])^2, written in the NV label variants err'[P][v] = err[v ^ (P << 1)].
 // UC > 0: the table width U as a compile-time constant (the minimum over u unrolled, same operations in the same
 // order); UC = 0: any U and the half-integer tables (mix > 0).
-template <int NL, int NP, bool MD, int UC>
+template <int NL, int NP, bool MD, int UC, bool VAR>
 static __device__ __forceinline__ void build_err_u(float* myerr, const float* s_x, const float* s_w, const float* s_tab,
                                                 const float* s_tabhi, float gain, float gainhi, int t0, int sub, int U,
                                                 int U_hi, int mix, int lane)
 {
-    constexpr int NV = NL / 2, EW = NL * NP;
+    constexpr int NV = VAR ? NL / 2 : 1, EW = NL * NP;  // label variants per step (none for run-time masks)
     __syncwarp();
-    if constexpr (UC > 0) {
+    if constexpr (UC > 0 && 32 % EW == 0) {
         // EW divides 32, so every entry of this lane has the same (label, class) pair: its table values and its NV
         // destination offsets are loaded / computed once (the stores below could alias s_tab for the compiler, which
         // then reloaded the table for every entry); the arithmetic per entry is unchanged
@@ -605,21 +612,21 @@ static __device__ __forceinline__ void build_err_u(float* myerr, const float* s_
     __syncwarp();
 }
 
-template <int NL, int NP, bool MD>
+template <int NL, int NP, bool MD, bool VAR>
 static __device__ __forceinline__ void build_err(float* myerr, const float* s_x, const float* s_w, const float* s_tab,
                                                  const float* s_tabhi, float gain, float gainhi, int t0, int sub,
                                                  int U, int U_hi, int mix, int lane)
 {
     if (mix == 0) {
         switch (U) {
-            case 2: build_err_u<NL, NP, MD, 2>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
-            case 4: build_err_u<NL, NP, MD, 4>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
-            case 8: build_err_u<NL, NP, MD, 8>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
-            case 16: build_err_u<NL, NP, MD, 16>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
+            case 2: build_err_u<NL, NP, MD, 2, VAR>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
+            case 4: build_err_u<NL, NP, MD, 4, VAR>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
+            case 8: build_err_u<NL, NP, MD, 8, VAR>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
+            case 16: build_err_u<NL, NP, MD, 16, VAR>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane); return;
             default: break;
         }
     }
-    build_err_u<NL, NP, MD, 0>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane);
+    build_err_u<NL, NP, MD, 0, VAR>(myerr, s_x, s_w, s_tab, s_tabhi, gain, gainhi, t0, sub, U, U_hi, mix, lane);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -632,7 +639,8 @@ template <class MP, int MD, bool SUB2>
 __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, unsigned char* smem, const float* xrow,
                                              const float* wrow)
 {
-    constexpr int NL = MP::NL, NP = MD ? 2 : 1, NV = NL / 2, EW = NL * NP;
+    constexpr int NL = MP::NL, NP = MD ? 2 : 1, EW = NL * NP;
+    constexpr int NV = MP::RT ? 1 : NL / 2;  // branch-error row variants per step (run-time masks: one, unpermuted)
     constexpr bool PP = MD == 1, G4 = MD >= 2, EQ = MD == 3;
     const int T = p.T, G = p.G, sub = p.sub, nsub = T / sub, U = p.U, U_hi = p.U_hi, mix = p.mix, Gf = p.Gfull;
     const int tid = threadIdx.x, lane = tid & 31, g = tid >> 5, nthr = blockDim.x;
@@ -702,8 +710,8 @@ __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, un
     float* s_mg = s_dp + (size_t)G * NSP;  // merged metrics after a sub-block boundary
     auto build = [&](int sb) {
         const int gi = p.cand ? (int)s_gc[sb * G + g] : g;
-        build_err<NL, NP, MD != 0>(myerr, s_x, s_w, s_tab, s_tabhi, s_gain[gi], s_gainhi[gi], sb * sub, sub, U, U_hi, mix,
-                                   lane);
+        build_err<NL, NP, MD != 0, !MP::RT>(myerr, s_x, s_w, s_tab, s_tabhi, s_gain[gi], s_gainhi[gi], sb * sub, sub, U,
+                                            U_hi, mix, lane);
     };
     // per-lane exchange addresses: layout-0 reads (4 bases, by r & 3) and layout-4 chunk writes (4 bases, by chunk)
     int rbase[4], wbase[4];
@@ -749,7 +757,12 @@ __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, un
 
     // ---- forward: groups of 4 steps ----
     int sb = 0, tt = 0;  // sub-block of the next step, its offset in the sub-block
-    auto row = [&](int off, int j) -> const float* { return myerr + ((size_t)(tt + off) * NV + PLj[j]) * EW; };
+    // the branch-error row of step tt + off for this lane's label part in layout j: its variant (compiled-in masks) or
+    // the unpermuted row with the lane part kept beside it (run-time masks)
+    auto lrow = [&](ERow<EW>& e, int off, int j) {
+        if constexpr (MP::RT) load_row<MP>(e, myerr + (size_t)(tt + off) * EW, PLj[j]);
+        else load_row<MP>(e, myerr + ((size_t)(tt + off) * NV + PLj[j]) * EW);
+    };
     const float* src = mydp;
     // survivor words: groups that fit entirely in region A are stored through a plain pointer
     const long long gw4 = (long long)p.W4 * 32;
@@ -760,16 +773,16 @@ __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, un
         __syncwarp();
         read0(cur, src);
         ERow<EW> E0, E1;
-        load_row<MP>(E0, row(0, 0));
-        load_row<MP>(E1, row(1, 1));
+        lrow(E0, 0, 0);
+        lrow(E1, 1, 1);
         // plain mode: the second pair's rows load with the first pair's, so their latency overlaps the first pair
         // (measured: faster for plain, slower for the parity modes, whose units hold more registers)
         constexpr bool EARLY_ROWS = MD == 0 && !SUB2;
         ERow<EW> P2, P3;
         if constexpr (EARLY_ROWS) {
             if (t4 + 2 < T) {
-                load_row<MP>(P2, row(2, 2));
-                load_row<MP>(P3, row(3, 3));
+                lrow(P2, 2, 2);
+                lrow(P3, 3, 3);
             }
         }
         uint32_t wd[9];
@@ -797,8 +810,8 @@ __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, un
                 E2 = P2;
                 E3 = P3;
             } else {
-                load_row<MP>(E2, row(0, 2));
-                load_row<MP>(E3, row(1, 3));
+                lrow(E2, 0, 2);
+                lrow(E3, 1, 3);
             }
             if constexpr (MD == 0) {
                 wd[1] = pair_plain<2>(mp, cur, E2, E3);

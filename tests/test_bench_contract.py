@@ -31,3 +31,18 @@ def test_short_warmup_refused():
     p = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1"],
                        cwd=ROOT, capture_output=True, text=True, timeout=300)
     assert p.returncode != 0 and "--warmup must be at least 3" in p.stderr
+
+
+def test_cpu_baseline_names_reference_and_port():
+    """cpu_baseline: the reference's own torch viterbi_ub when its install is present (kind "reference"), with the
+    oracle's C port timed beside it as a second, labelled number; the port alone otherwise."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from oracle.refroot import reference_root
+    cb = bench.cpu_baseline_sample(1.0, port_seconds=1.0)
+    assert cb["value"] > 0 and cb["cores"] >= 1 and cb["unit"] == bench.METRIC
+    if reference_root() is not None:
+        assert cb["kind"] == "reference" and "viterbi_ub" in cb["sample"]
+        assert cb["port"]["kind"] == "port" and cb["port"]["value"] > 0 and "tcq_oracle.c" in cb["port"]["sample"]
+    else:
+        assert cb["kind"] == "port" and "port" not in cb

@@ -135,3 +135,28 @@ def direct_cases(N=16, seed=11):
         init = rng.integers(0, 1024, N).astype(np.int32)
         out.append((f"tail_rot_{name}", dict(kw, init_state=init, _tail=True, _rot=128, return_code=True), x, None))
     return out
+
+
+def nl32_cases(N=12, seed=31):
+    """32 label subsets (three extra masks; no format of the tables uses them, the reference kernel accepts them): the
+    run-time-mask kernel in the plain, D2 and D4 modes, with gain candidates, and a single carried pass."""
+    rng = np.random.default_rng(seed)
+    me = (77, 301, 123)
+    out = []
+
+    def table(K):
+        U = 1 << (K - 1)
+        q = np.sort(rng.standard_normal(32 * U)).astype(np.float32)
+        return q.reshape(U, 32).T.copy().reshape(-1)
+    g4 = np.asarray(F["TCQ3X"]["gains_cpu"], np.float32)
+    g8 = np.asarray(F["TCQ4X"]["gains_cpu"], np.float32)
+    base = dict(nu=10, m=359, sub=16, m_extra=me, tail_biting=True, return_code=True)
+    out.append(("nl32_plain", dict(base, K=2, small=table(2), gains=g4), _x(rng, N, 256), None))
+    for pp in (1, 2):
+        out.append((f"nl32_pp{pp}", dict(base, K=3, small=table(3), gains=g4, pair_parity=pp), _x(rng, N, 256), None))
+    out.append(("nl32_cand2of8", dict(base, K=3, small=table(3), gains=g8, n_cand=2, tb_window=32),
+                _x(rng, N, 256), rng.uniform(0.2, 3.0, 256).astype(np.float32)))
+    init = rng.integers(0, 1024, N).astype(np.int32)
+    out.append(("nl32_carry", dict(K=2, nu=10, m=359, sub=16, m_extra=me, small=table(2), gains=g4, init_state=init,
+                                   return_end_state=True), _x(rng, N, 256), None))
+    return out
