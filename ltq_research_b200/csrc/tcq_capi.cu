@@ -18,7 +18,8 @@ long long sv_words(int T, int pp)  // words per (tile, gain slot), one lane row 
 int gsel_planes(int G) { return G <= 2 ? 1 : (G <= 4 ? 2 : 4); }
 
 // The reference's validation table (src/cuda/tcq_viterbi.cu:748-751 and the dispatch limits :720-763) plus this
-// implementation's limit S = 1024 (the reference also runs S = 256 with 4 subsets).  The reference's TCQ_BLOCK switch only picks its thread-block shape.
+// implementation's G values (1, 2, 3, 4, 8: the reference's dispatch).  S = 256 (4 subsets, plain mode, by the
+// reference's table) runs the 256-state kernel.  The reference's TCQ_BLOCK switch only picks its thread-block shape.
 static bool valid(int N, int T, int S, int U, int G, int Gfull, bool cand, int sub, int U_hi, int mix, int nl, int ld,
                   int pp)
 {
@@ -31,7 +32,7 @@ static bool valid(int N, int T, int S, int U, int G, int Gfull, bool cand, int s
         nl * U_hi > 4 * MAXU)
         return false;
     if (!(G == 1 || G == 2 || G == 3 || G == 4 || G == 8)) return false;
-    if (S != 1024 || nl > 32 || U < 1 || U_hi < 1) return false;
+    if ((S != 1024 && S != 256) || nl > 32 || U < 1 || U_hi < 1) return false;
     if (cand && G > Gfull) return false;
     return true;
 }
@@ -58,8 +59,12 @@ static int dispatch(const VitParams& p, int pp, cudaStream_t st)
 }
 
 // one Viterbi pass over N tiles (the reference kernel's contract)
-static int run_pass(VitParams p, int pp, cudaStream_t st)
+static int run_pass(VitParams p, int pp, int S, cudaStream_t st)
 {
+    if (S == 256) {
+        if (p.N <= 0) return (int)cudaErrorInvalidConfiguration;
+        return run_pass_s256(p, st);
+    }
     p.W4 = words_per_group(pp);
     p.NB = gsel_planes(p.G);
     p.nsl = p.T / p.sub;
@@ -98,7 +103,7 @@ extern "C" int tcq_viterbi(const float* x, const float* w, const float* tab, con
     p.mix = mix; p.ld = ld; p.ldw = ld; p.rot = rot; p.m = m; p.m2 = m2; p.m3 = m3; p.m4 = m4; p.nl = nl;
     p.cand = gcand != nullptr;
     // gsel bytes per tile in the reference layout: (T / sub) * 1024; ours: (T / sub) * 512 — fits
-    const int rc = run_pass(p, pp, (cudaStream_t)stream);
+    const int rc = run_pass(p, pp, S, (cudaStream_t)stream);
     if (rc != 0) return rc;
     return (int)cudaGetLastError();
 }
@@ -125,7 +130,7 @@ extern "C" int ltq_viterbi_tb(const float* x, const float* w, int w_stride, cons
                               int mix, int pp, int tb_passes, int tb_cand1, int tb_window, void* workspace,
                               size_t workspace_bytes, void* stream)
 {
-    if (nu != 10 || K < 1 || K > 8 || n_extra < 0 || n_extra > 3 || tb_passes < 2 || tb_window < 0 ||
+    if ((nu != 10 && nu != 8) || K < 1 || K > 8 || n_extra < 0 || n_extra > 3 || tb_passes < 2 || tb_window < 0 ||
         (n_extra > 0 && !m_extra))
         return -1;
     const int S = 1 << nu, U = 1 << (K - 1), nl = 4 << n_extra, h = T / 2;
@@ -166,7 +171,7 @@ extern "C" int ltq_viterbi_tb(const float* x, const float* w, int w_stride, cons
     p1.G = G1; p1.cand = G1 < Gfull; p1.gcand = p1.cand ? gc : nullptr;
     p1.T = T1; p1.rot = tb_window ? h - tb_window : 0; p1.mid_t = tb_window ? tb_window : h; p1.mid_st = mid;
     p1.init_st = nullptr; p1.tail = 0; p1.code = nullptr;
-    int rc = run_pass(p1, pp, st);
+    int rc = run_pass(p1, pp, S, st);
     if (rc != 0) return rc;
     // further passes on the tile rotated by h, start = end = the middle state (src/tcq_proto.py:600-608)
     int shift = 0;
@@ -177,7 +182,7 @@ extern "C" int ltq_viterbi_tb(const float* x, const float* w, int w_stride, cons
         q.T = T; q.rot = shift; q.init_st = mid; q.tail = 1;
         if (pass + 1 < tb_passes) { q.mid_st = mid; q.mid_t = h; q.code = nullptr; }
         else { q.mid_st = nullptr; q.mid_t = 0; q.code = code; }
-        rc = run_pass(q, pp, st);
+        rc = run_pass(q, pp, S, st);
         if (rc != 0) return rc;
     }
     return (int)cudaGetLastError();

@@ -93,6 +93,7 @@ int launch_ct_m359_40_475(const VitParams& p, int md, int smem, cudaStream_t st)
 int launch_rt(const VitParams& p, int md, int smem, cudaStream_t st);               // any masks, nl 4 / 8 / 16
 int launch_rt_sub2(const VitParams& p, int md, int smem, cudaStream_t st);          // any masks, sub = 2 mod 4
 int launch_tb(const VitParams& p, int md, cudaStream_t st);                          // traceback + reconstruction
+int run_pass_s256(VitParams p, cudaStream_t st);                                      // the 256-state trellis
 // fused LDLQ block, per label-mask set (same sets as the forward kernel)
 int ldlq_ct_m359(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);
 int ldlq_ct_m359_241(const LdlqParams& q, int md, int smem, int grid, cudaStream_t st);

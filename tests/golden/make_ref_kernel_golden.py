@@ -65,3 +65,4 @@ if __name__ == "__main__":
     record(VC.menu_tb_cases(N=6, L=256, seed=23, window=32, weighted=True), out / "ref_kernel_menu_ldlq.npz")
     record(VC.special_cases(N=6, seed=24) + VC.direct_cases(N=6, seed=25), out / "ref_kernel_special.npz")
     record(VC.nl32_cases(N=6, seed=26), out / "ref_kernel_nl32.npz")
+    record(VC.s256_cases(N=6, seed=27), out / "ref_kernel_s256.npz")

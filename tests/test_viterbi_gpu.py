@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 
 ALL_CASES = (VC.menu_tb_cases(N=24, L=256, seed=1) + VC.menu_tb_cases(N=16, L=160, seed=2)
              + VC.menu_tb_cases(N=16, L=256, seed=4, window=32, weighted=True) + VC.special_cases()
-             + VC.direct_cases() + VC.nl32_cases())
+             + VC.direct_cases() + VC.nl32_cases() + VC.s256_cases())
 
 
 def _to_dev(kw, dev):

@@ -160,3 +160,33 @@ def nl32_cases(N=12, seed=31):
     out.append(("nl32_carry", dict(K=2, nu=10, m=359, sub=16, m_extra=me, small=table(2), gains=g4, init_state=init,
                                    return_end_state=True), _x(rng, N, 256), None))
     return out
+
+
+def s256_cases(N=12, seed=41):
+    """The 256-state trellis (nu = 8; 4 subsets, plain mode, as the reference's table allows): tail-biting with and
+    without the first-pass window, gain candidates, all 8 gains, half-integer tables, a carried pass and a middle-state
+    pass."""
+    rng = np.random.default_rng(seed)
+
+    def table(K):
+        U = 1 << (K - 1)
+        q = np.sort(rng.standard_normal(4 * U)).astype(np.float32)
+        return q.reshape(U, 4).T.copy().reshape(-1)
+    g4 = np.asarray(F["TCQ3X"]["gains_cpu"], np.float32)
+    g8 = np.asarray(F["TCQ4X"]["gains_cpu"], np.float32)
+    base = dict(nu=8, m=91, sub=16, tail_biting=True, return_code=True)
+    out = [("s256_k2", dict(base, K=2, small=table(2), gains=g4), _x(rng, N, 256), None),
+           ("s256_k3_window", dict(base, K=3, small=table(3), gains=g4, tb_window=32), _x(rng, N, 256),
+            rng.uniform(0.2, 3.0, 256).astype(np.float32)),
+           ("s256_g8", dict(base, K=3, small=table(3), gains=g8), _x(rng, N, 256), None),
+           ("s256_cand3of8", dict(base, K=3, small=table(3), gains=g8, n_cand=3), _x(rng, N, 256), None)]
+    c2, c3 = F["TCQ3X1"], F["TCQ4X1"]
+    out.append(("s256_mix16", dict(base, K=3, m=45, small=np.asarray(c2["lut"], np.float32)[:16],
+                                   gains=np.asarray(c2["gains_cpu"], np.float32),
+                                   small_hi=np.asarray(c3["lut"], np.float32)[:32],
+                                   gains_hi=np.asarray(c3["gains_cpu"], np.float32), mix=16), _x(rng, N, 256), None))
+    init = rng.integers(0, 256, N).astype(np.int32)
+    out.append(("s256_carry", dict(K=2, nu=8, m=91, sub=16, small=table(2), gains=g4, init_state=init,
+                                   return_end_state=True), _x(rng, N, 256), None))
+    out.append(("s256_mid", dict(K=3, nu=8, m=91, sub=16, small=table(3), gains=g4, _mid=128), _x(rng, N, 256), None))
+    return out
