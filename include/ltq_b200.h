@@ -35,9 +35,9 @@ const char* ltq_b200_version(void);
  * bp [N, T, G, S/32] u32, gsel [N, T/sub, S] u8 and pbits (pp = 1: [N, T/2, G, S/32]; pp >= 2: [N, T/4, G, 9, S/32])
  * are caller-allocated scratch of the sizes the reference's Python wrapper allocates (src/tcq_proto.py:623-637);
  * this implementation stores its own survivor layout in them.
- * Limits beyond the reference: S must be 1024 (nu = 10; the reference also runs S = 256 with 4 subsets); with pp = 1
- * and T < 10 the caller's scratch is too small for the survivor layout (returns -1).  nl = 32 (m2, m3, m4 all used)
- * runs the run-time-mask kernel.
+ * S = 1024 (nu = 10) or 256 (nu = 8; 4 subsets and plain mode, the reference's table); nl = 32 (m2, m3, m4 all used)
+ * runs the run-time-mask kernel.  Limit beyond the reference: with pp = 1 and T < 10 the caller's scratch is too small
+ * for the survivor layout (returns -1).
  */
 int tcq_viterbi(const float* x, const float* w, const float* tab, const float* gains, float* rec, uint32_t* bp,
                 uint8_t* gsel, const int* init_st, int* end_st, const float* tab_hi, const float* gains_hi,
@@ -53,6 +53,7 @@ int tcq_viterbi(const float* x, const float* w, const float* tab, const float* g
  * original positions.
  *   x [N, T] fp32; w: per-position weights, row stride w_stride (0 = one row [T] shared by all tiles);
  *   tab [nl * 2^(K-1)], gains [Gfull]; tab_hi / gains_hi / mix: half-integer mode (NULL / 0 when unused);
+ *   nu: 10 (1024 states) or 8 (256 states, no extra masks, pp = 0);
  *   m: primary label mask, m_extra[n_extra]: extra label masks (n_extra <= 3, nl = 4 << n_extra);
  *   n_cand: Viterbi over n_cand gain candidates per sub-block (0 = all Gfull); pp: 0 none, 1 D2, 2 D4, 3 EQ.
  * workspace: device memory of at least ltq_viterbi_tb_workspace_bytes(...) bytes, 256-byte aligned.
