@@ -65,18 +65,6 @@ def _check(rc: int, what: str):
         raise RuntimeError(f"{what}: error {rc}")
 
 
-def _split6(x: torch.Tensor, xbs: int, rows: int, cols: int, batch: int, order: int, side: int, neg: bool,
-            ld: int) -> torch.Tensor:
-    """Batched six-slot bf16 operand (ltq_bf16x6_split_batched) of `batch` rows x cols matrices at x + z * xbs (row
-    stride ld): [batch, rows, 6 cols] (side 0) or [batch, 6 rows, cols] (side 1)."""
-    shape = (batch, rows, 6 * cols) if side == 0 else (batch, 6 * rows, cols)
-    out = torch.empty(shape, dtype=torch.bfloat16, device=x.device)
-    _check(_lib.lib().ltq_bf16x6_split_batched(
-        x.data_ptr(), ld, xbs, rows, cols, batch, order, side, int(neg), ptr(out), out.stride(1), out.stride(0),
-        _stream(x.device)), "ltq_bf16x6_split_batched")
-    return out
-
-
 def _square_fp32_cuda(A: torch.Tensor, what: str):
     if A.dim() != 2 or A.shape[0] != A.shape[1] or A.shape[0] % QK or A.dtype != torch.float32 or not A.is_cuda:
         raise ValueError(f"{what}: a square fp32 CUDA matrix with a multiple of 256 rows is required")

@@ -112,22 +112,6 @@ def _right6(b: torch.Tensor) -> torch.Tensor:
     return o if o is not None else _bcat(_split3(b))
 
 
-def _gram_lower6(x: torch.Tensor) -> torch.Tensor:
-    """x^T x ([K, K]) of an fp32 [M, K] in the six-product form, for a consumer that reads the lower triangle only:
-    the leading half square and the rows below it are computed (three quarters of the product), the 256-column blocks
-    above the diagonal blocks of the rest are left uninitialised."""
-    K = x.shape[1]
-    left, right = _left6(x.T), _right6(x)  # [K, 6 M], [6 M, K]
-    h = QK_K * (K // QK_K // 2) if K >= 4 * QK_K else K
-    C = torch.empty((K, K), dtype=torch.float32, device=x.device)
-    top = C[:h, :h]
-    torch.addmm(top, left[:h], right[:, :h], beta=0, out_dtype=torch.float32, out=top)
-    if h < K:
-        bottom = C[h:]
-        torch.addmm(bottom, left[h:], right, beta=0, out_dtype=torch.float32, out=bottom)
-    return C
-
-
 def _mm(a: torch.Tensor, b: torch.Tensor, gemm: str) -> torch.Tensor:
     """a @ b for fp32 [M, K] x [K, N] in the given mode: torch's fp32 matmul, or the six-product tensor-core GEMM."""
     if gemm == "fp32":

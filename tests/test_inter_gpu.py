@@ -133,15 +133,16 @@ def test_block_inverses_from_the_cholesky_factor(cuda_dev):
 
 
 @pytest.mark.parametrize("K", [512, 1024, 1280])
-def test_gram_lower6_lower_triangle(K, cuda_dev):
-    """_gram_lower6(x) (the refit's Gram matrix, computed on the lower triangle's cover only) against fp64 x^T x: every
-    element on or below the diagonal within the fp32 error bound of a dot product of length M, and every 256 x 256
-    diagonal block computed in full (the blockwise Cholesky reads whole diagonal blocks)."""
-    from ltq_research_b200.liqk_v2 import _gram_lower6
+def test_gram_lower_lower_triangle(K, cuda_dev):
+    """tcgemm.gram_lower(x) (the refit's Gram matrix on the tcgen05 GEMM, computed on the lower triangle's cover only,
+    as the fast mode calls it) against fp64 x^T x: every element on or below the diagonal within the fp32 error bound
+    of a dot product of length M, and every 256 x 256 diagonal block computed in full (the blockwise Cholesky reads
+    whole diagonal blocks)."""
+    from ltq_research_b200 import tcgemm
     g = torch.Generator().manual_seed(K)
     M = 640
     x = _wide((M, K), g, cuda_dev)
-    C = _gram_lower6(x)
+    C = tcgemm.gram_lower(x, 256 * (K // 256 // 2) if K >= 4 * 256 else K)
     torch.cuda.synchronize()
     xd = x.double()
     want = xd.T @ xd

@@ -50,10 +50,15 @@ def test_validation_matches_reference(over):
     assert _call(**over) == -1
 
 
-def test_limits_beyond_reference():
-    """Documented limits of this implementation: 1024 states, at most 16 subsets."""
-    assert _call(S=256) == -1
-    assert _call(nl=32, U=2) == -1
+def test_state_and_subset_limits():
+    """The 256-state trellis and 32 label subsets are accepted (GPU tests check them); what the reference's table
+    rejects around them is rejected before any launch: 256 states with a parity mode or extra subsets, other state
+    counts, 32 subsets with too wide a table or too many slot x step x label errors."""
+    assert _call(S=256, pp=1) == -1
+    assert _call(S=256, nl=16, m2=5, m3=9) == -1
+    assert _call(S=512) == -1 and _call(S=2048) == -1
+    assert _call(nl=32, U=32) == -1
+    assert _call(nl=32, U=2, G=8, Gfull=8, sub=32) == -1
 
 
 def test_workspace_size():
