@@ -159,6 +159,13 @@ int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt3, float* X, lo
 int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t* B, long long ldb, float* C, long long ldc,
                      int M, int N, int Kd, float alpha, float beta, int* err, void* stream);
 /*
+ * Self-test of the GEMMs' bounded pipeline waits (device pointers err, done): one thread waits on an mbarrier that
+ * expects one arrival.  arrive = 1: the arrival is made first, the wait completes, *done = 1.  arrive = 0: nothing
+ * arrives, the wait gives up after `limit` polls (1 .. 2^26), sets *err = 1 and returns, *done = 2 — the path a lost
+ * TMA or MMA completion takes inside the GEMMs, run without a fault or a hang.
+ */
+int ltq_gemm_wait_selftest(int arrive, unsigned int limit, int* err, int* done, void* stream);
+/*
  * The same product in the six-product form from compact three-part operands A3 = [a0 a1 a2] [M, 3 Kp] and
  * B3 = [b0 b1 b2] [N, 3 Kp] (x = x0 + x1 + x2 the three-way bf16 split of an fp32 operand):
  *     C = beta C + alpha (a0 b0^T + a0 b1^T + a1 b0^T + a0 b2^T + a1 b1^T + a2 b0^T),

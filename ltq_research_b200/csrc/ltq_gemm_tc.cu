@@ -74,13 +74,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity)
         : "memory");
     return ok != 0;
 }
-// bounded wait for the phase with parity `parity`; false after GEMM_WAIT_LIMIT polls (the timeout is recorded)
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err)
+// bounded wait for the phase with parity `parity`; false after `limit` polls (the timeout is recorded in *err)
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err, uint32_t limit = GEMM_WAIT_LIMIT)
 {
-    for (uint32_t i = 0; i < GEMM_WAIT_LIMIT; i++)
+    for (uint32_t i = 0; i < limit; i++)
         if (mbar_try_wait(b, parity)) return true;
     if (err) atomicExch(err, 1);
     return false;
+}
+
+// Self-test of the bounded wait: one thread waits on a fresh mbarrier that expects one arrival; with arrive = 1 the
+// arrival is made first and the wait completes (*done = 1), with arrive = 0 nothing arrives and the wait gives up after
+// `limit` polls, sets *err and returns (*done = 2).  No copy, no tensor memory: the timeout path runs without a fault.
+__global__ void gemm_wait_selftest_kernel(int arrive, uint32_t limit, int* err, int* done)
+{
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        if (arrive) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&bar)) : "memory");
+        *done = mbar_wait(&bar, 0, err, limit) ? 1 : 2;
+    }
 }
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar)
@@ -527,6 +541,13 @@ bool make_map(CUtensorMap* m, const void* base, int rows, int cols, long long ld
 }
 
 }  // namespace
+
+extern "C" int ltq_gemm_wait_selftest(int arrive, unsigned int limit, int* err, int* done, void* stream)
+{
+    if (!err || !done || limit == 0 || limit > GEMM_WAIT_LIMIT) return -1;
+    gemm_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(arrive, limit, err, done);
+    return (int)cudaGetLastError();
+}
 
 extern "C" int ltq_gemm_bf16_tn(const uint16_t* A, long long lda, const uint16_t* B, long long ldb, float* C,
                                 long long ldc, int M, int N, int Kd, float alpha, float beta, int* err, void* stream)

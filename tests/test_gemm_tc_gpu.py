@@ -251,3 +251,22 @@ def test_mm_and_gram_within_fp32_bound(cuda_dev):
     low = torch.tril(torch.ones(1024, 1024, dtype=torch.bool, device=cuda_dev))
     torch.cuda.synchronize()
     assert ((C.double() - ref).abs() <= bound)[low].all()
+
+
+def test_bounded_wait_times_out_with_error_flag(cuda_dev):
+    """The GEMMs' pipeline waits are bounded: a wait on an mbarrier that nothing completes gives up after its poll limit,
+    sets the error flag and returns (the kernel ends, the context stays usable); the same wait completes when the
+    arrival is made.  No copy and no tensor memory are involved."""
+    from ltq_research_b200 import _lib
+    L = _lib.lib()
+    st = torch.cuda.current_stream(cuda_dev).cuda_stream
+    for arrive, want_err, want_done in ((1, 0, 1), (0, 1, 2)):
+        err = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+        done = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+        assert L.ltq_gemm_wait_selftest(arrive, 4096, err.data_ptr(), done.data_ptr(), st) == 0
+        torch.cuda.synchronize()
+        assert int(err) == want_err and int(done) == want_done, (arrive, int(err), int(done))
+    assert L.ltq_gemm_wait_selftest(0, 0, err.data_ptr(), done.data_ptr(), st) == -1
+    # the device still runs work afterwards
+    x = torch.ones(1024, device=cuda_dev)
+    assert float(x.sum()) == 1024.0
