@@ -147,6 +147,14 @@ int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* X, long lon
  * *info = c0 + j + 1 when *info is 0 (LAPACK's convention).  The panel and trailing updates are tensor-core GEMMs.
  */
 int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt3, float* X, long long ldx, int* info, void* stream);
+/*   (ldx = 256 with c0 > 0: X is the 256 x 256 inverse alone, the compact form ltq_chol_solve reads.) */
+/*
+ * The refit system's solve (src/liqk_v2.py:1161-1163, A_in suh = b_in with A_in = L L^T): x = L^-T L^-1 b for the
+ * blocked factor L [K, K] (row-major, row stride ld, K a multiple of 256) and the inverses Dinv [K/256][256][256] of
+ * its diagonal blocks (lower triangles, from ltq_chol256_diag).  2 K / 256 launches on `stream`; work: 2 K floats.
+ */
+int ltq_chol_solve(const float* L, long long ld, int K, const float* Dinv, const float* b, float* x, float* work,
+                   void* stream);
 /*
  * Tensor-core GEMM of the fast mode's fp32-accurate products (tcgen05.mma, accumulator in tensor memory, operands by
  * TMA): C[M, N] = beta * C + alpha * A[M, Kd] B[N, Kd]^T with A, B bf16 (K contiguous, row strides lda / ldb) and C

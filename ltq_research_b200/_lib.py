@@ -46,6 +46,7 @@ SIGNATURES = {
     "ltq_gemm_bf16_tn": (I, [P, LL, P, LL, P, LL, I, I, I, ctypes.c_float, ctypes.c_float, P, P]),
     "ltq_gemm_bf16x6_tn": (I, [P, LL, P, LL, P, LL, I, I, I, ctypes.c_float, ctypes.c_float, P, P]),
     "ltq_gemm_wait_selftest": (I, [I, ctypes.c_uint, P, P, P]),
+    "ltq_chol_solve": (I, [P, LL, I, P, P, P, P, P]),
     "ltq_gemm_bf16x3p_tn": (I, [P, LL, LL, P, LL, LL, P, LL, LL, I, I, I, I, I, ctypes.c_float, ctypes.c_float, P, P]),
     "ltq_bf16x3_split": (I, [P, LL, LL, I, I, I, I, I, I, P, LL, LL, P]),
     "ltq_ldlq_inter3": (I, [P, LL, P, LL, P, LL, P, LL, I, P, LL, P, LL, P, P]),
@@ -71,7 +72,7 @@ KERNELS_PER_CALL = {
     "ltq_viterbi_tb": lambda a: 2 * int(a[22]),
     "ltq_viterbi_tb_noalloc": lambda a: 2 * int(a[22]),
     "ltq_fwht256": 1, "ltq_scale_fit": 1, "ltq_ldlq_gather": 1, "ltq_ldlq_feedback": 1, "ltq_ldlq_block": 2,
-    "ltq_ldlq_bcat": 1, "ltq_ldlq_bcat_t": 1, "ltq_gemm_bf16_tn": 1, "ltq_gemm_bf16x6_tn": 1, "ltq_gemm_bf16x3p_tn": 1, "ltq_gemm_wait_selftest": 1, "ltq_bf16x3_split": 1,
+    "ltq_ldlq_bcat": 1, "ltq_ldlq_bcat_t": 1, "ltq_gemm_bf16_tn": 1, "ltq_gemm_bf16x6_tn": 1, "ltq_gemm_bf16x3p_tn": 1, "ltq_gemm_wait_selftest": 1, "ltq_chol_solve": lambda a: 2 * (int(a[2]) // 256), "ltq_bf16x3_split": 1,
     "ltq_ldlq_inter": 1, "ltq_ldlq_inter3": 1, "ltq_bf16x6_split": 1, "ltq_bf16x6_split_batched": 1,
     "ltq_trtri256_lower": 1, "ltq_chol256_diag": 1, "lut_subs_quant": 1, "ltq_int8_rings": 1, "ltq_matvec_slice": 1,
     "ltq_pack_slice": 1, "ltq_decode_slice": 1,

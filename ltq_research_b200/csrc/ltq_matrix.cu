@@ -462,8 +462,9 @@ __global__ void __launch_bounds__(128) trtri256_lower_kernel(const float* __rest
 //   phase 2, Y = L~^-1 by Gauss-Jordan on the identity: at pivot j the owners of tile row j/8 broadcast row j of Y and
 //     every tile below it and left of it takes y_ik -= L~_ij y_jk (rows i > j); then X = L^-1 = D^-1/2 Y;
 //   outputs: L in A's block (zeros above the diagonal); xt3 [256][768] (bf16) = the compact right operand of the panel
-//     product A_21 X^T for ltq_gemm_bf16x3p_tn, row n = [x0 x1 x2] of row n of X (every element written); X itself in the
-//     block at (c0, c0) of Xo (row stride ldx) when Xo is given; *info = c0 + j + 1 for the first pivot that is not
+//     product A_21 X^T for ltq_gemm_bf16x3p_tn, row n = [x0 x1 x2] of row n of X (every element written); X itself at Xo
+//     (the block's first element, row stride ldx; tiles on and below the diagonal) when Xo is given; *info = c0 + j + 1
+//     for the first pivot that is not
 //     positive (or NaN) when *info was 0 (LAPACK's convention).
 constexpr int LT_FLOATS = 33792;  // sum over columns of 256 - 8 * (j / 8)
 __device__ __forceinline__ int lt_col(int j)
@@ -630,7 +631,7 @@ __global__ void __launch_bounds__(544, 1) chol256_tiled_kernel(float* __restrict
         for (int cc = 0; cc < 8; cc++) a[r][cc] *= rs;
     }
     if (Xo) {
-        float* Xb = Xo + (long long)c0 * (ldx + 1);
+        float* Xb = Xo;  // the block's first element (the caller placed it)
 #pragma unroll
         for (int r = 0; r < 8; r++) {
             float* dst = Xb + (long long)(8 * bi + r) * ldx + 8 * bk;
@@ -659,6 +660,100 @@ __global__ void __launch_bounds__(544, 1) chol256_tiled_kernel(float* __restrict
             if (bi != bk)
                 *reinterpret_cast<uint4*>(xt3 + (long long)(8 * bk + r) * 768 + 256 * q + 8 * bi) = make_uint4(0, 0, 0, 0);
         }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Solve L L^T x = b for a blocked lower Cholesky factor L [K, K] (row-major, K a multiple of 256) given the inverses
+// Dinv[p] of its 256 x 256 diagonal blocks (as the factorization's leaves write them; upper parts zero).  Block forward
+// substitution, one launch per 256-row block and direction, no waits between CTAs:
+//   forward  step p: y_p = Dinv_p r_p, then r_q -= L[q, p] y_p for the blocks q > p;
+//   backward step p: x_p = Dinv_p^T r_p, then r_q -= L[p, q]^T x_p for the blocks q < p.
+// Every CTA of a step computes y_p (x_p) itself from the block's residual (a 256 x 256 product, from L2), then updates
+// its own 256 entries of r; CTA 0 writes y_p (x_p).  Each entry is one thread's fma chain in a fixed order: the result
+// is deterministic.  Multiplying by the inverted diagonal blocks instead of substituting is the form the factorization
+// itself uses for its panels (backward stable, slightly larger forward error than substitution).
+// ------------------------------------------------------------------------------------------------
+// 256 row sums out[i] = sum_k M[i][k] v[k] (k < 256) by a CTA of 1024 threads: warp w takes rows 8 w .. 8 w + 7, each
+// lane two float4 of a row (coalesced 512-byte rows), then a fixed shuffle tree per row
+__device__ __forceinline__ void rowdot256(const float* __restrict__ M, long long ldm, const float* v, float* out)
+{
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    float4 m[8][2];
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+            m[r][h] = __ldg(reinterpret_cast<const float4*>(M + (long long)(8 * w + r) * ldm + 128 * h + 4 * lane));
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+        float a = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int k = 128 * h + 4 * lane;
+            a = __fmaf_rn(m[r][h].x, v[k], a);
+            a = __fmaf_rn(m[r][h].y, v[k + 1], a);
+            a = __fmaf_rn(m[r][h].z, v[k + 2], a);
+            a = __fmaf_rn(m[r][h].w, v[k + 3], a);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) out[8 * w + r] = a;
+    }
+}
+
+// 256 column sums out[j] = sum_i M[i][j] v[i] (i < 256) by 1024 threads: thread (j, quarter) sums rows 64 quarter ..
+// + 63 of column j (reads coalesced along j), then the four quarters are added in order through `part`
+__device__ __forceinline__ void coldot256(const float* __restrict__ M, long long ldm, const float* v, float* part,
+                                          float* out)
+{
+    const int j = threadIdx.x & 255, qtr = threadIdx.x >> 8;
+    float a = 0.f;
+#pragma unroll 16
+    for (int i = 64 * qtr; i < 64 * qtr + 64; i++) a = __fmaf_rn(__ldg(M + (long long)i * ldm + j), v[i], a);
+    part[threadIdx.x] = a;
+    __syncthreads();
+    if (qtr == 0)
+        out[j] = __fadd_rn(__fadd_rn(__fadd_rn(part[j], part[256 + j]), part[512 + j]), part[768 + j]);
+}
+
+__global__ void __launch_bounds__(1024) chol_solve_fwd_step(const float* __restrict__ L, long long ld,
+                                                            const float* __restrict__ Dinv, float* __restrict__ r,
+                                                            float* __restrict__ y, int p, int K)
+{
+    __shared__ float rp[256], yp[256], u[256];
+    const int t = threadIdx.x, c0 = 256 * p;
+    if (t < 256) rp[t] = r[c0 + t];
+    __syncthreads();
+    // y_p = Dinv_p r_p (Dinv_p is lower with exact zeros above the diagonal)
+    rowdot256(Dinv + (size_t)p * 65536, 256, rp, yp);
+    __syncthreads();
+    if (blockIdx.x == 0 && t < 256) y[c0 + t] = yp[t];
+    const long long q0 = c0 + 256 + 256LL * blockIdx.x;  // this CTA's 256 rows of the blocks below p
+    if (q0 < K) {
+        rowdot256(L + q0 * ld + c0, ld, yp, u);
+        __syncthreads();
+        if (t < 256) r[q0 + t] = __fsub_rn(r[q0 + t], u[t]);
+    }
+}
+
+__global__ void __launch_bounds__(1024) chol_solve_bwd_step(const float* __restrict__ L, long long ld,
+                                                            const float* __restrict__ Dinv, float* __restrict__ r,
+                                                            float* __restrict__ x, int p)
+{
+    __shared__ float rp[256], xp[256], u[256], part[1024];
+    const int t = threadIdx.x, c0 = 256 * p;
+    if (t < 256) rp[t] = r[c0 + t];
+    __syncthreads();
+    // x_p = Dinv_p^T r_p: column sums of Dinv_p
+    coldot256(Dinv + (size_t)p * 65536, 256, rp, part, xp);
+    __syncthreads();
+    if (blockIdx.x == 0 && t < 256) x[c0 + t] = xp[t];
+    const int q0 = 256 * blockIdx.x;  // this CTA's 256 entries of the blocks before p
+    if (q0 < c0) {
+        coldot256(L + (long long)c0 * ld + q0, ld, xp, part, u);
+        __syncthreads();
+        if (t < 256) r[q0 + t] = __fsub_rn(r[q0 + t], u[t]);
     }
 }
 
@@ -825,7 +920,8 @@ extern "C" int ltq_trtri256_lower(const float* L, long long ldL, int nb, float* 
 extern "C" int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt3, float* X, long long ldx, int* info,
                                 void* stream)
 {
-    if (!A || !xt3 || !info || c0 < 0 || ld < c0 + 256LL || (X && ldx < c0 + 256LL)) return -1;
+    // X: the inverse at (c0, c0) of X (ldx >= c0 + 256), or the 256 x 256 inverse alone at X (ldx == 256)
+    if (!A || !xt3 || !info || c0 < 0 || ld < c0 + 256LL || (X && ldx != 256 && ldx < c0 + 256LL)) return -1;
     if (c0 % 4 || ld % 4 || (X && ldx % 4) || ((uintptr_t)A & 15) || ((uintptr_t)xt3 & 15) || ((uintptr_t)X & 15)) return -1;
     static std::atomic<int> attr_done[64];
     constexpr int smem = (LT_FLOATS + 768) * 4;
@@ -836,6 +932,27 @@ extern "C" int ltq_chol256_diag(float* A, long long ld, int c0, uint16_t* xt3, f
         if (e != cudaSuccess) return (int)e;
         attr_done[dev].store(1, std::memory_order_release);
     }
-    chol256_tiled_kernel<<<1, 544, smem, (cudaStream_t)stream>>>(A, ld, c0, xt3, X, ldx, info);
+    float* Xb = X ? (ldx == 256 ? X : X + (long long)c0 * (ldx + 1)) : nullptr;
+    chol256_tiled_kernel<<<1, 544, smem, (cudaStream_t)stream>>>(A, ld, c0, xt3, Xb, ldx, info);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ltq_chol_solve(const float* L, long long ld, int K, const float* Dinv, const float* b, float* x,
+                              float* work, void* stream)
+{
+    if (!L || !Dinv || !b || !x || !work || K <= 0 || K % 256 || ld < K || (ld % 4) || ((uintptr_t)L & 15)) return -1;
+    const cudaStream_t st = (cudaStream_t)stream;
+    const int nb = K / 256;
+    // work [2 K]: the residual r, then y
+    float* r = work;
+    float* y = work + K;
+    cudaError_t e = cudaMemcpyAsync(r, b, sizeof(float) * K, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return (int)e;
+    for (int p = 0; p < nb; p++) {
+        const int grid = nb - p - 1 > 0 ? nb - p - 1 : 1;
+        chol_solve_fwd_step<<<grid, 1024, 0, st>>>(L, ld, Dinv, r, y, p, K);
+    }
+    for (int p = nb - 1; p >= 0; p--)
+        chol_solve_bwd_step<<<p > 0 ? p : 1, 1024, 0, st>>>(L, ld, Dinv, y, x, p);
     return (int)cudaGetLastError();
 }

@@ -117,28 +117,35 @@ def _merge(Lr: torch.Tensor, X: torch.Tensor, a0: int, ba: int, bc: int, batch: 
     tcgemm.gemm3(tcgemm.split3(XC, neg=True, Kp=bc), tcgemm.split3(T, trans=True, Kp=bc), X21, bc)
 
 
-def cholesky_lower(A: torch.Tensor, inverse: bool = False, overwrite: bool = False
+def cholesky_lower(A: torch.Tensor, inverse: bool = False, overwrite: bool = False, diag_inv: bool = False
                    ) -> Tuple[torch.Tensor, torch.Tensor, Optional[torch.Tensor]]:
     """(L, info, X): the lower Cholesky factor of the symmetric positive definite fp32 A (lower triangle read; K a
     multiple of 256), row-major with exact zeros above the diagonal; info an int32 device scalar, 0 or the order of the
     first leading minor that is not positive (torch.linalg.cholesky_ex's convention; the factor is then not usable);
-    X = L^-1 (as tri_inv_lower) with inverse=True, else None.  overwrite=True factors a contiguous A in place.  On the
-    current stream, without host synchronisation."""
+    X = L^-1 (as tri_inv_lower) with inverse=True; with diag_inv=True instead the inverses of L's 256 x 256 diagonal
+    blocks [K / 256, 256, 256] (lower triangles; what chol_solve needs), as the leaves compute them; else None.
+    overwrite=True factors a contiguous A in place.  On the current stream, without host synchronisation."""
     _square_fp32_cuda(A, "cholesky_lower")
     K = A.shape[0]
     dev = A.device
     if not (overwrite and A.is_contiguous()):
         A = A.contiguous().clone() if A.is_contiguous() else A.contiguous()
+    if inverse and diag_inv:
+        raise ValueError("cholesky_lower: inverse and diag_inv are exclusive")
     info = torch.zeros(1, dtype=torch.int32, device=dev)
     X = torch.zeros_like(A) if inverse else None
+    D = torch.zeros((K // QK, QK, QK), dtype=torch.float32, device=dev) if diag_inv else None
     xt3 = torch.empty((QK, 3 * QK), dtype=torch.bfloat16, device=dev)  # the leaf's compact operand of L11^-1
     st = _stream(dev)
     L_ = _lib.lib()
     nb = K // QK
     for p in range(nb):
         c0, c1 = QK * p, QK * (p + 1)
-        _check(L_.ltq_chol256_diag(ptr(A), K, c0, ptr(xt3), ptr(X) if X is not None else None, K, ptr(info), st),
-               "ltq_chol256_diag")
+        if D is not None:  # the leaf's inverse into its own compact block (row stride 256)
+            _check(L_.ltq_chol256_diag(ptr(A), K, c0, ptr(xt3), ptr(D[p]), QK, ptr(info), st), "ltq_chol256_diag")
+        else:
+            _check(L_.ltq_chol256_diag(ptr(A), K, c0, ptr(xt3), ptr(X) if X is not None else None, K, ptr(info), st),
+                   "ltq_chol256_diag")
         if c1 == K:
             break
         m = K - c1
@@ -156,4 +163,19 @@ def cholesky_lower(A: torch.Tensor, inverse: bool = False, overwrite: bool = Fal
     A.tril_()
     if inverse:
         tri_inv_lower(A, X)
-    return A, info.view(()), X
+    return A, info.view(()), (D if diag_inv else X)
+
+
+def chol_solve(L: torch.Tensor, Dinv: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """x with L L^T x = b (src/liqk_v2.py:1163's solve of the refit system, factored by cholesky_lower with
+    diag_inv=True): block forward and backward substitution through the inverted diagonal blocks, 2 K / 256 launches
+    (ltq_chol_solve), no library kernel.  L [K, K] fp32 lower, Dinv [K / 256, 256, 256], b [K]; on the current stream."""
+    K = L.shape[0]
+    if L.dtype != torch.float32 or not L.is_cuda or L.stride(1) != 1 or Dinv.shape != (K // QK, QK, QK):
+        raise ValueError("chol_solve: an fp32 CUDA factor with unit column stride and its diagonal-block inverses")
+    b = b.float().contiguous()
+    x = torch.empty(K, dtype=torch.float32, device=L.device)
+    work = torch.empty(2 * K, dtype=torch.float32, device=L.device)
+    _check(_lib.lib().ltq_chol_solve(ptr(L), L.stride(0), K, ptr(Dinv.contiguous()), ptr(b), ptr(x), ptr(work),
+                                     _stream(L.device)), "ltq_chol_solve")
+    return x

@@ -25,7 +25,7 @@ import torch
 
 from . import _lib, tcgemm
 from ._lib import ptr
-from .hessian import cholesky_lower
+from .hessian import chol_solve, cholesky_lower
 from .formats import LIQK_V2_SPECS, QK_K, SUBBLOCK_SIZE, TCQ_CONFIG  # noqa: F401
 from .tcq_proto import make_gains
 
@@ -849,9 +849,9 @@ def _quantize_matrix_steps(W: torch.Tensor, H: torch.Tensor, spec_or_row_specs, 
     if gemm == "fp32":
         sol, solve_info = torch.linalg.solve_ex(A_in, b_in)
     else:
-        Lc, solve_info, _ = cholesky_lower(A_in, overwrite=True)
-        sol = torch.cholesky_solve(b_in.unsqueeze(1), Lc).squeeze(1)
-        del Lc
+        Lc, solve_info, Dinv = cholesky_lower(A_in, overwrite=True, diag_inv=True)
+        sol = chol_solve(Lc, Dinv, b_in)
+        del Lc, Dinv
     suh_cand = sol.to(torch.float16).to(torch.float32)
     valid_s = torch.isfinite(suh_cand) & (suh_cand.abs() > 0.05) & (suh_cand.abs() < 10.0)
     suh_cand = torch.where(valid_s, suh_cand, suh)

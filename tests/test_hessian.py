@@ -133,22 +133,33 @@ def test_cholesky_lower_accuracy(K, cuda_dev):
 
 
 @pytest.mark.gpu
-def test_cholesky_lower_solve_refit_system(cuda_dev):
-    """The refit system of the fast mode: A = (U^T U) o H + 1e-3 mean(diag) I, solved through the blocked factor and
-    torch.cholesky_solve, against fp64."""
-    from ltq_research_b200.hessian import cholesky_lower
-    K = 1024
+@pytest.mark.parametrize("K", [256, 1024, 3072])
+def test_cholesky_lower_solve_refit_system(K, cuda_dev):
+    """The refit system of the fast mode: A = (U^T U) o H + 1e-3 mean(diag) I, factored with the leaves' diagonal-block
+    inverses kept and solved by chol_solve (block substitution through those inverses, ltq_chol_solve), against fp64
+    and against torch.cholesky_solve on the same factor; the kept blocks invert L's diagonal blocks."""
+    from ltq_research_b200.hessian import chol_solve, cholesky_lower
     g = torch.Generator(device=cuda_dev).manual_seed(3)
     U = torch.randn(512, K, device=cuda_dev, generator=g)
     H = _damped_gram(K, 4, cuda_dev)
     A = (U.T @ U) * H
     A.diagonal().add_(1e-3 * A.diagonal().mean())
     b = torch.randn(K, device=cuda_dev, generator=g)
-    L, info, _ = cholesky_lower(A)
-    x = torch.cholesky_solve(b.unsqueeze(1), L).squeeze(1)
+    L, info, D = cholesky_lower(A, diag_inv=True)
+    assert int(info) == 0 and D.shape == (K // 256, 256, 256)
+    for p in range(K // 256):
+        Lp = L[256 * p:256 * (p + 1), 256 * p:256 * (p + 1)].double()
+        res = (torch.tril(D[p]).double() @ Lp - torch.eye(256, device=cuda_dev, dtype=torch.float64)).abs().max()
+        assert res.item() < 1e-4, (p, res.item())
+    x = chol_solve(L, D, b)
+    lib = torch.cholesky_solve(b.unsqueeze(1), L).squeeze(1)
     want = torch.linalg.solve(A.double(), b.double())
-    assert int(info) == 0
-    assert ((x.double() - want).norm() / want.norm()).item() < 1e-4
+    err = ((x.double() - want).norm() / want.norm()).item()
+    err_lib = ((lib.double() - want).norm() / want.norm()).item()
+    assert err < 1e-4 and err < 4 * err_lib + 1e-6, (err, err_lib)
+    assert torch.equal(chol_solve(L, D, b), x)  # deterministic
+    with pytest.raises(ValueError):
+        cholesky_lower(A, inverse=True, diag_inv=True)
 
 
 @pytest.mark.gpu
