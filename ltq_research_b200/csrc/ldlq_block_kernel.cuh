@@ -279,7 +279,10 @@ __device__ __forceinline__ void ldlq_tb(const VitParams& p, int n, unsigned char
 }
 
 template <class MP, int MD>
-__global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) ldlq_block_kernel(const __grid_constant__ LdlqParams q)
+// 128 registers a thread in every mode: for the plain mode the tighter cap of 85 (3 x 256 threads per SM) made the
+// compiler move register data around the branch-error row loads (measured: 12 % more instructions in the forward pass,
+// the isolated TCQ3X block 7.20 -> 6.93 ms with the looser cap, although one CTA fewer fits per SM)
+__global__ void __launch_bounds__(256, 2) ldlq_block_kernel(const __grid_constant__ LdlqParams q)
 {
     extern __shared__ __align__(16) unsigned char smem[];
     const int n = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x;

@@ -772,19 +772,11 @@ __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, un
     for (int t4 = 0, grp = 0;; t4 += 4, grp++, svp += gw4) {
         __syncwarp();
         read0(cur, src);
+        // each pair's two rows load just before the pair (loading the second pair's rows with the first pair's held
+        // 16 more registers over the first pair: 6 % more instructions in the plain mode, measured)
         ERow<EW> E0, E1;
         lrow(E0, 0, 0);
         lrow(E1, 1, 1);
-        // plain mode: the second pair's rows load with the first pair's, so their latency overlaps the first pair
-        // (measured: faster for plain, slower for the parity modes, whose units hold more registers)
-        constexpr bool EARLY_ROWS = MD == 0 && !SUB2;
-        ERow<EW> P2, P3;
-        if constexpr (EARLY_ROWS) {
-            if (t4 + 2 < T) {
-                lrow(P2, 2, 2);
-                lrow(P3, 3, 3);
-            }
-        }
         uint32_t wd[9];
         if constexpr (MD == 0) {
             wd[0] = pair_plain<0>(mp, cur, E0, E1);
@@ -806,13 +798,8 @@ __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, un
                 }
             }
             ERow<EW> E2, E3;
-            if constexpr (EARLY_ROWS) {
-                E2 = P2;
-                E3 = P3;
-            } else {
-                lrow(E2, 0, 2);
-                lrow(E3, 1, 3);
-            }
+            lrow(E2, 0, 2);
+            lrow(E3, 1, 3);
             if constexpr (MD == 0) {
                 wd[1] = pair_plain<2>(mp, cur, E2, E3);
             } else if constexpr (PP) {
@@ -885,9 +872,10 @@ __device__ __forceinline__ void vit_fwd_tile(const VitParams& p, const int n, un
     }
 }
 
-// Plain mode is capped at 85 registers (3 x 256 threads per SM) so that 6 four-slot tiles fit per SM.
+// 128 registers a thread: the plain mode at the tighter cap of 85 (6 four-slot tiles per SM) spent 12 % more
+// instructions on register moves around the branch-error row loads and ran 5 % slower than with 4 tiles per SM.
 template <class MP, int MD, bool SUB2>
-__global__ void __launch_bounds__(256, MD == 0 ? 3 : 2) vit_fwd_kernel(const VitParams p)
+__global__ void __launch_bounds__(256, 2) vit_fwd_kernel(const VitParams p)
 {
     extern __shared__ __align__(16) unsigned char smem[];
     const int n = blockIdx.x;
