@@ -279,10 +279,11 @@ __device__ __forceinline__ void ldlq_tb(const VitParams& p, int n, unsigned char
 }
 
 template <class MP, int MD>
-// 128 registers a thread in every mode: for the plain mode the tighter cap of 85 (3 x 256 threads per SM) made the
-// compiler move register data around the branch-error row loads (measured: 12 % more instructions in the forward pass,
-// the isolated TCQ3X block 7.20 -> 6.93 ms with the looser cap, although one CTA fewer fits per SM)
-__global__ void __launch_bounds__(256, 2) ldlq_block_kernel(const __grid_constant__ LdlqParams q)
+// Register caps (a CTA has 32 G <= 128 threads): 128 a thread for the plain mode — at the tighter cap of 85 (3 x 256
+// threads per SM) the compiler moved register data around the branch-error row loads (12 % more instructions in the
+// forward pass; isolated TCQ3X block 7.20 -> 6.93 ms with 128, although fewer CTAs fit per SM; 7.33 ms at 96);
+// 168 for the parity modes, whose class planes spilled at 128 (TCQ25X block 6.45 -> 6.18 ms; 6.94 ms uncapped)
+__global__ void __launch_bounds__(MD == 0 ? 256 : 192, 2) ldlq_block_kernel(const __grid_constant__ LdlqParams q)
 {
     extern __shared__ __align__(16) unsigned char smem[];
     const int n = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x;
