@@ -513,10 +513,11 @@ __device__ __forceinline__ void phase_b(const MP& mp, const float (&o0)[32], con
 // sub-block gain merge (src/cuda/tcq_viterbi.cu:185-201), in state space over the exchange regions of all G slots:
 // every state continues from its best slot (strict <, lowest slot wins).  The merged metrics go to one region that
 // every slot reads next; the winners are 4-bit codes, 8 states per word (word s >> 3, nibble s & 7).  Thread i of the
-// CTA handles states 8i .. 8i + 7 (two 16-byte chunks per region).  Kept out of line: it runs once per sub-block.
+// CTA handles states 8i .. 8i + 7 (two 16-byte chunks per region).  Inline: with the register caps of the kernels
+// that call it, the out-of-line call cost 0.5 % of the fused kernel's time (measured).
 // ------------------------------------------------------------------------------------------------
 template <int G>
-static __device__ __noinline__ void merge_slots(const float* s_dp, float* s_mg, uint32_t* gw)
+static __device__ __forceinline__ void merge_slots(const float* s_dp, float* s_mg, uint32_t* gw)
 {
     for (int i = threadIdx.x; i < NS / 8; i += 32 * G) {
         const int a0 = swz(8 * i), a1 = swz(8 * i + 4);
