@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(MD == 0 ? 256 : 192, 2) ldlq_block_kernel(cons
 #pragma unroll 1
         for (int ps = 0; ps < 2; ps++) {
             const VitParams& pp = ps ? q.p2 : q.p1;
-            vit_fwd_tile<MP, MD, false>(pp, n, smem, xr, wr);
+            vit_fwd_tile<MP, MD, false, true>(pp, n, smem, xr, wr);
             __threadfence();
             __syncthreads();
             ldlq_tb<MP, MD>(pp, n, smem, q.fb_off, xr);
