@@ -325,6 +325,7 @@ def gemm_ldlq_compare(dev) -> dict:
     from ltq_research_b200 import _lib
     L = _lib.lib()
     st = torch.cuda.current_stream(dev).cuda_stream
+    peaks = measured_peaks()
 
     def med_us(fn):
         return _event_ms(lambda: [fn() for _ in range(5)], reps=10) / 5 * 1e3
@@ -340,8 +341,9 @@ def gemm_ldlq_compare(dev) -> dict:
         tc = med_us(lambda: L.ltq_gemm_bf16x6_tn(A3.data_ptr(), 768, B3.data_ptr(), 768, C.data_ptr(), N, M, N, 256,
                                                   -1.0, 1.0, None, st))
         cb = med_us(lambda: torch.addmm(C, A6, B6.T, beta=1, alpha=-1, out_dtype=torch.float32, out=C))
-        res[f"{M}x{N}"] = {"tcgen05_us": round(tc, 1), "cublas_us": round(cb, 1),
-                           "tcgen05_tflops": round(2 * M * N * 1536 / (tc * 1e-6) / 1e12, 1)}
+        tf = 2 * M * N * 1536 / (tc * 1e-6) / 1e12
+        res[f"{M}x{N}"] = {"tcgen05_us": round(tc, 1), "cublas_us": round(cb, 1), "tcgen05_tflops": round(tf, 1),
+                           "frac_of_bf16_burst": round(tf / peaks["bf16_tflops"], 3) if peaks.get("bf16_tflops") else None}
     return res
 
 
