@@ -882,6 +882,9 @@ def main():
     ap.add_argument("--profile-viterbi", default=None, metavar="FORMAT",
                     help="three stand-alone two-pass Viterbi calls (ltq_viterbi_tb) of FORMAT over the --rows / 16 "
                          "tiles of one sub-block, for ncu captures of vit_fwd_kernel")
+    ap.add_argument("--profile-gemm", action="store_true",
+                    help="the tcgen05 six-product GEMM of the LDLQ update at 8192 x 2816 and 8192 x 7936 (K = 3 x 256), "
+                         "three launches each, untimed, for ncu captures")
     ap.add_argument("--profile-hbm", action="store_true",
                     help="the HBM-bound kernels (FWHT-256, scale fit, pack, verify decode) on a 16384 x 4096 matrix, "
                          "three launches each, untimed, for ncu captures")
@@ -916,6 +919,22 @@ def main():
 
     if args.aux:
         print(json.dumps(aux_measurements(dev, fmts)), flush=True)
+        return
+    if args.profile_gemm:
+        from ltq_research_b200 import _lib
+        L = _lib.lib()
+        st = torch.cuda.current_stream(dev).cuda_stream
+        g = torch.Generator(device=dev).manual_seed(9)
+        for M, N in ((8192, 2816), (8192, 7936)):
+            A3 = torch.randn(M, 768, device=dev, generator=g).to(torch.bfloat16)
+            B3 = torch.randn(N, 768, device=dev, generator=g).to(torch.bfloat16)
+            C = torch.randn(M, N, device=dev, generator=g)
+            for _ in range(3):
+                rc = L.ltq_gemm_bf16x6_tn(A3.data_ptr(), 768, B3.data_ptr(), 768, C.data_ptr(), N, M, N, 256, -1.0, 1.0,
+                                          None, st)
+                assert rc == 0, rc
+        torch.cuda.synchronize()
+        print("profile run: tcgen05 LDLQ-update GEMM, 8192 x 2816 and 8192 x 7936, 3 launches each", flush=True)
         return
     if args.profile_hbm:
         hbm_kernels(dev, fmts["TCQ3X"], reps=3, timed=False)
