@@ -17,7 +17,9 @@
 //   all four warps     epilogue: warp w reads lanes 32 w .. 32 w + 31 (rows of the tile) with tcgen05.ld; for beta 0 / 1
 //                      32 x 32 boxes go through swizzled shared buffers to a TMA store (beta 0) or a TMA reduce-add
 //                      into C (beta 1), so C is never read by the SMs; any other beta reads and writes C row by row.
-// gemm_bf16x3p_tn_kernel (below) is the same pipeline over compact three-part operands, batched over blockIdx.z.
+// gemm_bf16x3p_tn_kernel (below) is the same pipeline over compact three-part operands, batched over blockIdx.z;
+// gemm_bf16x3p_tn_persist runs its beta 0 / 1 products of more tiles than SMs, one CTA per SM walking the tiles with a
+// double-buffered accumulator so that epilogue and operand loads overlap the MMAs (bit-identical results).
 // Every wait on an mbarrier is bounded: after GEMM_WAIT_LIMIT polls the thread records a timeout in *err (when given)
 // and leaves its loop; the CTA still meets at its final barrier and frees its tensor memory.  No cluster, no multicast:
 // every TMA load reads this GPU's own memory.
@@ -32,6 +34,9 @@ namespace {
 
 #ifndef LTQ_GEMM_BN
 #define LTQ_GEMM_BN 256
+#endif
+#ifndef LTQ_GEMM_PERSIST
+#define LTQ_GEMM_PERSIST 1  // beta 0 / 1 products of ltq_gemm_bf16x3p_tn on the persistent kernel
 #endif
 #ifndef LTQ_GEMM_STAGES
 #define LTQ_GEMM_STAGES 2
@@ -491,6 +496,208 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return f;
 }
 
+// Persistent form of gemm_bf16x3p_tn_kernel for beta 0 / 1 (TMA store / reduce-add epilogue): one CTA per SM walks
+// the tiles (tile t: batch z, row block, column block; t += gridDim.x) with warp-specialised roles,
+//   warp 0 lane 0   TMA producer, the A / B rings of the one-tile kernel continued across tiles;
+//   warp 1 lane 0   MMA issuer into one of two 256-column accumulators in tensor memory (512 columns), tile i into
+//                   accumulator i & 1, once the epilogue has released it (accempty), then accfull;
+//   warps 2 .. 5    epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (its lane quarter), stages 32 x 32
+//                   boxes in its own 8 KB of shared memory and stores / adds them with TMA, then releases the
+//                   accumulator —
+// so the epilogue of tile i and the operand loads of tile i + 1 overlap the MMAs instead of following them.  Every wait
+// is bounded (GEMM_WAIT_LIMIT polls, then *err = 1 and the role stops); the CTA still meets at its last barrier.
+constexpr int PERSIST_STAGE = 4 * 8192;  // epilogue staging: 4 warps x two 4 KB boxes
+constexpr int SMEM6P_BYTES = 2 * A3_BYTES + 3 * B_BYTES + PERSIST_STAGE + 1024 + 256;
+
+__global__ void __launch_bounds__(192, 1) gemm_bf16x3p_tn_persist(const __grid_constant__ CUtensorMap tmA,
+                                                                  const __grid_constant__ CUtensorMap tmB,
+                                                                  const __grid_constant__ CUtensorMap tmC,
+                                                                  const GemmParams p, const int reduce, const int Kp,
+                                                                  const int nq, const int mt, const int ntl,
+                                                                  const int ntiles)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sa = smem;                   // 2 A buffers of nq parts
+    uint8_t* sb = smem + 2 * A3_BYTES;    // B stages (stage q = part q)
+    uint8_t* sst = sb + 3 * B_BYTES;      // epilogue staging
+    uint64_t* afull = reinterpret_cast<uint64_t*>(sst + PERSIST_STAGE);
+    uint64_t* aempty = afull + 2;
+    uint64_t* bfull = aempty + 2;
+    uint64_t* bempty = bfull + 3;
+    uint64_t* accfull = bempty + 3;
+    uint64_t* accempty = accfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nk = Kp / BK;
+
+    if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmB) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmC) : "memory");
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&afull[i], 1);
+            mbar_init(&aempty[i], 1);
+            mbar_init(&accfull[i], 1);
+            mbar_init(&accempty[i], 4);  // one arrival per epilogue warp
+        }
+        for (int i = 0; i < 3; i++) {
+            mbar_init(&bfull[i], 1);
+            mbar_init(&bempty[i], 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto tile_of = [&](int t, int& m0, int& n0, int& z) {
+        z = t / (mt * ntl);
+        const int r = t - z * mt * ntl;
+        n0 = (r / mt) * BN;  // consecutive tiles share a column block (its B operand stays in L2)
+        m0 = (r % mt) * BM;
+    };
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer; g counts chunks over all of this CTA's tiles
+            int g = 0, ga = 0, lastb[3] = {-1, -1, -1};
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                int m0, n0, z;
+                tile_of(t, m0, n0, z);
+                for (int j = 0; j < nk && ok; j++, g++) {
+                    const int a = g & 1;
+                    if (g >= 2 && !mbar_wait(&aempty[a], ((g >> 1) - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&afull[a], nq * A_BYTES);
+                    for (int pt = 0; pt < nq; pt++)
+                        tma_load_3d(sa + a * A3_BYTES + pt * A_BYTES, &tmA, pt * Kp + j * BK, m0, z, &afull[a]);
+                    ga = g + 1;
+#pragma unroll
+                    for (int q = 0; q < 3; q++) {
+                        if (q >= nq) break;
+                        if (g >= 1 && !mbar_wait(&bempty[q], (g - 1) & 1, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(&bfull[q], B_BYTES);
+                        tma_load_3d(sb + q * B_BYTES, &tmB, q * Kp + j * BK, n0, z, &bfull[q]);
+                        lastb[q] = g;
+                    }
+                }
+            }
+            // every copy started has landed before the CTA can leave
+            for (int h = ga > 2 ? ga - 2 : 0; h < ga; h++) mbar_wait(&afull[h & 1], (h >> 1) & 1, p.err);
+#pragma unroll
+            for (int q = 0; q < 3; q++)
+                if (lastb[q] >= 0) mbar_wait(&bfull[q], lastb[q] & 1, p.err);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            int g = 0, i = 0, last = -1;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, i++) {
+                const int acc = i & 1;
+                if (i >= 2 && !mbar_wait(&accempty[acc], ((i >> 1) - 1) & 1, p.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * BN);
+                bool first = true;
+                for (int j = 0; j < nk && ok; j++, g++) {
+                    const int a = g & 1;
+                    if (!mbar_wait(&afull[a], (g >> 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t abase = smem_u32(sa + a * A3_BYTES);
+                    for (int q = 0; q < nq; q++) {
+                        if (!mbar_wait(&bfull[q], g & 1, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t bq = smem_u32(sb + q * B_BYTES);
+                        for (int pt = 0; pt < nq - q; pt++) {
+                            const uint32_t ap = abase + pt * A_BYTES;
+#pragma unroll
+                            for (int kk = 0; kk < BK / 16; kk++) {
+                                umma_bf16(d, sw128_kmajor_desc(ap + 32 * kk), sw128_kmajor_desc(bq + 32 * kk),
+                                          first ? 0u : 1u);
+                                first = false;
+                            }
+                        }
+                        umma_commit(&bempty[q]);
+                    }
+                    if (ok) umma_commit(&aempty[a]);
+                }
+                umma_commit(&accfull[acc]);  // arrives when every MMA issued so far has completed
+                last = i;
+            }
+            // no MMA may still write tensor memory when the CTA frees it
+            if (last >= 0) mbar_wait(&accfull[last & 1], (last >> 1) & 1, p.err);
+        }
+        __syncwarp();
+    } else {  // epilogue warps: lane quarter qr of tensor memory, rows m0 + 32 qr .. + 31
+        const int qr = warp & 3;
+        uint8_t* wbuf = sst + (warp - 2) * 8192;
+        int nbox = 0, i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+            int m0, n0, z;
+            tile_of(t, m0, n0, z);
+            const int acc = i & 1;
+            const bool ok = mbar_wait(&accfull[acc], (i >> 1) & 1, p.err);
+            __syncwarp();
+            tc_fence_after();
+            if (!ok) break;
+            const uint32_t tl = tmem + ((uint32_t)(32 * qr) << 16) + (uint32_t)(acc * BN);
+            for (int c = 0; c < BN; c += 32) {
+                if (n0 + c >= p.N) break;  // warp-uniform
+                float v[16], w[16];
+                tmem_ld16(tl + c, v);
+                tmem_ld16(tl + c + 16, w);
+                uint8_t* buf = wbuf + (nbox & 1) * 4096;
+                if (nbox >= 2) {  // the box stored from this buffer two boxes ago has been read out of shared memory
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
+                    __syncwarp();
+                }
+                uint8_t* row = buf + lane * 128;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    *reinterpret_cast<float4*>(row + ((q ^ (lane & 7)) << 4)) = make_float4(
+                        p.alpha * v[4 * q], p.alpha * v[4 * q + 1], p.alpha * v[4 * q + 2], p.alpha * v[4 * q + 3]);
+                    *reinterpret_cast<float4*>(row + (((q + 4) ^ (lane & 7)) << 4)) = make_float4(
+                        p.alpha * w[4 * q], p.alpha * w[4 * q + 1], p.alpha * w[4 * q + 2], p.alpha * w[4 * q + 3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                __syncwarp();
+                if (lane == 0) tma_store_box(&tmC, buf, n0 + c, m0 + 32 * qr, z, reduce != 0);
+                nbox++;
+            }
+            // this warp's reads of the accumulator are complete (tcgen05.wait::ld): hand it back to the MMA issuer
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&accempty[acc])) : "memory");
+        }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(512) : "memory");
+    }
+}
+static_assert(2 * BN == 512, "two accumulators of BN columns fill the 512 columns of tensor memory");
+static_assert(SMEM6P_BYTES <= 232448, "shared memory of one CTA");
 // 3-D tensor map of the fp32 output C [batch][rows, cols] (row stride ld, batch stride bs elements) for the epilogue's
 // {32 x 32 x 1} boxes, 128-byte swizzle
 bool make_map_c(CUtensorMap* m, const float* base, int rows, int cols, long long ld, int batch, long long bs)
@@ -591,11 +798,15 @@ extern "C" int ltq_gemm_bf16x3p_tn(const uint16_t* A3, long long lda, long long 
     if (!make_map3(&ta, A3, M, nq * Kp, lda, batch, abs_, BM) || !make_map3(&tb, B3, N, nq * Kp, ldb, batch, bbs, BN))
         return -1;
     static std::atomic<int> attr_set[64];
+    static int sm_count[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
     if (!attr_set[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(gemm_bf16x3p_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM6_BYTES) !=
-            cudaSuccess)
+                cudaSuccess ||
+            cudaFuncSetAttribute(gemm_bf16x3p_tn_persist, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 SMEM6P_BYTES) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             return -1;
         attr_set[dev].store(1, std::memory_order_release);
     }
@@ -603,8 +814,16 @@ extern "C" int ltq_gemm_bf16x3p_tn(const uint16_t* A3, long long lda, long long 
     CUtensorMap tc{};
     if (cm && !make_map_c(&tc, C, M, N, ldc, batch, cbs)) return -1;
     GemmParams p{C, ldc, cbs, M, N, Kp, alpha, beta, err};
-    dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, batch);
-    gemm_bf16x3p_tn_kernel<<<grid, 128, SMEM6_BYTES, (cudaStream_t)stream>>>(ta, tb, tc, p, cm, Kp, nq);
+    const int mt = (M + BM - 1) / BM, ntl = (N + BN - 1) / BN;
+    const long long ntiles = 1LL * mt * ntl * batch;
+    // more tiles than SMs: the persistent kernel (one wave is faster on the one-tile kernel, which starts lighter)
+    if (cm && LTQ_GEMM_PERSIST && ntiles > sm_count[dev] && ntiles < (1LL << 31)) {
+        gemm_bf16x3p_tn_persist<<<sm_count[dev], 192, SMEM6P_BYTES, (cudaStream_t)stream>>>(ta, tb, tc, p, cm == 2, Kp, nq, mt,
+                                                                                   ntl, (int)ntiles);
+    } else {
+        dim3 grid(mt, ntl, batch);
+        gemm_bf16x3p_tn_kernel<<<grid, 128, SMEM6_BYTES, (cudaStream_t)stream>>>(ta, tb, tc, p, cm, Kp, nq);
+    }
     return (int)cudaGetLastError();
 }
 

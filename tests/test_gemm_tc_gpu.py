@@ -86,7 +86,10 @@ def _six(X3, Kp, order):
     return torch.cat([p[i] for i in idx], dim=1).contiguous()
 
 
-@pytest.mark.parametrize("M,N,Kp", [(16, 16, 64), (1040, 272, 256), (300, 2816, 256), (2048, 512, 128)])
+# (2600, 4112, 128): 21 x 17 = 357 tiles, more than the SMs, so the beta 0 / 1 products run on the persistent kernel
+# (CTAs walking two or three tiles each, a 16-column tail block)
+@pytest.mark.parametrize("M,N,Kp", [(16, 16, 64), (1040, 272, 256), (300, 2816, 256), (2048, 512, 128),
+                                    (2600, 4112, 128)])
 def test_gemm6_exact_on_small_integers(cuda_dev, M, N, Kp):
     g = torch.Generator(device=cuda_dev).manual_seed(M + 3 * N + Kp)
     A3 = torch.randint(-3, 4, (M, 3 * Kp), generator=g, device=cuda_dev).to(torch.bfloat16)
@@ -209,13 +212,14 @@ def test_split3_layout(cuda_dev, trans, neg):
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
 
-@pytest.mark.parametrize("nq", [2, 3])
-def test_gemm3_batched_exact(cuda_dev, nq):
+@pytest.mark.parametrize("nq,batch", [(2, 3), (3, 3), (3, 50)])
+def test_gemm3_batched_exact(cuda_dev, nq, batch):
     """Batched part GEMM on small integers into strided C views: beta 0 (TMA store), 1 (TMA reduce-add), 0.5
-    (read-modify-write), exactly the integer sum of the nq (nq + 1) / 2 products."""
+    (read-modify-write), exactly the integer sum of the nq (nq + 1) / 2 products.  Batch 50 is 200 tiles, more than
+    the SMs: its beta 0 / 1 products run on the persistent kernel."""
     from ltq_research_b200.tcgemm import gemm3
-    g = torch.Generator(device=cuda_dev).manual_seed(10 + nq)
-    batch, M, N, Kp = 3, 200, 272, 128
+    g = torch.Generator(device=cuda_dev).manual_seed(10 + nq + batch)
+    M, N, Kp = 200, 272, 128
     A3 = torch.randint(-3, 4, (batch, M, 3 * Kp), generator=g, device=cuda_dev).to(torch.bfloat16)
     B3 = torch.randint(-3, 4, (batch, N, 3 * Kp), generator=g, device=cuda_dev).to(torch.bfloat16)
     a = [A3[:, :, i * Kp:(i + 1) * Kp].double() for i in range(3)]
