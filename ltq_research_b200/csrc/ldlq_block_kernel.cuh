@@ -97,7 +97,7 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
     uint32_t* cbits = buf + 2 * bufw;
     uint8_t* sg = reinterpret_cast<uint8_t*>(cbits + MAXT / 32);
     uint8_t* spar = sg + 32;
-    int* flag = reinterpret_cast<int*>(spar + MAXT);  // [0] state, [1] slot, [3] state at t = 0
+    int* flag = reinterpret_cast<int*>(spar + MAXT);  // [3] state at t = 0
 
     // stage chunk c (all slots' words — per_slot consecutive words per slot in the survivor stream — and the merge
     // winners of boundary c) into buffer b with 16-byte asynchronous copies by threads t0, t0 + ts, ...
@@ -112,10 +112,11 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
             for (int k = t0; k < NS / 32; k += ts) cp_async16(d + 4 * k, gsrc + 4 * k);
         }
     };
+    int wst = 0, wgs = 0;  // thread 0: the walk's state and gain slot, carried from chunk to chunk in registers
     if (tid == 0) {
         const int bi = p.best[n];
-        flag[0] = bi % NS;
-        flag[1] = bi / NS;
+        wst = bi % NS;
+        wgs = bi / NS;
     }
     // the last chunk by every thread; then, while thread 0 walks chunk c, the staging threads (the warps that do not
     // walk, or lanes 1..31 when there is one warp) copy chunk c - 1 into the other buffer
@@ -129,10 +130,9 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
         const int b = c & 1, lo = c * sub;
         if (stager && c > 0) stage(c - 1, b ^ 1, G > 1 ? tid - 32 : tid - 1, G > 1 ? nthr - 32 : nthr - 1);
         if (tid == 0) {
-            int st = flag[0];
-            const int gs = flag[1];
-            sg[c] = (uint8_t)gs;
-            const uint32_t* B = buf + b * bufw + gs * per_slot;
+            int st = wst;
+            sg[c] = (uint8_t)wgs;
+            const uint32_t* B = buf + b * bufw + wgs * per_slot;
             uint32_t acc = 0;
             bool stop = false, done = false;
             for (int gl = NGRP - 1; gl >= 0 && !done; gl--) {
@@ -244,10 +244,10 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
             }
             if (sub == 32) cbits[c] = acc;
             else reinterpret_cast<uint16_t*>(cbits)[c] = (uint16_t)acc;
-            flag[0] = st;
+            wst = st;
             stopped = stop;
             if (!stop && G > 1 && c > 0)  // the walk ended at the chunk's first step: the slot of the previous chunk
-                flag[1] = (int)((buf[b * bufw + G * per_slot + (st >> 3)] >> (4 * (st & 7))) & 15u);
+                wgs = (int)((buf[b * bufw + G * per_slot + (st >> 3)] >> (4 * (st & 7))) & 15u);
         }
         cp_async_wait_all();
         // the stop travels with the barrier (bar.red.or): a flag in shared memory read after the barrier could already
