@@ -149,64 +149,12 @@ __device__ __forceinline__ void tb_coop(const VitParams& p, const int n, unsigne
 #pragma unroll
                 for (int k = 0; k < W4C; k++) w[k] = Wg[32 * k];
                 {
-                    // a group with neither the first-pass middle nor t = 0: the same steps on the butterfly index
-                    // b = r >> 1, each b' = (b >> 1) | (decision bit << 3) with the decision half-word pre-shifted by 3
-                    // (plain: two dependent instructions a step; parity modes: every candidate half extracted while
-                    // the class bits are read, then selects).  The group's code bits r & 1 at steps 3, 2, 1, 0 are
-                    // bits 0, 1, 2, 3 of the group's first r (each step shifts r down by one).
+                    // a group with neither the first-pass middle nor t = 0: tb_walk_group, its code bits from the
+                    // entry register
                     const int tg = lo + 4 * gl;
                     if (tg != 0 && !(p.mid_st && (unsigned)(p.mid_t - 1 - tg) < 4u)) {
                         acc |= (__brev((uint32_t)r & 15u) >> 28) << (tg - lo);
-                        uint32_t b = (uint32_t)r >> 1;
-                        if constexpr (MD == 0) {
-                            b = (b >> 1) | (((w[1] << 3) >> b) & 8u);
-                            b = (b >> 1) | ((((w[1] >> 16) << 3) >> b) & 8u);
-                            b = (b >> 1) | (((w[0] << 3) >> b) & 8u);
-                        } else if constexpr (PP) {
-                            // step 3: class bit of the pair from w[4] at r, decision from the half of w[3] it picks
-                            const uint32_t c3 = (w[4] >> r) & 1u;
-                            const uint32_t lo3 = ((w[3] << 3) >> b) & 8u, hi3 = (((w[3] >> 16) << 3) >> b) & 8u;
-                            spar[tg + 3] = spar[tg + 2] = (uint8_t)c3;
-                            b = (b >> 1) | (c3 ? lo3 : hi3);
-                            // step 2: low half of w[0]; the full register r of step 1 for its class bit
-                            const uint32_t r1 = b | (((w[0] << 4) >> b) & 16u);
-                            b = r1 >> 1;
-                            // step 1: class bit from w[2] at r1, decision from the half of w[1] it picks
-                            const uint32_t c1 = (w[2] >> r1) & 1u;
-                            const uint32_t lo1 = ((w[1] << 3) >> b) & 8u, hi1 = (((w[1] >> 16) << 3) >> b) & 8u;
-                            spar[tg + 1] = spar[tg] = (uint8_t)c1;
-                            pcur = (int)c1;
-                            b = (b >> 1) | (c1 ? lo1 : hi1);
-                        } else {
-                            // step 3: quad class c (w[7]) and pair bit (w[8]) at r pick the half of w[5] / w[6]
-                            const uint32_t c3 = (w[7] >> r) & 1u, p3 = (w[8] >> r) & 1u;
-                            const uint32_t wq = c3 ? w[6] : w[5];
-                            const uint32_t lo3 = ((wq << 3) >> b) & 8u, hi3 = (((wq >> 16) << 3) >> b) & 8u;
-                            cstar = (int)c3;
-                            if (EQ) {
-                                spar[tg + 3] = spar[tg + 2] = spar[tg + 1] = spar[tg] = (uint8_t)c3;
-                            } else {
-                                spar[tg + 3] = (uint8_t)(p3 ^ c3);
-                                spar[tg + 2] = (uint8_t)p3;
-                            }
-                            b = (b >> 1) | (p3 ? lo3 : hi3);
-                            // step 2: the half of w[4] picked by the quad class; the full register r of step 1
-                            const uint32_t r1 = b | ((((c3 ? w[4] : (w[4] >> 16)) << 4) >> b) & 16u);
-                            b = r1 >> 1;
-                            // step 1: pair bit from w[2] / w[3] (by the quad class) at r1 picks the half of w[1]
-                            const uint32_t p1 = ((c3 ? w[3] : w[2]) >> r1) & 1u;
-                            const uint32_t lo1 = ((w[1] << 3) >> b) & 8u, hi1 = (((w[1] >> 16) << 3) >> b) & 8u;
-                            if (!EQ) {
-                                spar[tg + 1] = (uint8_t)(p1 ^ c3);
-                                spar[tg] = (uint8_t)p1;
-                            }
-                            b = (b >> 1) | (p1 ? lo1 : hi1);
-                            // step 0: low half of w[0]
-                            r = (int)(b | (((w[0] << 4) >> b) & 16u));
-                            st = L | (r << 5);
-                            continue;
-                        }
-                        r = (int)(b | ((((w[0] >> 16) << 4) >> b) & 16u));  // step 0: high half of w[0]
+                        r = tb_walk_group<MD>(w, r, spar, tg, pcur, cstar);
                         st = L | (r << 5);
                         continue;
                     }

@@ -887,6 +887,72 @@ __global__ void __launch_bounds__(256, 2) vit_fwd_kernel(const VitParams p)
 }
 
 // ------------------------------------------------------------------------------------------------
+// One 4-step group of a traceback walk (steps tg + 3 .. tg, none of them the first pass's stop or t = 0), for both
+// traceback kernels.  `w` holds the group's survivor words of lane column L (bits 4..8 of the state at step tg + 3) and
+// r that state's register in layout 4, ((s >> 9) << 4) | (s & 15).  The walk runs on the butterfly index b = r >> 1:
+// each step b' = (b >> 1) | (decision bit << 3), with the decision half-word pre-shifted by 3, so a plain-mode step is
+// one variable shift (beside b >> 1) and one LOP3; the parity modes extract every candidate half while their class bits
+// are read, then select.  Writes the parity class of the group's steps to par[tg .. tg + 3] (D2 / D4 / EQ) and returns
+// the register of the state before step tg, in layout 4 of the previous group; that state is L | r << 5.  The group's
+// code bits (r & 1 at steps 3, 2, 1, 0) are bits 0, 1, 2, 3 of the entry r: each step shifts r down by one.
+// Same decisions as the per-step walk (the decision bit h of step j picks the predecessor register (r >> 1) | h << 4).
+// ------------------------------------------------------------------------------------------------
+template <int MD>
+__device__ __forceinline__ int tb_walk_group(const uint32_t* w, const int r, uint8_t* par, const int tg, int& pcur,
+                                             int& cstar)
+{
+    constexpr bool PP = MD == 1, EQ = MD == 3;
+    uint32_t b = (uint32_t)r >> 1;
+    if constexpr (MD == 0) {
+        b = (b >> 1) | (((w[1] << 3) >> b) & 8u);
+        b = (b >> 1) | ((((w[1] >> 16) << 3) >> b) & 8u);
+        b = (b >> 1) | (((w[0] << 3) >> b) & 8u);
+        return (int)(b | ((((w[0] >> 16) << 4) >> b) & 16u));  // step 0: high half of w[0]
+    } else if constexpr (PP) {
+        // step 3: class bit of the pair from w[4] at r, decision from the half of w[3] it picks
+        const uint32_t c3 = (w[4] >> r) & 1u;
+        const uint32_t lo3 = ((w[3] << 3) >> b) & 8u, hi3 = (((w[3] >> 16) << 3) >> b) & 8u;
+        par[tg + 3] = par[tg + 2] = (uint8_t)c3;
+        b = (b >> 1) | (c3 ? lo3 : hi3);
+        // step 2: low half of w[0]; the full register r of step 1 for its class bit
+        const uint32_t r1 = b | (((w[0] << 4) >> b) & 16u);
+        b = r1 >> 1;
+        // step 1: class bit from w[2] at r1, decision from the half of w[1] it picks
+        const uint32_t c1 = (w[2] >> r1) & 1u;
+        const uint32_t lo1 = ((w[1] << 3) >> b) & 8u, hi1 = (((w[1] >> 16) << 3) >> b) & 8u;
+        par[tg + 1] = par[tg] = (uint8_t)c1;
+        pcur = (int)c1;
+        b = (b >> 1) | (c1 ? lo1 : hi1);
+        return (int)(b | ((((w[0] >> 16) << 4) >> b) & 16u));  // step 0: high half of w[0]
+    } else {
+        // step 3: quad class c (w[7]) and pair bit (w[8]) at r pick the half of w[5] / w[6]
+        const uint32_t c3 = (w[7] >> r) & 1u, p3 = (w[8] >> r) & 1u;
+        const uint32_t wq = c3 ? w[6] : w[5];
+        const uint32_t lo3 = ((wq << 3) >> b) & 8u, hi3 = (((wq >> 16) << 3) >> b) & 8u;
+        cstar = (int)c3;
+        if (EQ) {
+            par[tg + 3] = par[tg + 2] = par[tg + 1] = par[tg] = (uint8_t)c3;
+        } else {
+            par[tg + 3] = (uint8_t)(p3 ^ c3);
+            par[tg + 2] = (uint8_t)p3;
+        }
+        b = (b >> 1) | (p3 ? lo3 : hi3);
+        // step 2: the half of w[4] picked by the quad class; the full register r of step 1
+        const uint32_t r1 = b | ((((c3 ? w[4] : (w[4] >> 16)) << 4) >> b) & 16u);
+        b = r1 >> 1;
+        // step 1: pair bit from w[2] / w[3] (by the quad class) at r1 picks the half of w[1]
+        const uint32_t p1 = ((c3 ? w[3] : w[2]) >> r1) & 1u;
+        const uint32_t lo1 = ((w[1] << 3) >> b) & 8u, hi1 = (((w[1] >> 16) << 3) >> b) & 8u;
+        if (!EQ) {
+            par[tg + 1] = (uint8_t)(p1 ^ c3);
+            par[tg] = (uint8_t)p1;
+        }
+        b = (b >> 1) | (p1 ? lo1 : hi1);
+        return (int)(b | (((w[0] << 4) >> b) & 16u));  // step 0: low half of w[0]
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
 // traceback, reconstruction and codes (src/cuda/tcq_viterbi.cu:580-682), one warp per tile
 // ------------------------------------------------------------------------------------------------
 // Traceback of tile n by one warp.  Tables and gains are in shared memory (s_tab ...); `wbase` is the warp's region of
@@ -930,6 +996,28 @@ __device__ __forceinline__ void vit_tb_tile(const VitParams& p, const int n, con
             int st = s_flag[0], gs = s_flag[1], pcur = 0, cstar = 0;
             bool stop = false;
             for (int t = lo + sub - 1; t >= lo; t--) {
+                // a whole 4-step group inside this sub-block, without the first pass's stop or t = 0: the group walk;
+                // the states of its steps are the 10-bit windows of V = (state before the group) << 4 | (s_t & 15)
+                if ((t & 3) == 3 && t - 3 >= lo && t != 3 && !(p.mid_st && (unsigned)(p.mid_t - 1 - (t - 3)) < 4u)) {
+                    constexpr int W4C = MD == 0 ? 2 : (MD == 1 ? 5 : 9);
+                    const int L = (st >> 4) & 31;
+                    const uint32_t* Wg = s_tbw + ((t >> 2) - grp0) * p.W4 * 32 + L;
+                    uint32_t w[W4C];
+#pragma unroll
+                    for (int k = 0; k < W4C; k++) w[k] = Wg[32 * k];
+                    const int rn = tb_walk_group<MD>(w, ((st >> 9) << 4) | (st & 15), s_par, t - 3, pcur, cstar);
+                    const int stn = L | (rn << 5);
+                    const int V = (stn << 4) | (st & 15);
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        s_st[t - k] = (uint16_t)((V >> k) & 1023);
+                        s_sg[t - k] = (uint8_t)gs;
+                    }
+                    st = stn;
+                    t -= 3;  // the loop's t-- moves on to the step before the group
+                    if (G > 1 && t == lo) gs = (int)((s_tbg[st >> 3] >> (4 * (st & 7))) & 15u);
+                    continue;
+                }
                 s_st[t] = (uint16_t)st;
                 s_sg[t] = (uint8_t)gs;
                 const int j = t & 3;
