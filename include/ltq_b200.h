@@ -190,7 +190,9 @@ int ltq_gemm_bf16x6_tn(const uint16_t* A3, long long lda, const uint16_t* B3, lo
  * columns).  The fast mode's products with H, the refit's Gram matrix, the Cholesky panel and trailing updates and the
  * triangular-inverse merges (src/liqk_v2.py:1074-1088, :1139-1180) run on it.  Limits as ltq_gemm_bf16x6_tn;
  * batch <= 65535; batched strides multiples of 8 (A, B) / 4 (C) elements.  beta 0 and 1 write C by TMA store /
- * reduce-add (no read of C; one rounding of beta C + alpha acc), other beta by a read-modify-write.
+ * reduce-add (no read of C; one rounding of beta C + alpha acc), other beta by a read-modify-write.  One launch per
+ * call: with beta 0 / 1 and more 128 x 256 tiles (over all batches) than the device has SMs, a persistent kernel of one
+ * CTA per SM with two accumulators in tensor memory, bit-identical to the one-tile kernel used otherwise.
  */
 int ltq_gemm_bf16x3p_tn(const uint16_t* A3, long long lda, long long abs, const uint16_t* B3, long long ldb,
                         long long bbs, float* C, long long ldc, long long cbs, int M, int N, int Kp, int nq, int batch,
